@@ -1,0 +1,233 @@
+/*
+ * qwen_b200.h — C ABI of the B200 ragged hybrid-Qwen decode step.
+ *
+ * This header replaces the reference's native/mlx_bridge.h for the decode path:
+ * the Rust executor (src/serving/native_device.rs:1087-1207,
+ * src/serving/native_mtp_device.rs:332-393) binds these symbols unchanged.
+ * Every declaration cites the reference declaration it replaces.
+ *
+ * Conventions (all inherited from the reference, native/mlx_bridge.cpp:19-31):
+ *  - functions returning int return 0 on success and -1 on error; on error a
+ *    NUL-terminated message is written into error[capacity];
+ *  - constructors return NULL on error with the same message convention;
+ *  - no C++ exception ever crosses this boundary;
+ *  - every handle is worker-confined: one host thread uses a handle at a time
+ *    (native/mlx_bridge.h:7); the library keeps no internal locks;
+ *  - callers own every host buffer; inputs are copied before the call returns.
+ *
+ * The library has no CPU path: a session can only be created on a CUDA device
+ * of compute capability 10.0 (B200). A missing or different device is an error.
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model geometry and execution knobs; field order and size are the
+ * reference's rs_qwen_config (native/mlx_bridge.h:50-53, 132 bytes), mirrored
+ * in Rust by #[repr(C)] Architecture (src/serving/native_qwen.rs:62-98).
+ * Knobs that steer MLX graph construction (layer_group, fused_recurrent,
+ * compiled_decode, fused_attention, expert_kernel) are validated for range and
+ * otherwise ignored: this backend always runs its fused CUDA kernels. */
+typedef struct {
+  int32_t hidden, layers, vocab, q_heads, kv_heads, head_dim, key_heads, value_heads,
+      key_dim, value_dim, conv, interval, experts, top, intermediate, shared, group, bits,
+      context, chunk, rope_dims, activation_precision, layer_group, fused_recurrent,
+      execution_timing, compiled_decode, operator_profile, fused_attention, validation_mode,
+      validation_interval, expert_kernel;
+  float epsilon, theta;
+} rs_qwen_config;
+
+/* Layer program entry (native/mlx_bridge.h:54): mixer 1 = gated attention,
+ * 0 = Gated-DeltaNet; mixer == ((index+1) % interval == 0). */
+typedef struct { uint32_t index, mixer; } rs_qwen_layer;
+
+/* Generation-checked state version handle (native/mlx_bridge.h:72-75,
+ * native/state_table.h:11-13). 40 bytes. */
+#ifndef RS_QWEN_STATE_ID_DEFINED
+#define RS_QWEN_STATE_ID_DEFINED
+typedef struct StateId { uint64_t owner, slot, generation, position, bytes; } StateId;
+#endif
+
+/* ---- weight store (native/mlx_bridge.h:30-32, mlx_bridge.cpp:98-119) ---- */
+
+/* Replaces rs_mlx_weights_create (native/mlx_bridge.h:30). Creates an empty
+ * device weight store on the calling thread's current CUDA device. */
+void* rs_mlx_weights_create(char* error, size_t capacity);
+/* Replaces rs_mlx_weights_destroy (native/mlx_bridge.h:31). */
+void rs_mlx_weights_destroy(void* store);
+/* Replaces rs_mlx_weights_load (native/mlx_bridge.h:32). Reading safetensors
+ * shards is not implemented by this backend yet: returns -1 with a message. */
+int rs_mlx_weights_load(void* store, const char* file, char* error, size_t capacity);
+/* Replaces rs_qwen_quant (native/mlx_bridge.h:55, native/qwen_model.inc:273-276):
+ * per-module quantization override. This backend's kernels implement 4-bit
+ * affine, group 64; any other (group, bits) is rejected with a message. */
+int rs_qwen_quant(void* store, const char* module, int group, int bits, char* error,
+                  size_t capacity);
+/* Replaces rs_mlx_weight_bytes (native/mlx_bridge.h:64, mlx_bridge.cpp:177-187):
+ * copies bytes of a named tensor in the reference's canonical layout
+ * (packed uint32 [rows, cols*bits/32] for ".weight", float32 for ".scales",
+ * ".biases" and unquantized vectors) starting at byte `offset`.
+ * dtype: 0 float32, 2 uint32 (the reference's rs_mlx_input codes). */
+int rs_mlx_weight_bytes(void* store, const char* name, const int32_t* shape, size_t rank,
+                        int dtype, size_t offset, uint8_t* output, size_t count, char* error,
+                        size_t capacity);
+
+/* NEW (no reference counterpart; the reference loads a private checkpoint,
+ * src/serving/qwen_tests.rs:17-243 builds a synthetic one): fill `store` with
+ * seeded random-init weights of the given architecture, generated on the
+ * device: every matrix is N(0, 0.02) quantized to 4-bit affine g64 with bf16
+ * scale and bias; RMSNorm gains are 1; conv, A_log and dt_bias are N(0, 0.02).
+ * with_mtp != 0 also creates the MTP head ("language_model.mtp.*").
+ * The same generator is restated in the test oracle (bit-identical bytes). */
+int rs_qwen_weights_synthetic(void* store, const rs_qwen_config* config, uint64_t seed,
+                              int with_mtp, char* error, size_t capacity);
+
+/* ---- device session (native/qwen_device.inc) ---- */
+
+/* Replaces rs_qwen_device_create (native/mlx_bridge.h:76, qwen_device.inc:13-32).
+ * gpu must be 1 (the reference's "GPU" code); 0 (CPU) is rejected because this
+ * backend has no CPU path. slots = maximum live state versions (target +
+ * draft); bytes = resident state budget (KV pages + DeltaNet state) charged
+ * in StateId.bytes. Unlike the reference, any architecture the kernels
+ * support is accepted (hidden, expert and head widths multiples of 64). */
+void* rs_qwen_device_create(void* weights, int gpu, const rs_qwen_config* config,
+                            const rs_qwen_layer* layers, size_t count, size_t slots,
+                            uint64_t bytes, char* error, size_t capacity);
+/* Replaces rs_qwen_device_destroy (native/mlx_bridge.h:86). */
+void rs_qwen_device_destroy(void* session);
+
+/* Replaces rs_qwen_device_decode_batch (native/mlx_bridge.h:77,
+ * qwen_batch.inc:77-125). One token per row; unlike the reference (B <= 3,
+ * equal positions) any batch size and any mix of positions is accepted.
+ * logits_count = batch * vocab, row-major. */
+int rs_qwen_device_decode_batch(void* session, const StateId* parents, const uint32_t* tokens,
+                                size_t batch, StateId* outputs, float* logits,
+                                size_t logits_count, char* error, size_t capacity);
+/* Replaces rs_qwen_device_step (native/mlx_bridge.h:78, qwen_device.inc:33-50):
+ * previous is NULL iff position == 0; count <= config.chunk; logits of the
+ * last input token (vocab floats). trace must be NULL/0 (diagnostic traces are
+ * an MLX-baseline feature not offered by this backend). */
+int rs_qwen_device_step(void* session, const StateId* previous, size_t position,
+                        const uint32_t* tokens, size_t count, StateId* output, float* logits,
+                        size_t logits_count, float* trace, size_t trace_count, char* error,
+                        size_t capacity);
+/* Replaces rs_qwen_device_step_sampled (native/mlx_bridge.h:79): greedy
+ * total-order argmax on the device, only the token returns. */
+int rs_qwen_device_step_sampled(void* session, const StateId* previous, size_t position,
+                                const uint32_t* tokens, size_t count, StateId* output,
+                                uint32_t* token, char* error, size_t capacity);
+/* Replaces rs_qwen_device_block (native/mlx_bridge.h:80-81): position-major
+ * logits for every input token (count * vocab floats). */
+int rs_qwen_device_block(void* session, const StateId* previous, size_t position,
+                         const uint32_t* tokens, size_t count, StateId* output, float* logits,
+                         size_t logits_count, char* error, size_t capacity);
+/* Replace rs_qwen_device_hidden_step / _hidden_block (native/mlx_bridge.h:94-95):
+ * as step / block, and the new version also keeps the post-final-norm hidden
+ * rows of its input tokens (read with rs_qwen_device_hidden_snapshot, and the
+ * MTP head's input). */
+int rs_qwen_device_hidden_step(void* session, const StateId* previous, size_t position,
+                               const uint32_t* tokens, size_t count, StateId* output,
+                               float* logits, size_t logits_count, char* error,
+                               size_t capacity);
+int rs_qwen_device_hidden_block(void* session, const StateId* previous, size_t position,
+                                const uint32_t* tokens, size_t count, StateId* output,
+                                float* logits, size_t logits_count, char* error,
+                                size_t capacity);
+/* Replaces rs_qwen_device_hidden_snapshot (native/mlx_bridge.h:96). */
+int rs_qwen_device_hidden_snapshot(void* session, const StateId* id, float* output,
+                                   size_t count, char* error, size_t capacity);
+/* Replaces rs_qwen_device_release (native/mlx_bridge.h:82, qwen_device.inc:55). */
+int rs_qwen_device_release(void* session, const StateId* id, char* error, size_t capacity);
+/* Replaces rs_qwen_device_snapshot (native/mlx_bridge.h:83, qwen_device.inc:56-61):
+ * exports a version's state as float32 in the reference layout
+ * (native/qwen_model.inc:268-271): per layer in order, DeltaNet conv
+ * [conv-1, 2*kd+vd] then S [hv, dv, dk]; attention K [kv, context, d] then V,
+ * positions >= version position zero. count = rs_qwen_state_count(). */
+int rs_qwen_device_snapshot(void* session, const StateId* id, float* output, size_t count,
+                            char* error, size_t capacity);
+/* Replaces rs_qwen_device_stats (native/mlx_bridge.h:84, qwen_device.inc:62):
+ * count must be 17 + 19*3 = 74; same slot meaning (residents, bytes, exports,
+ * uploads, steps, device bytes in use, peak, timing calls/completed/graph_ns/
+ * wait_ns/export_ns/wall_ns/groups, graphs/graph misses/graph launches, then
+ * per-stage calls/host_ns/wait_ns for the 19 operator stages). */
+int rs_qwen_device_stats(void* session, uint64_t* output, size_t count, char* error,
+                         size_t capacity);
+/* Replaces rs_qwen_device_drain (native/mlx_bridge.h:85, qwen_device.inc:65). */
+int rs_qwen_device_drain(void* session, uint64_t* invalidated, char* error, size_t capacity);
+
+/* ---- MTP draft head (native/qwen_mtp.inc) ---- */
+
+/* Replaces rs_qwen_device_mtp_attach (native/mlx_bridge.h:103, qwen_mtp.inc:127-131).
+ * The MTP weights live in the same store as the target ("language_model.mtp.*");
+ * `weights` must be that store or a store with the MTP head. Must precede
+ * any admission. */
+int rs_qwen_device_mtp_attach(void* session, void* weights, char* error, size_t capacity);
+/* Replaces rs_qwen_device_mtp_step (native/mlx_bridge.h:104, qwen_mtp.inc:133-181). */
+int rs_qwen_device_mtp_step(void* session, const StateId* previous, const StateId* source,
+                            int draft_source, size_t row, const uint32_t* tokens, size_t count,
+                            StateId* output, float* logits, size_t logits_count,
+                            int diagnostics, char* error, size_t capacity);
+/* Replaces rs_qwen_device_mtp_release (native/mlx_bridge.h:105). */
+int rs_qwen_device_mtp_release(void* session, const StateId* id, char* error, size_t capacity);
+/* Replaces rs_qwen_device_mtp_snapshot (native/mlx_bridge.h:112): draft KV
+ * [kv, context, d] K then V, then the hidden rows. count = id.bytes/4 is not
+ * used here; count = 2*kv*context*d + rows*hidden. */
+int rs_qwen_device_mtp_snapshot(void* session, const StateId* id, float* output, size_t count,
+                                char* error, size_t capacity);
+
+/* ---- NEW ragged entry points (additive; no reference counterpart) ---- */
+
+/* Flags for rs_qwen_device_step_ragged. */
+#define RS_QWEN_RAGGED_SAMPLED 1u      /* write greedy tokens (one per output row) */
+#define RS_QWEN_RAGGED_LOGITS 2u       /* write fp32 logits (vocab per output row) */
+#define RS_QWEN_RAGGED_ALL_ROWS 4u     /* output rows = every input token, else last per sequence */
+#define RS_QWEN_RAGGED_HIDDEN 8u       /* keep post-norm hidden rows in each new version */
+#define RS_QWEN_RAGGED_CONSUME 16u     /* parents are released by the call (in-place DeltaNet
+                                          state update, no second state slot) */
+
+/* One step over a ragged batch: sequence s feeds counts[s] tokens starting at
+ * positions[s] (parents[s] is a zeroed StateId iff positions[s] == 0; its
+ * position must equal positions[s]). Tokens are packed sequence-major in
+ * tokens_flat. Prefill chunks and decode tokens mix freely. Packing (prefix
+ * sums, per-token sequence/position, paged-KV block tables and DeltaNet slot
+ * indices) is built on the device. Outputs: outs[s] for every sequence; per
+ * output row (see flags) a sampled token and/or vocab logits.
+ * Generalises rs_qwen_device_decode_batch (qwen_batch.inc:77-125) and
+ * rs_qwen_device_step (qwen_device.inc:33-54). */
+int rs_qwen_device_step_ragged(void* session, size_t n_seq, const StateId* parents,
+                               const uint32_t* positions, const uint32_t* counts,
+                               const uint32_t* tokens_flat, uint32_t flags, StateId* outs,
+                               uint32_t* sampled, size_t sampled_count, float* logits,
+                               size_t logits_count, char* error, size_t capacity);
+
+/* Speculative verify + accept over a ragged batch, on the device.
+ * Sequence s: parents[s] holds target logits' argmax seed[s] (the greedy token
+ * after the parent, already emitted), and drafts[s*width .. +ndraft[s]] are
+ * MTP proposals. The call runs the target over [seed, drafts...] for every
+ * sequence in one ragged step, computes the accepted length with the
+ * reference's plan() rule (src/serving/native_speculative.rs:74-128: accept
+ * while draft[i] == argmax(row i) and not EOS), and compacts KV pages and
+ * DeltaNet state on the device to the version after the emitted tokens
+ * (replay semantics of native_mtp_decode.rs:238-272 without a replay).
+ * Outputs per sequence: accepted[s], emitted tokens (width+1 per sequence,
+ * n_emitted[s] valid), outs[s] = the compacted version. */
+int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId* parents,
+                                     const uint32_t* seeds, const uint32_t* drafts,
+                                     const uint32_t* ndraft, size_t width, const uint32_t* eos,
+                                     size_t n_eos, uint32_t flags, StateId* outs,
+                                     uint32_t* accepted, uint32_t* emitted,
+                                     uint32_t* n_emitted, char* error, size_t capacity);
+
+/* Number of floats of a version's reference-layout snapshot
+ * (native/qwen_model.inc:268-271 qwen_state_count). */
+size_t rs_qwen_state_count(const rs_qwen_config* config);
+
+/* Version string of this backend (replaces rs_mlx_version, native/mlx_bridge.h:16). */
+const char* rs_mlx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
