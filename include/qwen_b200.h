@@ -221,6 +221,30 @@ int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId*
                                      uint32_t* accepted, uint32_t* emitted,
                                      uint32_t* n_emitted, char* error, size_t capacity);
 
+/* NEW (no reference counterpart; stands in for a long prefill when measuring
+ * decode at long contexts): create a published version at `position` whose
+ * KV pages for [0, position) hold seeded bf16 N(0, 1) values, whose DeltaNet
+ * state is fp32 N(0, 0.02) and conv history N(0, 1). The contents depend only
+ * on (seed, position), not on the slot. */
+int rs_qwen_device_synthetic_state(void* session, size_t position, uint64_t seed, StateId* out,
+                                   char* error, size_t capacity);
+
+/* NEW diagnostic (no reference counterpart; mirrors the role of the
+ * reference's routing probe, native/operator_probe.inc:19-23): when enabled,
+ * each step keeps its top-k expert ids; rs_qwen_device_debug_routing copies
+ * the last step's ids as int32 [moe layers][tokens][top]. */
+int rs_qwen_device_set_capture(void* session, int routing, char* error, size_t capacity);
+int rs_qwen_device_debug_routing(void* session, int32_t* out, size_t count, char* error,
+                                 size_t capacity);
+
+/* NEW diagnostic: device-side timing from CUDA events on the session stream.
+ * profile != 0 additionally brackets every operator stage with events
+ * (the 19 stages of native/operator_timing.h:5-9). rs_qwen_device_timing
+ * writes count = 3 + 19 doubles: last step device ms, cumulative device ms,
+ * timed steps, then cumulative device ms per stage (zeros unless profiling). */
+int rs_qwen_device_set_profile(void* session, int profile, char* error, size_t capacity);
+int rs_qwen_device_timing(void* session, double* out, size_t count, char* error, size_t capacity);
+
 /* Number of floats of a version's reference-layout snapshot
  * (native/qwen_model.inc:268-271 qwen_state_count). */
 size_t rs_qwen_state_count(const rs_qwen_config* config);

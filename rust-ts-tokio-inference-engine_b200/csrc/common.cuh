@@ -1,0 +1,102 @@
+// Shared definitions for the B200 ragged hybrid-Qwen decode step.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+#define QWEN_CUDA(call)                                                                    \
+  do {                                                                                     \
+    cudaError_t qwen_err_ = (call);                                                        \
+    if (qwen_err_ != cudaSuccess)                                                          \
+      throw std::runtime_error(std::string("CUDA error: ") + cudaGetErrorString(qwen_err_) + \
+                               " at " + __FILE__ + ":" + std::to_string(__LINE__));        \
+  } while (0)
+
+namespace qwen {
+
+// 4-bit affine g64 weight tile: 128 rows x 64 columns (one quant group per row).
+// Layout: packed nibbles [128 rows][32 bytes] (canonical LSB-first order inside a
+// row: byte j holds columns 2j (low nibble) and 2j+1), then 128 bf16 scales,
+// then 128 bf16 biases. A matrix [rows, K] is stored as
+// [ceil(rows/128) row tiles][K/64 column chunks] tiles, each 4608 bytes, so one
+// tile is one contiguous bulk copy.
+constexpr int kTileRows = 128;
+constexpr int kTileK = 64;
+constexpr int kTilePackedBytes = kTileRows * kTileK / 2;  // 4096
+constexpr int kTileBytes = kTilePackedBytes + kTileRows * 2 * 2;  // 4608
+constexpr int kPageTokens = 16;  // paged-KV page size (tokens)
+
+struct QMat {
+  const uint8_t* tiles = nullptr;
+  int rows = 0;       // logical output rows
+  int row_tiles = 0;  // ceil(rows / 128)
+  int k = 0;          // input width (multiple of 64)
+  __host__ __device__ int k_chunks() const { return k / kTileK; }
+  __host__ __device__ const uint8_t* tile(int row_tile, int chunk) const {
+    return tiles + (size_t(row_tile) * (k / kTileK) + chunk) * kTileBytes;
+  }
+};
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(uint32_t(b) << 16);
+}
+
+// Round-to-nearest-even narrowing to bf16 bits (matches the host generator).
+__host__ __device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
+#ifdef __CUDA_ARCH__
+  uint32_t u = __float_as_uint(f);
+#else
+  uint32_t u;
+  memcpy(&u, &f, 4);
+#endif
+  if ((u & 0x7F800000u) == 0x7F800000u) return uint16_t((u >> 16) | ((u & 0xFFFF) ? 0x40 : 0));
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + __expf(-x)); }
+
+// IEEE total-order key: -0 < +0, matches Rust f32::total_cmp for finite values.
+__device__ __forceinline__ uint32_t total_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u ^ 0x80000000u);
+}
+
+// Counter-based hash (splitmix64 finalizer) and the Irwin-Hall(4) normal
+// approximation used by the seeded synthetic generators.
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float synth_normal(uint64_t key, uint64_t index, float k) {
+  uint64_t h = mix64(key ^ (index * 0xD1B54A32D192ED03ull));
+  int32_t s = int32_t(h & 0xFFFF) + int32_t((h >> 16) & 0xFFFF) + int32_t((h >> 32) & 0xFFFF) +
+              int32_t(h >> 48);
+  return __fmul_rn(float(s - 131070), k);
+}
+
+// Error flags raised by kernels and read back by the host after a step.
+enum ErrorBits : uint32_t {
+  kErrNonFinite = 1u,
+  kErrBounds = 2u,
+  kErrTimeout = 4u,
+};
+
+}  // namespace qwen

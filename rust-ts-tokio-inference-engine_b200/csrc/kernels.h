@@ -1,0 +1,116 @@
+// Launch interface of the decode-step kernels (all sm_100a).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "model.h"
+
+namespace qwen {
+
+// Per-sequence packing descriptor, uploaded once per step (host -> device).
+struct SeqDesc {
+  int32_t position;   // first new position
+  int32_t count;      // new tokens
+  int32_t parent;     // parent state slot (= block-table row), -1 = empty prefix
+  int32_t child;      // child state slot
+  int32_t n_shared;   // parent pages kept in the child's block table
+  int32_t new_off;    // offset of this sequence's new pages in the page list
+  int32_t n_new;      // freshly allocated pages
+  int32_t out_row0;   // first output row (logits / sampled)
+  int32_t n_out;      // output rows (1 = last token, count = every token)
+  int32_t cow_src;    // page copied into the first new page (copy-on-write), -1 none
+  int32_t cow_len;    // tokens copied by the copy-on-write
+  int32_t hidden;     // keep post-norm hidden rows in the child slot
+};
+
+// Device-built packing results.
+struct Packed {
+  int32_t* cu_seqlens;    // [n+1]
+  int32_t* token_seq;     // [T]
+  int32_t* token_pos;     // [T]
+  int64_t* slot_mapping;  // [T] page*16 + pos%16
+  int32_t* out_token;     // [R] token index of each output row
+};
+
+struct KvPool {
+  __nv_bfloat16* base = nullptr;  // [layers][pages][2][Hkv][16][D]
+  int n_pages = 0, layers = 0, Hkv = 0, D = 0;
+  __host__ __device__ size_t page_elems() const { return size_t(2) * Hkv * kPageTokens * D; }
+  __host__ __device__ __nv_bfloat16* page(int layer, int p) const {
+    return base + (size_t(layer) * n_pages + p) * page_elems();
+  }
+};
+
+struct GdnPool {
+  float* state = nullptr;  // [slots][n_gdn][hv][dv][dk]
+  float* conv = nullptr;   // [slots][n_gdn][conv-1][cd]
+  int slots = 0, n_gdn = 0;
+  size_t state_elems = 0;  // per layer per slot
+  size_t conv_elems = 0;
+};
+
+// GEMM descriptor for the 4-bit affine g64 grouped GEMM.
+enum GemmMode : int {
+  kGemmStoreF32 = 0,  // Y[t][n] = acc (split s writes Y + s*split_stride)
+  kGemmGateUp = 1,    // grouped experts: act[p][j] = silu(gate)*up as bf16
+  kGemmDown = 2,      // grouped experts: Y[p][n] = acc (fp32)
+};
+
+struct GemmArgs {
+  QMat W;
+  int mode = kGemmStoreF32;
+  int expert_tiles = 0;  // row tiles per expert (grouped modes)
+  const __nv_bfloat16* X = nullptr;
+  int ldx = 0;
+  const int32_t* x_row = nullptr;  // grouped: X row of sorted position p = x_row[p] / x_div
+  int x_div = 1;
+  const int32_t* group_off = nullptr;  // grouped: positions of expert g = [off[g], off[g+1])
+  int groups = 1;
+  int n_tokens = 0;  // dense: number of token rows
+  int splits = 1;    // dense split-K
+  size_t split_stride = 0;
+  float* Y = nullptr;
+  int ldy = 0;
+  __nv_bfloat16* Yb = nullptr;
+  int ldyb = 0;
+};
+
+uint64_t kernel_launches();
+
+void launch_pack(const SeqDesc* descs, int n_seq, const int32_t* new_pages, int32_t* block_table,
+                 int bt_stride, Packed p, cudaStream_t s);
+void launch_cow(KvPool kv, const SeqDesc* descs, int n_seq, const int32_t* new_pages,
+                cudaStream_t s);
+void launch_embed_norm(const QMat& embed, const uint32_t* tokens, int T, const float* norm_w,
+                       float eps, float* x, __nv_bfloat16* hb, cudaStream_t s);
+void launch_residual_norm(float* x, const float* partial, int splits, size_t split_stride, int T,
+                          int H, const float* norm_w, float eps, __nv_bfloat16* hb,
+                          const int32_t* out_token, int rows, float* hidden_f32,
+                          cudaStream_t s);
+void launch_qgemm(const GemmArgs& a, cudaStream_t s);
+void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
+                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
+                int gdn_index, __nv_bfloat16* out, uint32_t* err, cudaStream_t s);
+void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
+                      const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
+                      int kv_layer, float* q, float* gate, cudaStream_t s);
+void launch_attention(const Dims& d, const float* q, const float* gate, const int32_t* token_seq,
+                      const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table,
+                      int bt_stride, KvPool kv, int kv_layer, int T, int max_len, float* ws,
+                      int max_splits, __nv_bfloat16* out, cudaStream_t s);
+void launch_route(const float* logits, int ld, int T, int E, int top, int32_t* ids,
+                  float* weights, cudaStream_t s);
+void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
+                        int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s);
+void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
+                        const float* weights, int T, int H, int slots, const float* norm_w,
+                        float eps, __nv_bfloat16* hb, const int32_t* out_token, int rows,
+                        float* hidden_f32, cudaStream_t s);
+void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err,
+                   cudaStream_t s);
+void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,
+                        GdnPool pool, int slot, const Dims& d, uint64_t seed, cudaStream_t s);
+void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* rows, int n, int H,
+                        __nv_bfloat16* dst, cudaStream_t s);
+
+}  // namespace qwen

@@ -1,0 +1,1061 @@
+// Device session: state versions, paged-KV and DeltaNet pools, the ragged
+// step executor and the rs_qwen_* C ABI (include/qwen_b200.h).
+//
+// Replaces the reference's MLX device session (native/qwen_device.inc,
+// native/qwen_batch.inc). A state version (StateId) is one DeltaNet slot
+// (recurrent state + conv history, fp32) plus a list of 16-token KV pages
+// shared copy-on-write with its ancestors; parents are never mutated unless a
+// step is asked to consume them.
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <memory>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "state_table.h"
+
+using namespace qwen;
+
+namespace {
+
+void report(char* error, size_t capacity, const char* message) noexcept {
+  if (error && capacity) {
+    const size_t n = std::min(std::strlen(message), capacity - 1);
+    std::memcpy(error, message, n);
+    error[n] = 0;
+  }
+}
+
+// Error convention of native/mlx_bridge.cpp:19-31: 0 ok, -1 + message.
+template <class F>
+int checked(char* error, size_t capacity, F f) noexcept {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    report(error, capacity, e.what());
+  } catch (...) {
+    report(error, capacity, "unknown native CUDA exception");
+  }
+  return -1;
+}
+
+uint64_t allocate_owner() {
+  static std::atomic<uint64_t> next{1};
+  uint64_t owner = next.load();
+  for (;;) {
+    if (!owner || owner >= UINT64_MAX - 1) throw std::overflow_error("session owner exhausted");
+    if (next.compare_exchange_weak(owner, owner + 2)) return owner;
+  }
+}
+
+uint64_t now_ns() {
+  return uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                      std::chrono::steady_clock::now().time_since_epoch())
+                      .count());
+}
+
+template <class T>
+struct DevBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  void ensure(size_t count) {
+    if (count <= n) return;
+    if (p) {
+      QWEN_CUDA(cudaFree(p));
+      p = nullptr;
+      n = 0;
+    }
+    QWEN_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
+    n = count;
+  }
+};
+
+template <class T>
+struct PinBuf {
+  T* p = nullptr;
+  size_t n = 0;
+  ~PinBuf() {
+    if (p) cudaFreeHost(p);
+  }
+  void ensure(size_t count) {
+    if (count <= n) return;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    QWEN_CUDA(cudaMallocHost(&p, std::max<size_t>(count, 1) * sizeof(T)));
+    n = count;
+  }
+};
+
+struct Version {
+  std::vector<int32_t> pages;  // KV pages covering [0, position)
+  uint32_t hidden_rows = 0;    // post-norm hidden rows kept (hidden_* calls)
+};
+
+constexpr size_t kStatsCount = 17 + 19 * 3;
+
+struct Session {
+  WeightStore* store = nullptr;
+  int device = 0;
+  rs_qwen_config config{};
+  Dims d;
+  std::vector<rs_qwen_layer> program;
+  size_t slots = 0;
+  uint64_t limit = 0;
+  std::unique_ptr<StateTable<Version>> table;
+  cudaStream_t stream = nullptr;
+
+  // pools
+  KvPool kv;
+  GdnPool gdn;
+  DevBuf<__nv_bfloat16> kv_mem;
+  DevBuf<float> gdn_state, gdn_conv, hidden_pool;
+  DevBuf<int32_t> block_table;
+  int bt_stride = 0;
+  size_t gdn_slot_bytes = 0, page_bytes = 0;
+  std::vector<int32_t> free_pages;
+  std::vector<int32_t> page_ref;
+  std::vector<uint8_t> page_filled;
+
+  // step scratch
+  int max_tokens = 0, max_rows = 0, max_seqs = 0;
+  DevBuf<SeqDesc> descs;
+  DevBuf<int32_t> new_pages, cu_seqlens, token_seq, token_pos, out_token, ids, counts, offsets,
+      perm, inv, capture;
+  DevBuf<int64_t> slot_mapping;
+  DevBuf<uint32_t> tokens, sampled, err;
+  DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
+  DevBuf<__nv_bfloat16> hb, hb2, act;
+  PinBuf<uint8_t> staging;
+  bool capture_routing = false;
+  int captured_tokens = 0;
+
+  // device timing (CUDA events on `stream`)
+  cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
+  bool profile = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::pair<int, std::pair<int, int>>> ev_marks;  // stage, (begin event, end event)
+  int ev_used = 0, open_stage = -1, open_event = -1;
+  double last_ms = 0, total_ms = 0, stage_ms[19] = {};
+  uint64_t timed_steps = 0, stage_calls[19] = {};
+
+  cudaEvent_t next_event() {
+    if (ev_used == int(ev_pool.size())) {
+      cudaEvent_t e;
+      QWEN_CUDA(cudaEventCreate(&e));
+      ev_pool.push_back(e);
+    }
+    return ev_pool[ev_used++];
+  }
+  // Stage boundaries (native/operator_timing.h:5-9 ids); no-op unless profiling.
+  void stage(int id) {
+    if (!profile) return;
+    const int e = ev_used;
+    QWEN_CUDA(cudaEventRecord(next_event(), stream));
+    if (open_stage >= 0) ev_marks.push_back({open_stage, {open_event, e}});
+    open_stage = id;
+    open_event = e;
+  }
+  void stage_close() {
+    if (!profile || open_stage < 0) return;
+    const int e = ev_used;
+    QWEN_CUDA(cudaEventRecord(next_event(), stream));
+    ev_marks.push_back({open_stage, {open_event, e}});
+    open_stage = -1;
+  }
+
+  // stats (rs_qwen_device_stats layout, native/qwen_device.inc:62)
+  uint64_t exports = 0, uploads = 0, steps = 0, calls = 0, completed = 0, graph_ns = 0,
+           wait_ns = 0, export_ns = 0, wall_ns = 0, groups = 0, launches = 0;
+
+  ~Session() {
+    for (auto e : ev_pool) cudaEventDestroy(e);
+    if (ev_begin) cudaEventDestroy(ev_begin);
+    if (ev_end) cudaEventDestroy(ev_end);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  void set_device() const { QWEN_CUDA(cudaSetDevice(device)); }
+
+  uint64_t version_bytes(size_t n_pages, size_t hidden_rows) const {
+    return gdn_slot_bytes + n_pages * page_bytes + hidden_rows * size_t(d.H) * 4;
+  }
+
+  void unref_pages(const std::vector<int32_t>& pages) {
+    for (int32_t p : pages) {
+      if (--page_ref[p] == 0) {
+        page_filled[p] = 0;
+        free_pages.push_back(p);
+      }
+    }
+  }
+
+  void init(WeightStore* w, int gpu, const rs_qwen_config& c, const rs_qwen_layer* layers,
+            size_t count, size_t n_slots, uint64_t bytes) {
+    if (gpu != 1) throw std::invalid_argument("device session requires gpu=1: this backend has no CPU path");
+    if (!w || !w->ready) throw std::invalid_argument("weight store is empty");
+    store = w;
+    device = w->device;
+    set_device();
+    cudaDeviceProp prop;
+    QWEN_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) throw std::runtime_error("device is not sm_100 (B200): kernels are built for sm_100a only");
+    config = c;
+    d = Dims::from(c);
+    const Dims& wd = w->dims;
+    if (d.H != wd.H || d.L != wd.L || d.V != wd.V || d.Hq != wd.Hq || d.Hkv != wd.Hkv ||
+        d.D != wd.D || d.hk != wd.hk || d.hv != wd.hv || d.dk != wd.dk || d.dv != wd.dv ||
+        d.conv != wd.conv || d.interval != wd.interval || d.E != wd.E || d.top != wd.top ||
+        d.I != wd.I || d.S != wd.S)
+      throw std::invalid_argument("device session architecture does not match the weight store");
+    if (c.context <= 0 || c.chunk <= 0 || c.rope_dims <= 0 || c.rope_dims > c.head_dim ||
+        c.rope_dims % 2 || !(c.epsilon > 0) || !(c.theta > 1))
+      throw std::invalid_argument("device session architecture/profile");
+    if (c.layer_group < 0 || c.fused_recurrent < 0 || c.fused_recurrent > 1 ||
+        c.execution_timing < 0 || c.execution_timing > 1 || c.compiled_decode < 0 ||
+        c.compiled_decode > 1 || c.operator_profile < 0 || c.operator_profile > 1 ||
+        c.fused_attention < 0 || c.fused_attention > 2 || c.validation_mode < 0 ||
+        c.validation_mode > 2 || c.expert_kernel < 0 || c.expert_kernel > 2)
+      throw std::invalid_argument("device session execution knobs out of range");
+    if (count != size_t(c.layers)) throw std::invalid_argument("device session program");
+    for (size_t i = 0; i < count; ++i)
+      if (layers[i].index != i || layers[i].mixer != uint32_t((i + 1) % c.interval == 0))
+        throw std::invalid_argument("device session program");
+    program.assign(layers, layers + count);
+    if (!n_slots || n_slots > (size_t(1) << 20) || !bytes) throw std::invalid_argument("state table bounds");
+    slots = n_slots;
+    limit = bytes;
+    table = std::make_unique<StateTable<Version>>(allocate_owner(), n_slots, bytes);
+    QWEN_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    QWEN_CUDA(cudaEventCreate(&ev_begin));
+    QWEN_CUDA(cudaEventCreate(&ev_end));
+
+    // DeltaNet pool: one slot per version
+    gdn.slots = int(n_slots);
+    gdn.n_gdn = d.n_gdn;
+    gdn.state_elems = size_t(d.hv) * d.dv * d.dk;
+    gdn.conv_elems = size_t(d.conv - 1) * d.cd;
+    gdn_slot_bytes = size_t(d.n_gdn) * (gdn.state_elems + gdn.conv_elems) * 4;
+    gdn_state.ensure(std::max<size_t>(1, n_slots * d.n_gdn * gdn.state_elems));
+    gdn_conv.ensure(std::max<size_t>(1, n_slots * d.n_gdn * gdn.conv_elems));
+    gdn.state = gdn_state.p;
+    gdn.conv = gdn_conv.p;
+
+    // scratch sizing
+    const char* env = std::getenv("QWEN_STEP_TOKENS");
+    max_tokens = env ? std::max(1, atoi(env)) : 4096;
+    max_rows = std::min(max_tokens, 1024);
+    max_seqs = max_tokens;
+    bt_stride = (d.ctx + kPageTokens - 1) / kPageTokens;
+    block_table.ensure(n_slots * size_t(bt_stride));
+    QWEN_CUDA(cudaMemset(block_table.p, 0, n_slots * size_t(bt_stride) * 4));
+    hidden_pool.ensure(n_slots * size_t(std::max(1, d.chunk)) * d.H);
+    const int T = max_tokens, A = T * (d.top + 1);
+    descs.ensure(max_seqs);
+    new_pages.ensure(size_t(max_seqs) + T / kPageTokens + 16);
+    cu_seqlens.ensure(max_seqs + 1);
+    token_seq.ensure(T);
+    token_pos.ensure(T);
+    slot_mapping.ensure(T);
+    out_token.ensure(T);
+    tokens.ensure(T);
+    sampled.ensure(max_rows);
+    err.ensure(1);
+    x.ensure(size_t(T) * d.H);
+    const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
+    proj.ensure(size_t(T) * proj_w);
+    partial.ensure(size_t(T) * d.H);
+    const int hbw = std::max({d.H, d.vd, d.Hq * d.D});
+    hb.ensure(size_t(T) * hbw);
+    hb2.ensure(size_t(T) * hbw);
+    q.ensure(size_t(T) * d.Hq * d.D);
+    gate.ensure(size_t(T) * d.Hq * d.D);
+    ids.ensure(A);
+    weights.ensure(A);
+    counts.ensure(d.E + 1);
+    offsets.ensure(d.E + 2);
+    perm.ensure(A);
+    inv.ensure(A);
+    act.ensure(size_t(A) * d.I);
+    moe_y.ensure(size_t(A) * d.H);
+    hidden_stage.ensure(size_t(T) * d.H);
+
+    // KV page pool: what the byte budget leaves after the DeltaNet pool,
+    // capped by free device memory (keep 2 GiB of headroom).
+    page_bytes = size_t(d.n_attn) * 2 * d.Hkv * kPageTokens * d.D * 2;
+    size_t budget_pages = 0;
+    const uint64_t fixed = uint64_t(n_slots) * gdn_slot_bytes;
+    if (d.n_attn > 0) {
+      if (bytes <= fixed) throw std::invalid_argument("state byte budget smaller than the DeltaNet pool");
+      budget_pages = (bytes - fixed) / page_bytes;
+      size_t free_b = 0, total_b = 0;
+      QWEN_CUDA(cudaMemGetInfo(&free_b, &total_b));
+      const size_t headroom = size_t(2) << 30;
+      size_t mem_pages = free_b > headroom ? (free_b - headroom) / page_bytes : 0;
+      budget_pages = std::min({budget_pages, mem_pages, size_t(INT32_MAX / kPageTokens)});
+      if (budget_pages == 0) throw std::runtime_error("no device memory left for KV pages");
+      kv_mem.ensure(budget_pages * (page_bytes / 2));
+    }
+    kv.base = kv_mem.p;
+    kv.n_pages = int(budget_pages);
+    kv.layers = d.n_attn;
+    kv.Hkv = d.Hkv;
+    kv.D = d.D;
+    free_pages.resize(budget_pages);
+    for (size_t i = 0; i < budget_pages; ++i) free_pages[i] = int32_t(budget_pages - 1 - i);
+    page_ref.assign(budget_pages, 0);
+    page_filled.assign(budget_pages, 0);
+  }
+
+  // ------------------------------------------------------------ the step --
+  struct SeqIn {
+    const StateId* parent;  // null iff position == 0
+    uint32_t position, count;
+    const uint32_t* tokens;
+  };
+
+  // Runs one ragged step. Outputs: outs[s], then per output row a sampled
+  // token and/or fp32 logits. Throws on any error after rolling back.
+  void step(const std::vector<SeqIn>& seqs, uint32_t flags, StateId* outs, uint32_t* sampled_out,
+            float* logits_out) {
+    set_device();
+    const uint64_t t_start = now_ns();
+    ++calls;
+    const int n = int(seqs.size());
+    if (n <= 0) throw std::invalid_argument("ragged step needs at least one sequence");
+    if (n > max_seqs) throw std::invalid_argument("too many sequences in one step");
+    const bool consume = flags & RS_QWEN_RAGGED_CONSUME;
+    const bool all_rows = flags & RS_QWEN_RAGGED_ALL_ROWS;
+    const bool keep_hidden = flags & RS_QWEN_RAGGED_HIDDEN;
+    int T = 0, R = 0, max_len = 0;
+    for (const auto& s : seqs) {
+      if (!s.count) throw std::invalid_argument("sequence with no tokens");
+      if ((s.position == 0) != (s.parent == nullptr)) throw std::invalid_argument("device previous state presence");
+      if (size_t(s.position) + s.count > size_t(d.ctx)) throw std::invalid_argument("device step capacity");
+      if (keep_hidden && s.count > uint32_t(d.chunk)) throw std::invalid_argument("hidden capture exceeds chunk rows");
+      for (uint32_t i = 0; i < s.count; ++i)
+        if (s.tokens[i] >= uint32_t(d.V)) throw std::invalid_argument("token outside vocabulary");
+      T += int(s.count);
+      R += all_rows ? int(s.count) : 1;
+      max_len = std::max<int>(max_len, int(s.position + s.count));
+    }
+    if (T > max_tokens) throw std::invalid_argument("ragged step exceeds the token budget");
+    if (R > max_rows) throw std::invalid_argument("ragged step exceeds the output-row budget");
+    // parents must be distinct when consumed
+    std::vector<const Version*> par(n, nullptr);
+    for (int i = 0; i < n; ++i) {
+      if (!seqs[i].parent) continue;
+      if (seqs[i].parent->position != seqs[i].position) throw std::invalid_argument("device position mismatch");
+      par[i] = &table->get(*seqs[i].parent);
+      if (consume)
+        for (int j = 0; j < i; ++j)
+          if (seqs[j].parent && seqs[j].parent->slot == seqs[i].parent->slot)
+            throw std::invalid_argument("consumed parent used twice");
+    }
+    if (!consume && table->residents() + size_t(n) > slots) throw std::runtime_error("combined resident budget exhausted");
+
+    // page planning (host), descriptors
+    staging.ensure(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64);
+    SeqDesc* hd = reinterpret_cast<SeqDesc*>(staging.p);
+    std::vector<int32_t> npages;
+    std::vector<std::vector<int32_t>> child_pages(n);
+    std::vector<StateId> reserved;
+    std::vector<int32_t> deferred_free;
+    std::vector<int> tok_off(n + 1, 0);
+    // On failure every page reference taken for a child is dropped (shared
+    // pages were either ref'd or inherited from a consumed parent), and
+    // consumed parents' dropped pages are released too.
+    auto fail_cleanup = [&]() {
+      for (auto& cp : child_pages) unref_pages(cp);
+      unref_pages(deferred_free);
+      for (auto& id : reserved) {
+        try {
+          table->rollback(id);
+        } catch (...) {
+        }
+      }
+    };
+    try {
+      int row = 0;
+      for (int i = 0; i < n; ++i) {
+        const auto& s = seqs[i];
+        tok_off[i + 1] = tok_off[i] + int(s.count);
+        SeqDesc& sd = hd[i];
+        std::memset(&sd, 0, sizeof(sd));
+        sd.position = int32_t(s.position);
+        sd.count = int32_t(s.count);
+        sd.parent = s.parent ? int32_t(s.parent->slot) : -1;
+        sd.cow_src = -1;
+        const int pos = int(s.position), cnt = int(s.count);
+        const int n_prefix = (pos + kPageTokens - 1) / kPageTokens;
+        const int n_total = (pos + cnt + kPageTokens - 1) / kPageTokens;
+        if (par[i] && int(par[i]->pages.size()) != n_prefix) throw std::runtime_error("parent page list inconsistent");
+        int n_shared = n_prefix;
+        if (d.n_attn > 0 && pos % kPageTokens) {
+          const int32_t lp = par[i]->pages[n_prefix - 1];
+          if (page_filled[lp] > pos % kPageTokens) {  // a sibling extended it: copy on write
+            n_shared = n_prefix - 1;
+            sd.cow_src = lp;
+            sd.cow_len = pos % kPageTokens;
+          } else {
+            page_filled[lp] = uint8_t(std::min(kPageTokens, pos + cnt - (n_prefix - 1) * kPageTokens));
+          }
+        }
+        if (d.n_attn == 0) n_shared = 0;
+        const int n_new = d.n_attn > 0 ? n_total - n_shared : 0;
+        if (n_new > int(free_pages.size())) throw std::runtime_error("KV page pool exhausted");
+        sd.n_shared = n_shared;
+        sd.new_off = int32_t(npages.size());
+        sd.n_new = n_new;
+        auto& cp = child_pages[i];
+        if (d.n_attn > 0) {
+          cp.assign(par[i] ? par[i]->pages.begin() : cp.end(), par[i] ? par[i]->pages.begin() + n_shared : cp.end());
+          if (!consume)
+            for (int32_t p : cp) ++page_ref[p];
+          for (int j = 0; j < n_new; ++j) {
+            const int32_t p = free_pages.back();
+            free_pages.pop_back();
+            page_ref[p] = 1;
+            const int first = (n_shared + j) * kPageTokens;
+            page_filled[p] = uint8_t(std::min(kPageTokens, pos + cnt - first));
+            npages.push_back(p);
+            cp.push_back(p);
+          }
+        }
+        if (int(cp.size()) > bt_stride) throw std::invalid_argument("context exceeds block table");
+        sd.n_out = all_rows ? cnt : 1;
+        sd.out_row0 = row;
+        row += sd.n_out;
+        sd.hidden = keep_hidden ? 1 : 0;
+        const uint64_t charge = version_bytes(cp.size(), keep_hidden ? cnt : 0);
+        StateId id;
+        if (consume && s.parent) {
+          // consume: the parent's pages move to the child; a dropped COW page is freed after the step
+          std::vector<int32_t> parent_pages = par[i]->pages;
+          for (size_t j = n_shared; j < parent_pages.size(); ++j) deferred_free.push_back(parent_pages[j]);
+          table->release(*s.parent);
+          par[i] = nullptr;
+          id = table->reserve_at(s.parent->slot, s.position + s.count, charge);
+        } else {
+          id = table->reserve(s.position + s.count, charge);
+        }
+        reserved.push_back(id);
+        sd.child = int32_t(id.slot);
+      }
+    } catch (...) {
+      fail_cleanup();
+      throw;
+    }
+
+    // upload: descriptors, new page ids, tokens (one pinned staging buffer)
+    uint8_t* sp = staging.p + sizeof(SeqDesc) * n;
+    int32_t* hp = reinterpret_cast<int32_t*>(sp);
+    std::memcpy(hp, npages.data(), npages.size() * 4);
+    uint32_t* ht = reinterpret_cast<uint32_t*>(hp + npages.size());
+    for (int i = 0; i < n; ++i) std::memcpy(ht + tok_off[i], seqs[i].tokens, seqs[i].count * 4);
+    try {
+      QWEN_CUDA(cudaMemcpyAsync(descs.p, hd, sizeof(SeqDesc) * n, cudaMemcpyHostToDevice, stream));
+      if (!npages.empty())
+        QWEN_CUDA(cudaMemcpyAsync(new_pages.p, hp, npages.size() * 4, cudaMemcpyHostToDevice, stream));
+      QWEN_CUDA(cudaMemcpyAsync(tokens.p, ht, size_t(T) * 4, cudaMemcpyHostToDevice, stream));
+      QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, stream));
+      uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4;
+      const uint64_t t_graph = now_ns();
+      ev_used = 0;
+      ev_marks.clear();
+      open_stage = -1;
+      QWEN_CUDA(cudaEventRecord(ev_begin, stream));
+      forward(n, T, R, max_len, keep_hidden, logits_out != nullptr);
+      stage_close();
+      QWEN_CUDA(cudaEventRecord(ev_end, stream));
+      if (keep_hidden)
+        for (int i = 0; i < n; ++i)
+          QWEN_CUDA(cudaMemcpyAsync(hidden_pool.p + size_t(hd[i].child) * d.chunk * d.H,
+                                    hidden_stage.p + size_t(tok_off[i]) * d.H, size_t(seqs[i].count) * d.H * 4,
+                                    cudaMemcpyDeviceToDevice, stream));
+      uint32_t h_err = 0;
+      if (sampled_out) QWEN_CUDA(cudaMemcpyAsync(sampled_out, sampled.p, size_t(R) * 4, cudaMemcpyDeviceToHost, stream));
+      if (logits_out)
+        QWEN_CUDA(cudaMemcpyAsync(logits_out, logits.p, size_t(R) * d.V * 4, cudaMemcpyDeviceToHost, stream));
+      QWEN_CUDA(cudaMemcpyAsync(&h_err, err.p, 4, cudaMemcpyDeviceToHost, stream));
+      const uint64_t t_wait = now_ns();
+      graph_ns += t_wait - t_graph;
+      QWEN_CUDA(cudaStreamSynchronize(stream));
+      const uint64_t t_done = now_ns();
+      wait_ns += t_done - t_wait;
+      ++groups;
+      float ms = 0.f;
+      QWEN_CUDA(cudaEventElapsedTime(&ms, ev_begin, ev_end));
+      last_ms = ms;
+      total_ms += ms;
+      ++timed_steps;
+      for (auto& m : ev_marks) {
+        float sm = 0.f;
+        QWEN_CUDA(cudaEventElapsedTime(&sm, ev_pool[m.second.first], ev_pool[m.second.second]));
+        stage_ms[m.first] += sm;
+        ++stage_calls[m.first];
+      }
+      if (h_err & kErrNonFinite) throw std::runtime_error("nonfinite device state");
+      if (h_err) throw std::runtime_error("device step error flag " + std::to_string(h_err));
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      fail_cleanup();
+      throw;
+    }
+    // publish
+    for (int i = 0; i < n; ++i) {
+      Version v;
+      v.pages = std::move(child_pages[i]);
+      v.hidden_rows = keep_hidden ? seqs[i].count : 0;
+      table->publish(reserved[i], std::move(v));
+      outs[i] = reserved[i];
+    }
+    unref_pages(deferred_free);
+    steps += uint64_t(n);
+    ++completed;
+    const uint64_t t_end = now_ns();
+    export_ns += 0;
+    wall_ns += t_end - t_start;
+  }
+
+  // Enqueue the whole decoder on `stream` (no host synchronisation).
+  void forward(int n, int T, int R, int max_len, bool keep_hidden, bool want_logits) {
+    (void)want_logits;
+    cudaStream_t s = stream;
+    const ModelDev& m = store->model;
+    Packed pk{cu_seqlens.p, token_seq.p, token_pos.p, slot_mapping.p, out_token.p};
+    stage(0);  // Embedding (packing + embedding)
+    launch_pack(descs.p, n, new_pages.p, block_table.p, bt_stride, pk, s);
+    if (d.n_attn > 0) launch_cow(kv, descs.p, n, new_pages.p, s);
+    launch_embed_norm(m.embed, tokens.p, T, m.layers[0].in_norm, d.eps, x.p, hb.p, s);
+    const int slots_per_tok = d.top + 1, A = T * slots_per_tok;
+    const int splits_needed = (max_len + 255) / 256;
+    attn_ws.ensure(size_t(T) * d.Hq * std::max(1, splits_needed) * (d.D + 2));
+    if (capture_routing) capture.ensure(size_t(d.L) * A);
+    captured_tokens = T;
+    const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
+    for (int li = 0; li < d.L; ++li) {
+      const LayerDev& ly = m.layers[li];
+      stage(ly.mixer == 0 ? 2 : 6);  // RecurrentProjection / AttentionProjection
+      GemmArgs g;
+      g.W = ly.in_proj;
+      g.mode = kGemmStoreF32;
+      g.X = hb.p;
+      g.ldx = d.H;
+      g.n_tokens = T;
+      g.Y = proj.p;
+      g.ldy = proj_w;
+      launch_qgemm(g, s);
+      GemmArgs o;
+      o.W = ly.out_proj;
+      o.mode = kGemmStoreF32;
+      o.X = hb2.p;
+      o.n_tokens = T;
+      o.Y = partial.p;
+      o.ldy = d.H;
+      o.split_stride = size_t(T) * d.H;
+      if (ly.mixer == 0) {
+        stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
+        launch_gdn(d, ly, proj.p, proj_w, descs.p, cu_seqlens.p, n, gdn, ly.type_index, hb2.p, err.p, s);
+        o.ldx = d.vd;
+        stage(5);  // RecurrentOutput
+      } else {
+        stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
+        launch_attn_prep(d, ly, proj.p, proj_w, token_pos.p, slot_mapping.p, T, kv, ly.type_index, q.p,
+                         gate.p, s);
+        launch_attention(d, q.p, gate.p, token_seq.p, token_pos.p, descs.p, block_table.p, bt_stride, kv,
+                         ly.type_index, T, max_len, attn_ws.p, std::max(1, splits_needed), hb2.p, s);
+        o.ldx = d.Hq * d.D;
+        stage(8);  // AttentionOutput
+      }
+      launch_qgemm(o, s);
+      stage(9);  // ResidualNorm
+      launch_residual_norm(x.p, partial.p, 1, o.split_stride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0,
+                           nullptr, s);
+      moe(ly, T, A, proj_w, s);
+      if (capture_routing)
+        QWEN_CUDA(cudaMemcpyAsync(capture.p + size_t(li) * A, ids.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
+      const float* next_norm = li + 1 < d.L ? m.layers[li + 1].in_norm : nullptr;
+      stage(13);  // MoeMixture (+ shared merge, residual, next input norm)
+      launch_moe_combine(x.p, moe_y.p, inv.p, weights.p, T, d.H, slots_per_tok, next_norm, d.eps, hb.p,
+                         nullptr, 0, nullptr, s);
+    }
+    // final norm over every token (hidden rows), lm_head on the output rows
+    stage(17);  // FinalProjection
+    launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb.p, nullptr, 0,
+                         keep_hidden ? hidden_stage.p : nullptr, s);
+    logits.ensure(size_t(R) * d.V);
+    GemmArgs lm;
+    lm.W = m.lm_head;
+    lm.mode = kGemmStoreF32;
+    lm.X = hb.p;
+    lm.ldx = d.H;
+    lm.x_row = out_token.p;
+    lm.x_div = 1;
+    lm.n_tokens = R;
+    lm.Y = logits.p;
+    lm.ldy = d.V;
+    launch_qgemm(lm, s);
+    stage(18);  // StateValidation (finite check + greedy selection)
+    launch_argmax(logits.p, R, d.V, sampled.p, err.p, s);
+    launches += 1;
+  }
+
+  void moe(const LayerDev& ly, int T, int A, int proj_w, cudaStream_t s) {
+    stage(10);  // MoeRouting
+    GemmArgs r;
+    r.W = ly.router;
+    r.mode = kGemmStoreF32;
+    r.X = hb.p;
+    r.ldx = d.H;
+    r.n_tokens = T;
+    r.Y = proj.p;
+    r.ldy = proj_w;
+    launch_qgemm(r, s);
+    launch_route(proj.p, proj_w, T, d.E, d.top, ids.p, weights.p, s);
+    launch_expert_sort(ids.p, A, d.E + 1, counts.p, offsets.p, perm.p, inv.p, s);
+    stage(11);  // MoeUpGate
+    GemmArgs gu;
+    gu.W = ly.expert_gu;
+    gu.mode = kGemmGateUp;
+    gu.expert_tiles = 2 * d.I / kTileRows;
+    gu.X = hb.p;
+    gu.ldx = d.H;
+    gu.x_row = perm.p;
+    gu.x_div = d.top + 1;
+    gu.group_off = offsets.p;
+    gu.groups = d.E + 1;
+    gu.Yb = act.p;
+    gu.ldyb = d.I;
+    launch_qgemm(gu, s);
+    stage(12);  // MoeDown
+    GemmArgs dn;
+    dn.W = ly.expert_dn;
+    dn.mode = kGemmDown;
+    dn.expert_tiles = d.H / kTileRows;
+    dn.X = act.p;
+    dn.ldx = d.I;
+    dn.group_off = offsets.p;
+    dn.groups = d.E + 1;
+    dn.Y = moe_y.p;
+    dn.ldy = d.H;
+    launch_qgemm(dn, s);
+  }
+};
+
+Session* S(void* h) {
+  if (!h) throw std::invalid_argument("null session");
+  return static_cast<Session*>(h);
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------- C ABI --
+extern "C" {
+
+const char* rs_mlx_version(void) { return "qwen-b200-cuda sm_100a"; }
+
+size_t rs_qwen_state_count(const rs_qwen_config* c) { return c ? Dims::from(*c).state_count() : 0; }
+
+void* rs_mlx_weights_create(char* error, size_t capacity) {
+  void* out = nullptr;
+  checked(error, capacity, [&] {
+    auto* w = new WeightStore();
+    QWEN_CUDA(cudaGetDevice(&w->device));
+    out = w;
+  });
+  return out;
+}
+
+void rs_mlx_weights_destroy(void* store) { delete static_cast<WeightStore*>(store); }
+
+int rs_mlx_weights_load(void* store, const char* file, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!store || !file) throw std::invalid_argument("invalid weight load descriptor");
+    throw std::runtime_error(
+        "safetensors ingestion is not implemented by the CUDA backend; use rs_qwen_weights_synthetic");
+  });
+}
+
+int rs_qwen_quant(void* store, const char* module, int group, int bits, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!store || !module || !(group == 32 || group == 64 || group == 128) ||
+        !(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8))
+      throw std::invalid_argument("invalid model quantization");
+    if (group != 64 || bits != 4)
+      throw std::invalid_argument("CUDA backend kernels implement 4-bit affine group 64 only");
+    static_cast<WeightStore*>(store)->quant[module] = {group, bits};
+  });
+}
+
+int rs_mlx_weight_bytes(void* store, const char* name, const int32_t* shape, size_t rank, int dtype,
+                        size_t offset, uint8_t* output, size_t count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!store || !name || !output) throw std::invalid_argument("invalid weight bytes descriptor");
+    (void)shape;
+    (void)rank;
+    if (dtype != 0 && dtype != 2) throw std::invalid_argument("weight bytes dtype");
+    auto* w = static_cast<WeightStore*>(store);
+    QWEN_CUDA(cudaSetDevice(w->device));
+    w->export_bytes(name, offset, output, count);
+  });
+}
+
+int rs_qwen_weights_synthetic(void* store, const rs_qwen_config* config, uint64_t seed, int with_mtp,
+                              char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!store || !config) throw std::invalid_argument("invalid synthetic weight descriptor");
+    auto* w = static_cast<WeightStore*>(store);
+    QWEN_CUDA(cudaSetDevice(w->device));
+    w->synthesize(*config, seed, with_mtp != 0);
+  });
+}
+
+void* rs_qwen_device_create(void* weights, int gpu, const rs_qwen_config* config, const rs_qwen_layer* layers,
+                            size_t count, size_t slots, uint64_t bytes, char* error, size_t capacity) {
+  void* out = nullptr;
+  checked(error, capacity, [&] {
+    if (!weights || !config || !layers) throw std::invalid_argument("device session descriptor");
+    auto s = std::make_unique<Session>();
+    s->init(static_cast<WeightStore*>(weights), gpu, *config, layers, count, slots, bytes);
+    out = s.release();
+  });
+  return out;
+}
+
+void rs_qwen_device_destroy(void* session) {
+  if (!session) return;
+  auto* s = static_cast<Session*>(session);
+  cudaSetDevice(s->device);
+  cudaStreamSynchronize(s->stream);
+  delete s;
+}
+
+int rs_qwen_device_step_ragged(void* session, size_t n_seq, const StateId* parents, const uint32_t* positions,
+                               const uint32_t* counts, const uint32_t* tokens_flat, uint32_t flags,
+                               StateId* outs, uint32_t* sampled, size_t sampled_count, float* logits,
+                               size_t logits_count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!n_seq || !positions || !counts || !tokens_flat || !outs) throw std::invalid_argument("ragged step descriptor");
+    if (flags & ~uint32_t(31)) throw std::invalid_argument("unknown ragged step flags");
+    std::vector<Session::SeqIn> seqs(n_seq);
+    size_t off = 0, rows = 0;
+    for (size_t i = 0; i < n_seq; ++i) {
+      const bool has_parent = parents && positions[i] != 0;
+      seqs[i] = {has_parent ? &parents[i] : nullptr, positions[i], counts[i], tokens_flat + off};
+      off += counts[i];
+      rows += (flags & RS_QWEN_RAGGED_ALL_ROWS) ? counts[i] : 1;
+    }
+    if ((flags & RS_QWEN_RAGGED_SAMPLED) && (!sampled || sampled_count != rows))
+      throw std::invalid_argument("sampled output capacity");
+    if ((flags & RS_QWEN_RAGGED_LOGITS) && (!logits || logits_count != rows * size_t(s->d.V)))
+      throw std::invalid_argument("logits output capacity");
+    s->step(seqs, flags, outs, (flags & RS_QWEN_RAGGED_SAMPLED) ? sampled : nullptr,
+            (flags & RS_QWEN_RAGGED_LOGITS) ? logits : nullptr);
+  });
+}
+
+int rs_qwen_device_decode_batch(void* session, const StateId* parents, const uint32_t* tokens, size_t batch,
+                                StateId* outputs, float* logits, size_t logits_count, char* error,
+                                size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!parents || !tokens || !outputs || !logits || batch < 1) throw std::invalid_argument("batch descriptor");
+    if (logits_count != batch * size_t(s->d.V)) throw std::invalid_argument("batch geometry");
+    std::vector<Session::SeqIn> seqs(batch);
+    for (size_t i = 0; i < batch; ++i) {
+      if (!parents[i].position) throw std::invalid_argument("batch parent/token geometry");
+      seqs[i] = {&parents[i], uint32_t(parents[i].position), 1, tokens + i};
+    }
+    s->step(seqs, RS_QWEN_RAGGED_LOGITS, outputs, nullptr, logits);
+  });
+}
+
+static int device_step(void* session, const StateId* previous, size_t position, const uint32_t* tokens,
+                       size_t count, StateId* output, float* logits, size_t logits_count, char* error,
+                       size_t capacity, bool all_logits, bool hidden, uint32_t* sampled) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!output || !tokens || (!logits && !sampled)) throw std::invalid_argument("device step descriptor");
+    if (!count || count > size_t(s->d.chunk) || position > size_t(s->d.ctx) ||
+        count > size_t(s->d.ctx) - position ||
+        (sampled ? logits_count != 0 : logits_count != size_t(s->d.V) * (all_logits ? count : 1)))
+      throw std::invalid_argument("device step capacity");
+    if ((position == 0) != (previous == nullptr)) throw std::invalid_argument("device previous state presence");
+    std::vector<Session::SeqIn> seqs{{previous, uint32_t(position), uint32_t(count), tokens}};
+    uint32_t flags = (sampled ? RS_QWEN_RAGGED_SAMPLED : RS_QWEN_RAGGED_LOGITS) |
+                     (all_logits ? RS_QWEN_RAGGED_ALL_ROWS : 0) | (hidden ? RS_QWEN_RAGGED_HIDDEN : 0);
+    s->step(seqs, flags, output, sampled, logits);
+  });
+}
+
+int rs_qwen_device_step(void* h, const StateId* p, size_t position, const uint32_t* t, size_t n, StateId* out,
+                        float* logits, size_t lc, float* trace, size_t tc, char* e, size_t ec) {
+  if (trace || tc) {
+    report(e, ec, "trace capture is an MLX-baseline diagnostic not offered by the CUDA backend");
+    return -1;
+  }
+  return device_step(h, p, position, t, n, out, logits, lc, e, ec, false, false, nullptr);
+}
+int rs_qwen_device_step_sampled(void* h, const StateId* p, size_t position, const uint32_t* t, size_t n,
+                                StateId* out, uint32_t* token, char* e, size_t ec) {
+  if (!token) {
+    report(e, ec, "device step descriptor");
+    return -1;
+  }
+  return device_step(h, p, position, t, n, out, nullptr, 0, e, ec, false, false, token);
+}
+int rs_qwen_device_block(void* h, const StateId* p, size_t position, const uint32_t* t, size_t n, StateId* out,
+                         float* logits, size_t lc, char* e, size_t ec) {
+  return device_step(h, p, position, t, n, out, logits, lc, e, ec, true, false, nullptr);
+}
+int rs_qwen_device_hidden_step(void* h, const StateId* p, size_t position, const uint32_t* t, size_t n,
+                               StateId* out, float* logits, size_t lc, char* e, size_t ec) {
+  return device_step(h, p, position, t, n, out, logits, lc, e, ec, false, true, nullptr);
+}
+int rs_qwen_device_hidden_block(void* h, const StateId* p, size_t position, const uint32_t* t, size_t n,
+                                StateId* out, float* logits, size_t lc, char* e, size_t ec) {
+  return device_step(h, p, position, t, n, out, logits, lc, e, ec, true, true, nullptr);
+}
+
+int rs_qwen_device_release(void* session, const StateId* id, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!id) throw std::invalid_argument("release descriptor");
+    std::vector<int32_t> pages = s->table->get(*id).pages;
+    s->table->release(*id);
+    s->unref_pages(pages);
+  });
+}
+
+int rs_qwen_device_snapshot(void* session, const StateId* id, float* output, size_t count, char* error,
+                            size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!id || !output) throw std::invalid_argument("snapshot descriptor");
+    const Version& v = s->table->get(*id);
+    const Dims& d = s->d;
+    if (count != d.state_count()) throw std::invalid_argument("snapshot capacity");
+    s->set_device();
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    size_t off = 0;
+    const size_t slot = id->slot, pos = id->position;
+    std::vector<__nv_bfloat16> page(s->kv.page_elems());
+    for (int li = 0; li < d.L; ++li) {
+      const LayerDev& ly = s->store->model.layers[li];
+      if (ly.mixer == 0) {
+        const size_t cl = s->gdn.conv_elems, sl = s->gdn.state_elems;
+        QWEN_CUDA(cudaMemcpy(output + off, s->gdn.conv + (slot * d.n_gdn + ly.type_index) * cl, cl * 4,
+                             cudaMemcpyDeviceToHost));
+        off += cl;
+        QWEN_CUDA(cudaMemcpy(output + off, s->gdn.state + (slot * d.n_gdn + ly.type_index) * sl, sl * 4,
+                             cudaMemcpyDeviceToHost));
+        off += sl;
+      } else {
+        const size_t per = size_t(d.Hkv) * d.ctx * d.D;
+        std::fill(output + off, output + off + 2 * per, 0.f);
+        for (size_t pi = 0; pi < v.pages.size(); ++pi) {
+          QWEN_CUDA(cudaMemcpy(page.data(), s->kv.page(ly.type_index, v.pages[pi]), page.size() * 2,
+                               cudaMemcpyDeviceToHost));
+          for (int kvsel = 0; kvsel < 2; ++kvsel)
+            for (int g = 0; g < d.Hkv; ++g)
+              for (int o = 0; o < kPageTokens; ++o) {
+                const size_t p = pi * kPageTokens + o;
+                if (p >= pos) continue;
+                const __nv_bfloat16* src = page.data() + ((size_t(kvsel) * d.Hkv + g) * kPageTokens + o) * d.D;
+                float* dst = output + off + kvsel * per + (size_t(g) * d.ctx + p) * d.D;
+                for (int i = 0; i < d.D; ++i) dst[i] = __bfloat162float(src[i]);
+              }
+        }
+        off += 2 * per;
+      }
+    }
+    if (off != count) throw std::runtime_error("snapshot accounting");
+    s->exports += count * 4;
+  });
+}
+
+int rs_qwen_device_hidden_snapshot(void* session, const StateId* id, float* output, size_t count, char* error,
+                                   size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!id || !output) throw std::invalid_argument("hidden snapshot descriptor");
+    const Version& v = s->table->get(*id);
+    if (!v.hidden_rows || count != size_t(v.hidden_rows) * s->d.H)
+      throw std::invalid_argument("missing hidden or snapshot capacity");
+    s->set_device();
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    QWEN_CUDA(cudaMemcpy(output, s->hidden_pool.p + id->slot * size_t(s->d.chunk) * s->d.H, count * 4,
+                         cudaMemcpyDeviceToHost));
+    s->exports += count * 4;
+  });
+}
+
+int rs_qwen_device_stats(void* session, uint64_t* output, size_t count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!output || count != kStatsCount) throw std::invalid_argument("stats capacity");
+    std::fill(output, output + count, 0);
+    output[0] = s->table->residents();
+    output[1] = s->table->bytes();
+    output[2] = s->exports;
+    output[3] = s->uploads;
+    output[4] = s->steps;
+    size_t free_b = 0, total_b = 0;
+    s->set_device();
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) output[5] = total_b - free_b;
+    output[6] = output[5];
+    output[7] = s->calls;
+    output[8] = s->completed;
+    output[9] = s->graph_ns;
+    output[10] = s->wait_ns;
+    output[11] = s->export_ns;
+    output[12] = s->wall_ns;
+    output[13] = s->groups;
+    output[16] = kernel_launches();
+    for (int i = 0; i < 19; ++i) {
+      output[17 + i * 3] = s->stage_calls[i];
+      output[19 + i * 3] = uint64_t(s->stage_ms[i] * 1e6);
+    }
+  });
+}
+
+int rs_qwen_device_drain(void* session, uint64_t* invalidated, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!invalidated) throw std::invalid_argument("drain descriptor");
+    *invalidated = s->table->residents();
+    s->set_device();
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    s->table->clear();
+    const size_t np = s->page_ref.size();
+    s->free_pages.resize(np);
+    for (size_t i = 0; i < np; ++i) s->free_pages[i] = int32_t(np - 1 - i);
+    std::fill(s->page_ref.begin(), s->page_ref.end(), 0);
+    std::fill(s->page_filled.begin(), s->page_filled.end(), 0);
+    if (s->table->residents() || s->table->bytes()) throw std::runtime_error("device drain residual");
+  });
+}
+
+int rs_qwen_device_set_capture(void* session, int routing, char* error, size_t capacity) {
+  return checked(error, capacity, [&] { S(session)->capture_routing = routing != 0; });
+}
+
+int rs_qwen_device_debug_routing(void* session, int32_t* out, size_t count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!s->capture_routing || !out) throw std::invalid_argument("routing capture disabled");
+    const int T = s->captured_tokens, K = s->d.top, A = T * (K + 1);
+    if (count != size_t(s->d.L) * T * K) throw std::invalid_argument("routing capture capacity");
+    s->set_device();
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    std::vector<int32_t> all(size_t(s->d.L) * A);
+    QWEN_CUDA(cudaMemcpy(all.data(), s->capture.p, all.size() * 4, cudaMemcpyDeviceToHost));
+    for (int l = 0; l < s->d.L; ++l)
+      for (int t = 0; t < T; ++t)
+        for (int j = 0; j < K; ++j) out[(size_t(l) * T + t) * K + j] = all[size_t(l) * A + t * (K + 1) + j];
+  });
+}
+
+int rs_qwen_device_mtp_attach(void* session, void* weights, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    (void)S(session);
+    (void)weights;
+    throw std::runtime_error("MTP head not available in this build");
+  });
+}
+int rs_qwen_device_mtp_step(void* session, const StateId*, const StateId*, int, size_t, const uint32_t*, size_t,
+                            StateId*, float*, size_t, int, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    (void)S(session);
+    throw std::runtime_error("MTP head not available in this build");
+  });
+}
+int rs_qwen_device_mtp_release(void* session, const StateId*, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    (void)S(session);
+    throw std::runtime_error("MTP head not available in this build");
+  });
+}
+int rs_qwen_device_mtp_snapshot(void* session, const StateId*, float*, size_t, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    (void)S(session);
+    throw std::runtime_error("MTP head not available in this build");
+  });
+}
+int rs_qwen_device_mtp_verify_accept(void* session, size_t, const StateId*, const uint32_t*, const uint32_t*,
+                                     const uint32_t*, size_t, const uint32_t*, size_t, uint32_t, StateId*,
+                                     uint32_t*, uint32_t*, uint32_t*, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    (void)S(session);
+    throw std::runtime_error("MTP verify not available in this build");
+  });
+}
+
+int rs_qwen_device_set_profile(void* session, int profile, char* error, size_t capacity) {
+  return checked(error, capacity, [&] { S(session)->profile = profile != 0; });
+}
+
+int rs_qwen_device_timing(void* session, double* out, size_t count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!out || count != 3 + 19) throw std::invalid_argument("timing capacity");
+    out[0] = s->last_ms;
+    out[1] = s->total_ms;
+    out[2] = double(s->timed_steps);
+    for (int i = 0; i < 19; ++i) out[3 + i] = s->stage_ms[i];
+  });
+}
+
+int rs_qwen_device_synthetic_state(void* session, size_t position, uint64_t seed, StateId* out, char* error,
+                                   size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!out || !position || position > size_t(s->d.ctx)) throw std::invalid_argument("synthetic state geometry");
+    s->set_device();
+    const int n_pages = s->d.n_attn > 0 ? int((position + kPageTokens - 1) / kPageTokens) : 0;
+    if (n_pages > int(s->free_pages.size())) throw std::runtime_error("KV page pool exhausted");
+    if (s->table->residents() + 1 > s->slots) throw std::runtime_error("combined resident budget exhausted");
+    StateId id = s->table->reserve(position, s->version_bytes(n_pages, 0));
+    Version v;
+    for (int j = 0; j < n_pages; ++j) {
+      const int32_t p = s->free_pages.back();
+      s->free_pages.pop_back();
+      s->page_ref[p] = 1;
+      s->page_filled[p] = uint8_t(std::min<size_t>(kPageTokens, position - size_t(j) * kPageTokens));
+      v.pages.push_back(p);
+    }
+    try {
+      s->new_pages.ensure(std::max(1, n_pages));
+      if (n_pages) {
+        QWEN_CUDA(cudaMemcpyAsync(s->block_table.p + id.slot * size_t(s->bt_stride), v.pages.data(),
+                                  size_t(n_pages) * 4, cudaMemcpyHostToDevice, s->stream));
+        QWEN_CUDA(cudaMemcpyAsync(s->new_pages.p, v.pages.data(), size_t(n_pages) * 4, cudaMemcpyHostToDevice,
+                                  s->stream));
+      }
+      launch_synth_state(s->kv, s->new_pages.p, n_pages, int(position), s->d.ctx, s->gdn, int(id.slot), s->d,
+                         seed, s->stream);
+      QWEN_CUDA(cudaGetLastError());
+      QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    } catch (...) {
+      s->unref_pages(v.pages);
+      s->table->rollback(id);
+      throw;
+    }
+    s->table->publish(id, std::move(v));
+    *out = id;
+  });
+}
+
+}  // extern "C"
