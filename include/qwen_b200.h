@@ -245,6 +245,15 @@ int rs_qwen_device_debug_routing(void* session, int32_t* out, size_t count, char
 int rs_qwen_device_set_profile(void* session, int profile, char* error, size_t capacity);
 int rs_qwen_device_timing(void* session, double* out, size_t count, char* error, size_t capacity);
 
+/* NEW diagnostic: run one dense 4-bit GEMM of the model on caller inputs.
+ * which: 0 = layer `layer` mixer input projection, 1 = its output projection,
+ * 2 = its MoE router (+ shared gate), 3 = lm_head. x: T rows of bf16 bits
+ * (row width = the matrix's input width). y: T x rows fp32 (split-K partials
+ * summed). engine: 0 = tcgen05 kernel, 1 = CUDA-core reference kernel.
+ * ms: device time of the GEMM launch(es). Returns 0/-1. */
+int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, size_t T, float* y,
+                       size_t y_count, int engine, double* ms, char* error, size_t capacity);
+
 /* Number of floats of a version's reference-layout snapshot
  * (native/qwen_model.inc:268-271 qwen_state_count). */
 size_t rs_qwen_state_count(const rs_qwen_config* config);

@@ -97,6 +97,8 @@ SIGNATURES = {
     "rs_qwen_device_set_profile": (C.c_int, [_P, C.c_int, _ERR, _SZ]),
     "rs_qwen_device_timing": (C.c_int, [_P, C.POINTER(C.c_double), _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_routing": (C.c_int, [_P, _I32P, _SZ, _ERR, _SZ]),
+    "rs_qwen_debug_gemm": (C.c_int, [_P, C.c_int, C.c_int, C.POINTER(C.c_uint16), _SZ, _F32P, _SZ, C.c_int,
+                                     C.POINTER(C.c_double), _ERR, _SZ]),
 }
 
 _lib = None
@@ -311,6 +313,16 @@ class DeviceSession:
         out = (C.c_double * 22)()
         _call("rs_qwen_device_timing", self.h, out, 22)
         return out[0], out[1], int(out[2]), list(out[3:])
+
+    def debug_gemm(self, which: int, layer: int, x_bf16, rows: int, engine: int = 0):
+        """Run one dense GEMM (0 in_proj, 1 out_proj, 2 router, 3 lm_head); returns (y, ms)."""
+        x = np.ascontiguousarray(x_bf16, np.uint16)
+        T = x.shape[0]
+        y = np.zeros((T, rows), np.float32)
+        ms = C.c_double()
+        _call("rs_qwen_debug_gemm", self.h, which, layer, x.ctypes.data_as(C.POINTER(C.c_uint16)), T,
+              _ptr(y, C.c_float), y.size, engine, C.byref(ms))
+        return y, ms.value
 
     def debug_routing(self, tokens: int):
         out = np.zeros((self.cfg.layers, tokens, self.cfg.top), np.int32)

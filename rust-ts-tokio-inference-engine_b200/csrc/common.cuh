@@ -18,9 +18,11 @@
 namespace qwen {
 
 // 4-bit affine g64 weight tile: 128 rows x 64 columns (one quant group per row).
-// Layout: packed nibbles [128 rows][32 bytes] (canonical LSB-first order inside a
-// row: byte j holds columns 2j (low nibble) and 2j+1), then 128 bf16 scales,
-// then 128 bf16 biases. A matrix [rows, K] is stored as
+// Layout: packed nibbles [128 rows][8 uint32 words], then 128 bf16 scales, then
+// 128 bf16 biases. Word w of a row holds columns 8w..8w+7 in pair-interleaved
+// nibble order: nibble i (bits 4i..4i+3) holds column 8w + nibble_col(i) with
+// nibble_col = {0,2,4,6,1,3,5,7}, so ((word >> 4j) & 0x000F000F) yields the
+// consecutive pair (8w+2j, 8w+2j+1) in the low/high 16-bit halves. A matrix [rows, K] is stored as
 // [ceil(rows/128) row tiles][K/64 column chunks] tiles, each 4608 bytes, so one
 // tile is one contiguous bulk copy.
 constexpr int kTileRows = 128;
@@ -28,6 +30,11 @@ constexpr int kTileK = 64;
 constexpr int kTilePackedBytes = kTileRows * kTileK / 2;  // 4096
 constexpr int kTileBytes = kTilePackedBytes + kTileRows * 2 * 2;  // 4608
 constexpr int kPageTokens = 16;  // paged-KV page size (tokens)
+
+// Nibble index holding column c (0..7) of a packed word, and its inverse.
+__host__ __device__ __forceinline__ int nibble_of_col(int c) { return (c & 1) ? 4 + (c >> 1) : (c >> 1); }
+__host__ __device__ __forceinline__ int col_of_nibble(int i) { return i < 4 ? 2 * i : 2 * (i - 4) + 1; }
+__device__ __forceinline__ uint32_t nibble(uint32_t word, int col) { return (word >> (4 * nibble_of_col(col))) & 15u; }
 
 struct QMat {
   const uint8_t* tiles = nullptr;

@@ -108,7 +108,7 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
         reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float v = fmaf(sc, float((word >> (4 * j)) & 15u), bi);
+      const float v = fmaf(sc, float(nibble(word, j)), bi);
       xr[c0 + j] = v;
       ss += v * v;
     }
@@ -160,8 +160,9 @@ __global__ void residual_norm_kernel(float* x, const float* __restrict__ partial
 //   y = rms(o, norm.weight) * silu(z)   (native/qwen_model.inc:203-204)
 template <int DK, int DV, int R>
 __global__ void __launch_bounds__(256 * R) gdn_kernel(
-    const float* __restrict__ proj, int ld, const SeqDesc* __restrict__ descs,
-    const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li, int hk, int hv, int conv,
+    const float* __restrict__ proj, int ld, int splits, size_t split_stride,
+    const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
+    int hk, int hv, int conv,
     float eps, const float* __restrict__ conv_w, const float* __restrict__ a_log,
     const float* __restrict__ dt_bias, const float* __restrict__ gnorm, __nv_bfloat16* out,
     uint32_t* err) {
@@ -209,11 +210,16 @@ __global__ void __launch_bounds__(256 * R) gdn_kernel(
     }
   }
 
+  auto P = [&](const float* pr, int col) {
+    float v = pr[col];
+    for (int s = 1; s < splits; ++s) v += pr[s * split_stride + col];
+    return v;
+  };
   for (int i = 0; i < d.count; ++i) {
     const int t = t0 + i;
     const float* pr = proj + size_t(t) * ld;
     if (gc >= 0) {
-      const float cur = pr[gc];
+      const float cur = P(pr, gc);
       float acc = 0.f;
       for (int j = 0; j < conv - 1; ++j) acc += taps[j] * cw[j];
       acc += cur * cw[conv - 1];
@@ -227,10 +233,10 @@ __global__ void __launch_bounds__(256 * R) gdn_kernel(
     }
     if (threadIdx.x < R) {
       const int h = kh * R + threadIdx.x;
-      const float av = pr[cd + vd + h] + dt_bias[h];
+      const float av = P(pr, cd + vd + h) + dt_bias[h];
       const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
       gs[threadIdx.x] = expf(-expf(a_log[h]) * sp);
-      bs[threadIdx.x] = sigmoidf_(pr[cd + vd + hv + h]);
+      bs[threadIdx.x] = sigmoidf_(P(pr, cd + vd + hv + h));
     }
     __syncthreads();
     if (threadIdx.x < 64) {  // warps 0/1: squared norms of q / k
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(256 * R) gdn_kernel(
       if (tig < DV) {
         float tot = 0.f;
         for (int w = 0; w < 8; ++w) tot += red[0][grp * 8 + w];
-        const float z = pr[cd + head * DV + tig];
+        const float z = P(pr, cd + head * DV + tig);
         const float y = o * rsqrtf(tot / DV + eps) * gnorm[tig] * siluf_(z);
         out[size_t(t) * vd + head * DV + tig] = __float2bfloat16_rn(y);
       }
@@ -310,7 +316,8 @@ __global__ void __launch_bounds__(256 * R) gdn_kernel(
 // ----------------------------------------------------------------- attention --
 // Per token: q/k RMSNorm (q_norm/k_norm), partial rotate-half RoPE on the
 // first rope dims (angle in double precision), KV append into the paged cache.
-__global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int Hq, int Hkv, int D,
+__global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
+                                 int Hq, int Hkv, int D,
                                  int rope, double theta, float eps, const float* __restrict__ qn,
                                  const float* __restrict__ kn, const int32_t* __restrict__ token_pos,
                                  const int64_t* __restrict__ slots, KvPool kv, int layer, float* q,
@@ -330,7 +337,12 @@ __global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int Hq,
     else if (v < Hq + Hkv) { src = pr + Hq * 2 * D + (v - Hq) * D; w = kn; }
     else src = pr + Hq * 2 * D + Hkv * D + (v - Hq - Hkv) * D;
     float ss = 0.f;
-    for (int i = lane; i < D; i += 32) { buf[i] = src[i]; ss += src[i] * src[i]; }
+    for (int i = lane; i < D; i += 32) {
+      float v = src[i];
+      for (int sp = 1; sp < splits; ++sp) v += src[sp * split_stride + i];
+      buf[i] = v;
+      ss += v * v;
+    }
     ss = warp_sum(ss);
     __syncwarp();
     if (w) {
@@ -349,7 +361,9 @@ __global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int Hq,
     if (v < Hq) {
       for (int i = lane; i < D; i += 32) {
         q[(size_t(t) * Hq + v) * D + i] = buf[i];
-        gate[(size_t(t) * Hq + v) * D + i] = src[D + i];
+        float gv = src[D + i];
+        for (int sp = 1; sp < splits; ++sp) gv += src[sp * split_stride + D + i];
+        gate[(size_t(t) * Hq + v) * D + i] = gv;
       }
     } else {
       const int g = v < Hq + Hkv ? v - Hq : v - Hq - Hkv;
@@ -446,8 +460,8 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
 // asc) on the fp32 total order; weights renormalised over the selection
 // (native/qwen_model.inc:77-79: softmax then divide by the selected sum);
 // slot `top` is the shared expert (id E) with weight sigmoid(shared gate).
-__global__ void route_kernel(const float* __restrict__ logits, int ld, int T, int E, int top,
-                             int32_t* ids, float* weights) {
+__global__ void route_kernel(const float* __restrict__ logits, int ld, int splits, size_t split_stride,
+                             int T, int E, int top, int32_t* ids, float* weights) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* lr = logits + size_t(warp) * ld;
@@ -457,7 +471,17 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int T, in
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int e = i * 32 + lane;
-    v[i] = e < E ? lr[e] : 0.f;
+    float x = 0.f;
+    if (e < E) {
+      x = lr[e];
+      for (int sp = 1; sp < splits; ++sp) x += lr[sp * split_stride + e];
+    }
+    v[i] = x;
+  }
+  float shared_logit = 0.f;
+  if (lane == 0) {
+    shared_logit = lr[E];
+    for (int sp = 1; sp < splits; ++sp) shared_logit += lr[sp * split_stride + E];
   }
   float sel_val = 0.f, top_val = 0.f, denom = 0.f;
   int32_t* out_ids = ids + size_t(warp) * (top + 1);
@@ -479,7 +503,13 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int T, in
     }
     const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
     if ((e & 31) == lane) taken |= 1u << (e >> 5);
-    sel_val = lr[e];
+    {
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i)
+        if (i == (e >> 5)) mine = v[i];
+      sel_val = __shfl_sync(0xffffffffu, mine, e & 31);
+    }
     if (r == 0) top_val = sel_val;
     const float w = expf(sel_val - top_val);
     denom += w;
@@ -489,7 +519,7 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int T, in
   if (lane == 0) {
     for (int r = 0; r < top; ++r) out_w[r] = out_w[r] / denom;
     out_ids[top] = E;
-    out_w[top] = 1.f / (1.f + expf(-lr[E]));
+    out_w[top] = 1.f / (1.f + expf(-shared_logit));
   }
 }
 
@@ -548,6 +578,17 @@ __global__ void moe_combine_kernel(float* x, const float* __restrict__ y, const 
   const float inv_r = rsqrtf(tot / H + eps);
   for (int c = threadIdx.x; c < H; c += blockDim.x)
     hb[size_t(t) * H + c] = __float2bfloat16_rn(xr[c] * inv_r * norm_w[c]);
+}
+
+// X_perm[p] = X[perm[p] / slots]: expert-sorted copy of the MoE input rows
+// (contiguous per expert, so the GEMM's TMA loads one box per expert).
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int ld, const int32_t* __restrict__ perm,
+                                   int div, int H, __nv_bfloat16* dst) {
+  const int p = blockIdx.x;
+  const int row = perm[p] / div;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(row) * ld);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + size_t(p) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d4[i] = s4[i];
 }
 
 // Greedy selection per row: IEEE total order, lowest index on ties
@@ -662,15 +703,16 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
   count_launch();
 }
 
-void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
-                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
+void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
+                size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
                 int gdn_index, __nv_bfloat16* out, uint32_t* err, cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
   dim3 grid(n_seq, d.hk);
 #define QWEN_GDN(DK_, DV_, R_)                                                                    \
   if (d.dk == DK_ && d.dv == DV_ && R == R_) {                                                   \
-    gdn_kernel<DK_, DV_, R_><<<grid, 256 * R_, 0, s>>>(proj, ld_proj, descs, cu_seqlens, pool,   \
+    gdn_kernel<DK_, DV_, R_><<<grid, 256 * R_, 0, s>>>(proj, ld_proj, splits, split_stride, descs, \
+                                                       cu_seqlens, pool,                         \
                                                        gdn_index, d.hk, d.hv, d.conv, d.eps,     \
                                                        ly.conv_w, ly.a_log, ly.dt_bias, ly.gnorm, \
                                                        out, err);      \
@@ -685,12 +727,12 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   throw std::invalid_argument("DeltaNet geometry unsupported (dk = dv in {64,128}, hv/hk in {1,2})");
 }
 
-void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
-                      const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
+void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
+                      size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s) {
   if (T <= 0) return;
   attn_prep_kernel<<<T, 256, 8 * d.D * sizeof(float), s>>>(
-      proj, ld_proj, d.Hq, d.Hkv, d.D, d.rope, double(d.theta), d.eps, ly.q_norm, ly.k_norm,
+      proj, ld_proj, splits, split_stride, d.Hq, d.Hkv, d.D, d.rope, double(d.theta), d.eps, ly.q_norm, ly.k_norm,
       token_pos, slot_mapping, kv, kv_layer, q, gate);
   count_launch();
 }
@@ -726,11 +768,11 @@ void launch_attention(const Dims& d, const float* q, const float* gate, const in
 
 int attention_max_splits(int ctx) { return (ctx + kSplitTokens - 1) / kSplitTokens; }
 
-void launch_route(const float* logits, int ld, int T, int E, int top, int32_t* ids, float* weights,
-                  cudaStream_t s) {
+void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
+                  int32_t* ids, float* weights, cudaStream_t s) {
   if (E > 1024) throw std::invalid_argument("more than 1024 experts");
   if (T <= 0) return;
-  route_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, T, E, top, ids, weights);
+  route_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, splits, split_stride, T, E, top, ids, weights);
   count_launch();
 }
 
@@ -754,6 +796,13 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
   moe_combine_kernel<<<T, 256, 0, s>>>(x, y_sorted, inv, weights, H, slots, norm_w, eps, hb);
+  count_launch();
+}
+
+void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
+                        __nv_bfloat16* dst, cudaStream_t s) {
+  if (n <= 0) return;
+  gather_rows_kernel<<<n, 128, 0, s>>>(src, ld, perm, div, H, dst);
   count_launch();
 }
 

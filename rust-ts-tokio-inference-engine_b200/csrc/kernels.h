@@ -88,18 +88,18 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
                           const int32_t* out_token, int rows, float* hidden_f32,
                           cudaStream_t s);
 void launch_qgemm(const GemmArgs& a, cudaStream_t s);
-void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
-                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
+void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
+                size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
                 int gdn_index, __nv_bfloat16* out, uint32_t* err, cudaStream_t s);
-void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
-                      const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
+void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
+                      size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);
 void launch_attention(const Dims& d, const float* q, const float* gate, const int32_t* token_seq,
                       const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table,
                       int bt_stride, KvPool kv, int kv_layer, int T, int max_len, float* ws,
                       int max_splits, __nv_bfloat16* out, cudaStream_t s);
-void launch_route(const float* logits, int ld, int T, int E, int top, int32_t* ids,
-                  float* weights, cudaStream_t s);
+void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
+                  int32_t* ids, float* weights, cudaStream_t s);
 void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
                         int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s);
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
@@ -110,7 +110,7 @@ void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint3
                    cudaStream_t s);
 void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,
                         GdnPool pool, int slot, const Dims& d, uint64_t seed, cudaStream_t s);
-void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* rows, int n, int H,
+void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
                         __nv_bfloat16* dst, cudaStream_t s);
 
 }  // namespace qwen

@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
       const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
       float w[kTileK];
 #pragma unroll
-      for (int j = 0; j < kTileK; ++j) w[j] = fmaf(sc, float((words[j / 8] >> (4 * (j % 8))) & 15u), bi);
+      for (int j = 0; j < kTileK; ++j) w[j] = fmaf(sc, float(nibble(words[j / 8], j % 8)), bi);
 #pragma unroll
       for (int i = 0; i < kTok; ++i) {
         if (i < nt) {

@@ -1,0 +1,438 @@
+// tcgen05 grouped GEMM over 4-bit affine (group 64, bf16 scale/bias) weights.
+//
+//   D[w_row, token] = sum_k deq(W)[w_row, k] * X[token, k]
+//
+// Weight rows are the MMA's M dimension (128 per tile), tokens are N (16..128),
+// so the tiny token counts of decode (1-10 rows per expert) cost one N=16 MMA.
+// Per CTA (persistent, one per SM), warp-specialised:
+//   warp 0  producer: cp.async.bulk of each 4608-byte weight tile and a TMA
+//           (128B-swizzled) load of the matching 64-column activation tile into
+//           an S-stage shared-memory ring (mbarrier complete_tx);
+//   warp 1  MMA issuer: allocates TMEM, issues tcgen05.mma (A from TMEM, B from
+//           shared memory) and tcgen05.commit to release stages;
+//   warps 2-5 dequantise: each thread owns one weight row, turns its 64 nibbles
+//           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
+//           them into TMEM with tcgen05.st (the A operand); they also run the
+//           epilogue (tcgen05.ld of the fp32 accumulator, split-K partial
+//           store / SwiGLU / fp32 store).
+// The dequantised weights never touch shared memory. Every mbarrier wait is
+// bounded (~1 s); on expiry the kernel raises kErrTimeout and drains out.
+#include <cuda.h>
+
+#include <atomic>
+
+#include "kernels.h"
+#include "qgemm_tc.h"
+
+namespace qwen {
+
+extern std::atomic<uint64_t> g_kernel_launches;
+
+namespace {
+
+constexpr int kWarps = 6;
+constexpr int kThreads = kWarps * 32;
+constexpr int kAStages = 4;          // TMEM A stages (32 columns each)
+constexpr int kDCol0 = kAStages * 32;  // accumulators start here (2 x 128 columns)
+constexpr int kTmemCols = 512;
+constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at 1.9 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and flags the error) after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint32_t* err) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      atomicOr(err, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= uint64_t((addr & 0x3FFFF) >> 4);  // start address
+  d |= uint64_t(1) << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;         // stride byte offset
+  d |= uint64_t(1) << 46;                 // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A/B bf16, D f32, both K-major, M=128.
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Two bf16 (q0*s+b, q1*s+b) packed low/high, from the nibble pair (q0, q1)
+// already placed as 128+q in the low/high halves of `pair_bits`.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t pair_bits, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const __nv_bfloat162 magic = __floats2bfloat162_rn(128.f, 128.f);
+  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&pair_bits);
+  x = __hsub2(x, magic);        // exact: integers 0..15
+  x = __hfma2(x, s2, b2);       // one rounding of scale*q + bias
+  return *reinterpret_cast<uint32_t*>(&x);
+}
+
+struct Work {
+  int rt;       // global row tile of W
+  int c0, c1;   // chunk range
+  int p0, p1;   // token / sorted-position range
+  int g;        // group (expert), or split index for dense
+  int rt_local; // row tile within the group
+  bool valid;
+};
+
+__device__ __forceinline__ int n_items(const TcArgs& a) {
+  return a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
+}
+
+__device__ __forceinline__ Work item_at(const TcArgs& a, int i) {
+  Work w;
+  const int kc = a.W.k_chunks();
+  if (a.mode == kGemmStoreF32) {
+    w.rt = i % a.W.row_tiles;
+    w.g = i / a.W.row_tiles;  // split
+    w.rt_local = w.rt;
+    const int per = (kc + a.splits - 1) / a.splits;
+    w.c0 = w.g * per;
+    w.c1 = min(kc, w.c0 + per);
+    w.p0 = 0;
+    w.p1 = a.n_tokens;
+  } else {
+    w.g = i / a.expert_tiles;
+    w.rt_local = i % a.expert_tiles;
+    w.rt = w.g * a.expert_tiles + w.rt_local;
+    w.c0 = 0;
+    w.c1 = kc;
+    w.p0 = a.group_off[w.g];
+    w.p1 = a.group_off[w.g + 1];
+  }
+  w.valid = w.p1 > w.p0 && w.c1 > w.c0;
+  return w;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // carve: [B ring (1024-aligned)] [W ring] [exchange] [barriers]
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  const int box = a.box_rows;
+  const uint32_t b_bytes = uint32_t(box) * 128;
+  uint8_t* ring_b = base;
+  uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
+  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [64][box+1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * (box + 1));
+  uint64_t* full = bars;                 // [S]
+  uint64_t* empty = full + S;            // [S]
+  uint64_t* a_full = empty + S;          // [kAStages]
+  uint64_t* a_empty = a_full + kAStages; // [kAStages]
+  uint64_t* acc_full = a_empty + kAStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;       // [2]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < kAStages; ++s) { mbar_init(&a_full[s], 4); mbar_init(&a_empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int total = n_items(a);
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
+        const Work w = item_at(a, i);
+        if (!w.valid) continue;
+        for (int tb = w.p0; tb < w.p1; tb += box) {
+          for (int c = w.c0; c < w.c1; ++c, ++it) {
+            const int s = it % S;
+            const uint32_t ph = (it / S) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
+            mbar_expect_tx(&full[s], kTileBytes + b_bytes);
+            bulk_load(ring_w + size_t(s) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[s]);
+            tma_load_2d(ring_b + size_t(s) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[s]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, acc_it = 0;
+      const uint32_t idesc = idesc_bf16(box);
+      for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
+        const Work w = item_at(a, i);
+        if (!w.valid) continue;
+        for (int tb = w.p0; tb < w.p1; tb += box, ++acc_it) {
+          const int d = acc_it & 1;
+          if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem + kDCol0 + d * 128;
+          for (int c = w.c0; c < w.c1; ++c, ++it) {
+            const int s = it % S, sa = it % kAStages;
+            if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) break;
+            if (!mbar_wait(&a_full[sa], (it / kAStages) & 1, abort_flag, a.err)) break;
+            tc_fence_after();
+            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(s) * b_bytes));
+#pragma unroll
+            for (int k = 0; k < kTileK / 16; ++k)
+              mma_ts(d_tmem, tmem + sa * 32 + k * 8, bdesc + uint64_t(k * 2), idesc, (c > w.c0 || k > 0) ? 1u : 0u);
+            mma_commit(&empty[s]);
+            mma_commit(&a_empty[sa]);
+          }
+          mma_commit(&acc_full[d]);
+        }
+      }
+    }
+  } else {
+    // ---------------- dequantise + epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;  // weight row within the tile
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    uint32_t it = 0, acc_it = 0;
+    for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i);
+      if (!w.valid) continue;
+      for (int tb = w.p0; tb < w.p1; tb += box, ++acc_it) {
+        for (int c = w.c0; c < w.c1; ++c, ++it) {
+          const int s = it % S, sa = it % kAStages;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) break;
+          const uint8_t* tile = ring_w + size_t(s) * kTileBytes;
+          const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
+          const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
+          const uint16_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
+          const uint16_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
+          const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+          __nv_bfloat162 s2, b2;
+          {
+            const uint32_t sv = uint32_t(sb) | (uint32_t(sb) << 16), bv = uint32_t(bb) | (uint32_t(bb) << 16);
+            s2 = *reinterpret_cast<const __nv_bfloat162*>(&sv);
+            b2 = *reinterpret_cast<const __nv_bfloat162*>(&bv);
+          }
+          uint32_t v[32];
+#pragma unroll
+          for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              v[wd * 4 + j] = deq_pair(((words[wd] >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
+          if (!mbar_wait(&a_empty[sa], ((it / kAStages) & 1) ^ 1, abort_flag, a.err)) break;
+          tmem_st32(tmem + lane_addr + sa * 32, v);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[sa]);
+        }
+        // epilogue for token block [tb, tb + box)
+        const int d = acc_it & 1;
+        if (!mbar_wait(&acc_full[d], (acc_it >> 1) & 1, abort_flag, a.err)) break;
+        tc_fence_after();
+        const int nvalid = min(box, w.p1 - tb);
+        const int n_glob = w.rt * kTileRows + r;
+        for (int j0 = 0; j0 < box; j0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_addr + kDCol0 + d * 128 + j0, v);
+          tmem_wait_ld();
+          if (a.mode == kGemmStoreF32) {
+            if (n_glob < a.W.rows) {
+              float* y = a.Y + size_t(w.g) * a.split_stride;
+              for (int j = 0; j < 16 && j0 + j < nvalid; ++j)
+                y[size_t(tb + j0 + j) * a.ldy + n_glob] = __uint_as_float(v[j]);
+            }
+          } else if (a.mode == kGemmDown) {
+            const int n = w.rt_local * kTileRows + r;
+            for (int j = 0; j < 16 && j0 + j < nvalid; ++j)
+              a.Y[size_t(tb + j0 + j) * a.ldy + n] = __uint_as_float(v[j]);
+          } else {
+            if (r >= 64)
+              for (int j = 0; j < 16; ++j) xchg[(r - 64) * (box + 1) + j0 + j] = __uint_as_float(v[j]);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (r < 64) {
+              const int jj = w.rt_local * 64 + r;
+              for (int j = 0; j < 16 && j0 + j < nvalid; ++j) {
+                const float gv = __uint_as_float(v[j]), uv = xchg[r * (box + 1) + j0 + j];
+                a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[d]);
+      }
+    }
+  }
+  // teardown: every warp reaches here (bounded waits); free TMEM
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+}  // namespace
+
+size_t qgemm_tc_smem(int box_rows, int stages) {
+  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) + 64 * size_t(box_rows + 1) * 4 +
+         (2 * size_t(stages) + 2 * kAStages + 4) * 8 + 16;
+}
+
+int qgemm_tc_stages(int box_rows) {
+  const size_t budget = 200 * 1024;
+  int s = 12;
+  while (s > 2 && qgemm_tc_smem(box_rows, s) > budget) --s;
+  return s;
+}
+
+void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {
+  if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
+    throw std::invalid_argument("tcgen05 GEMM box rows must be 16, 32, 64 or 128");
+  if (a.mode == kGemmStoreF32 && a.n_tokens <= 0) return;
+  a.stages = qgemm_tc_stages(a.box_rows);
+  const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
+  static bool configured = false;
+  if (!configured) {
+    QWEN_CUDA(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    configured = true;
+  }
+  const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
+  const int grid = std::max(1, std::min(items, sm_count));
+  qgemm_tc_kernel<<<grid, kThreads, smem, s>>>(bmap, a);
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// ---------------------------------------------------------------- tensor maps --
+namespace {
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    QWEN_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+}  // namespace
+
+CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k * 2) % 16)
+    throw std::invalid_argument("activation tensor map alignment");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(kTileK), cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+}  // namespace qwen

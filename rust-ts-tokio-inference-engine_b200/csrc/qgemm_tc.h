@@ -1,0 +1,35 @@
+// tcgen05 4-bit grouped GEMM: launch interface.
+#pragma once
+#include <cuda.h>
+
+#include "kernels.h"
+
+namespace qwen {
+
+struct TcArgs {
+  QMat W;
+  int mode = kGemmStoreF32;  // kGemmStoreF32 / kGemmGateUp / kGemmDown
+  int expert_tiles = 0;      // grouped: row tiles per expert
+  int groups = 1;
+  const int32_t* group_off = nullptr;  // grouped: sorted positions of expert g = [off[g], off[g+1])
+  int n_tokens = 0;                    // dense: token rows
+  int splits = 1;                      // dense: split-K slices (partials at Y + split*split_stride)
+  size_t split_stride = 0;
+  int b_row0 = 0;      // first activation row of the B tensor map
+  int box_rows = 16;   // N tile: 16, 32, 64 or 128 (the tensor map's box height)
+  int stages = 0;      // shared-memory ring depth (set by the launcher)
+  float* Y = nullptr;
+  int ldy = 0;
+  __nv_bfloat16* Yb = nullptr;
+  int ldyb = 0;
+  uint32_t* err = nullptr;
+};
+
+// Tensor map over a row-major bf16 activation matrix [rows, k] with a
+// (64 columns x box_rows) box and 128-byte swizzle (the UMMA K-major layout).
+CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows);
+void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
+size_t qgemm_tc_smem(int box_rows, int stages);
+int qgemm_tc_stages(int box_rows);
+
+}  // namespace qwen

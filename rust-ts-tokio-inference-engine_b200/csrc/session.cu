@@ -15,7 +15,11 @@
 #include <string>
 #include <vector>
 
+#include <map>
+#include <tuple>
+
 #include "kernels.h"
+#include "qgemm_tc.h"
 #include "state_table.h"
 
 using namespace qwen;
@@ -103,6 +107,7 @@ struct Version {
 };
 
 constexpr size_t kStatsCount = 17 + 19 * 3;
+constexpr int kMaxSplits = 8;
 
 struct Session {
   WeightStore* store = nullptr;
@@ -135,7 +140,48 @@ struct Session {
   DevBuf<int64_t> slot_mapping;
   DevBuf<uint32_t> tokens, sampled, err;
   DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
-  DevBuf<__nv_bfloat16> hb, hb2, act;
+  DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
+  int sm_count = 148;
+  bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
+  std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
+
+  const CUtensorMap& act_map(const void* p, int rows, int k, int box) {
+    auto key = std::make_tuple(p, rows, k, box);
+    auto it = maps.find(key);
+    if (it == maps.end()) it = maps.emplace(key, make_act_map(p, rows, k, box)).first;
+    return it->second;
+  }
+  static int box_for(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
+
+  // Dense Y[t][n] (+ split partials) = X[t] . deq(W)[n]; returns the split count.
+  int dense(const QMat& W, const __nv_bfloat16* X, int rows_cap, int T, float* Y, int ldy,
+            size_t split_stride, int max_splits, cudaStream_t s) {
+    if (simple_gemm) {
+      GemmArgs g;
+      g.W = W;
+      g.X = X;
+      g.ldx = W.k;
+      g.n_tokens = T;
+      g.Y = Y;
+      g.ldy = ldy;
+      launch_qgemm(g, s);
+      return 1;
+    }
+    TcArgs a;
+    a.W = W;
+    a.mode = kGemmStoreF32;
+    a.n_tokens = T;
+    a.box_rows = box_for(std::min(T, 128));
+    const int kc = W.k_chunks();
+    int splits = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc / 2}));
+    a.splits = splits;
+    a.split_stride = split_stride;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.err = err.p;
+    launch_qgemm_tc(act_map(X, rows_cap, W.k, a.box_rows), a, sm_count, s);
+    return splits;
+  }
   PinBuf<uint8_t> staging;
   bool capture_routing = false;
   int captured_tokens = 0;
@@ -274,7 +320,6 @@ struct Session {
     x.ensure(size_t(T) * d.H);
     const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
     proj.ensure(size_t(T) * proj_w);
-    partial.ensure(size_t(T) * d.H);
     const int hbw = std::max({d.H, d.vd, d.Hq * d.D});
     hb.ensure(size_t(T) * hbw);
     hb2.ensure(size_t(T) * hbw);
@@ -289,6 +334,12 @@ struct Session {
     act.ensure(size_t(A) * d.I);
     moe_y.ensure(size_t(A) * d.H);
     hidden_stage.ensure(size_t(T) * d.H);
+    xperm.ensure(size_t(A) * d.H);
+    hb_out.ensure(size_t(max_rows) * d.H);
+    QWEN_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device));
+    simple_gemm = std::getenv("QWEN_GEMM") && std::string(std::getenv("QWEN_GEMM")) == "simple";
+    const int max_split_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1, d.H});
+    partial.ensure(size_t(kMaxSplits) * T * max_split_w);
 
     // KV page pool: what the byte budget leaves after the DeltaNet pool,
     // capped by free device memory (keep 2 GiB of headroom).
@@ -544,45 +595,32 @@ struct Session {
     if (capture_routing) capture.ensure(size_t(d.L) * A);
     captured_tokens = T;
     const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
+    const size_t proj_stride = size_t(T) * proj_w;
     for (int li = 0; li < d.L; ++li) {
       const LayerDev& ly = m.layers[li];
       stage(ly.mixer == 0 ? 2 : 6);  // RecurrentProjection / AttentionProjection
-      GemmArgs g;
-      g.W = ly.in_proj;
-      g.mode = kGemmStoreF32;
-      g.X = hb.p;
-      g.ldx = d.H;
-      g.n_tokens = T;
-      g.Y = proj.p;
-      g.ldy = proj_w;
-      launch_qgemm(g, s);
-      GemmArgs o;
-      o.W = ly.out_proj;
-      o.mode = kGemmStoreF32;
-      o.X = hb2.p;
-      o.n_tokens = T;
-      o.Y = partial.p;
-      o.ldy = d.H;
-      o.split_stride = size_t(T) * d.H;
+      const int ps = dense(ly.in_proj, hb.p, max_tokens, T, partial.p, proj_w, proj_stride, kMaxSplits, s);
+      const int k_out = ly.mixer == 0 ? d.vd : d.Hq * d.D;
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
-        launch_gdn(d, ly, proj.p, proj_w, descs.p, cu_seqlens.p, n, gdn, ly.type_index, hb2.p, err.p, s);
-        o.ldx = d.vd;
+        launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, gdn, ly.type_index,
+                   hb2.p, err.p, s);
         stage(5);  // RecurrentOutput
       } else {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
-        launch_attn_prep(d, ly, proj.p, proj_w, token_pos.p, slot_mapping.p, T, kv, ly.type_index, q.p,
-                         gate.p, s);
+        launch_attn_prep(d, ly, partial.p, proj_w, ps, proj_stride, token_pos.p, slot_mapping.p, T, kv,
+                         ly.type_index, q.p, gate.p, s);
         launch_attention(d, q.p, gate.p, token_seq.p, token_pos.p, descs.p, block_table.p, bt_stride, kv,
                          ly.type_index, T, max_len, attn_ws.p, std::max(1, splits_needed), hb2.p, s);
-        o.ldx = d.Hq * d.D;
         stage(8);  // AttentionOutput
       }
-      launch_qgemm(o, s);
+      const size_t out_stride = size_t(T) * d.H;
+      const int os = dense(ly.out_proj, hb2.p, max_tokens, T, partial.p, d.H, out_stride, kMaxSplits, s);
+      (void)k_out;
       stage(9);  // ResidualNorm
-      launch_residual_norm(x.p, partial.p, 1, o.split_stride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0,
+      launch_residual_norm(x.p, partial.p, os, out_stride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0,
                            nullptr, s);
-      moe(ly, T, A, proj_w, s);
+      moe(ly, T, A, s);
       if (capture_routing)
         QWEN_CUDA(cudaMemcpyAsync(capture.p + size_t(li) * A, ids.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
       const float* next_norm = li + 1 < d.L ? m.layers[li + 1].in_norm : nullptr;
@@ -590,66 +628,81 @@ struct Session {
       launch_moe_combine(x.p, moe_y.p, inv.p, weights.p, T, d.H, slots_per_tok, next_norm, d.eps, hb.p,
                          nullptr, 0, nullptr, s);
     }
-    // final norm over every token (hidden rows), lm_head on the output rows
     stage(17);  // FinalProjection
-    launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb.p, nullptr, 0,
-                         keep_hidden ? hidden_stage.p : nullptr, s);
+    if (keep_hidden)  // post-norm hidden rows of every token (fp32)
+      launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb.p, nullptr, 0, hidden_stage.p, s);
+    // compact bf16 rows of the output tokens for the vocabulary projection
+    launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb_out.p, out_token.p, R, nullptr, s);
     logits.ensure(size_t(R) * d.V);
-    GemmArgs lm;
-    lm.W = m.lm_head;
-    lm.mode = kGemmStoreF32;
-    lm.X = hb.p;
-    lm.ldx = d.H;
-    lm.x_row = out_token.p;
-    lm.x_div = 1;
-    lm.n_tokens = R;
-    lm.Y = logits.p;
-    lm.ldy = d.V;
-    launch_qgemm(lm, s);
+    dense(m.lm_head, hb_out.p, max_rows, R, logits.p, d.V, size_t(R) * d.V, 1, s);
     stage(18);  // StateValidation (finite check + greedy selection)
     launch_argmax(logits.p, R, d.V, sampled.p, err.p, s);
     launches += 1;
   }
 
-  void moe(const LayerDev& ly, int T, int A, int proj_w, cudaStream_t s) {
+  void moe(const LayerDev& ly, int T, int A, cudaStream_t s) {
     stage(10);  // MoeRouting
-    GemmArgs r;
-    r.W = ly.router;
-    r.mode = kGemmStoreF32;
-    r.X = hb.p;
-    r.ldx = d.H;
-    r.n_tokens = T;
-    r.Y = proj.p;
-    r.ldy = proj_w;
-    launch_qgemm(r, s);
-    launch_route(proj.p, proj_w, T, d.E, d.top, ids.p, weights.p, s);
+    const int rw = d.E + 1;
+    const size_t rstride = size_t(T) * rw;
+    const int rs = dense(ly.router, hb.p, max_tokens, T, partial.p, rw, rstride, kMaxSplits, s);
+    launch_route(partial.p, rw, rs, rstride, T, d.E, d.top, ids.p, weights.p, s);
     launch_expert_sort(ids.p, A, d.E + 1, counts.p, offsets.p, perm.p, inv.p, s);
     stage(11);  // MoeUpGate
-    GemmArgs gu;
+    if (simple_gemm) {
+      GemmArgs gu;
+      gu.W = ly.expert_gu;
+      gu.mode = kGemmGateUp;
+      gu.expert_tiles = 2 * d.I / kTileRows;
+      gu.X = hb.p;
+      gu.ldx = d.H;
+      gu.x_row = perm.p;
+      gu.x_div = d.top + 1;
+      gu.group_off = offsets.p;
+      gu.groups = d.E + 1;
+      gu.Yb = act.p;
+      gu.ldyb = d.I;
+      launch_qgemm(gu, s);
+      stage(12);  // MoeDown
+      GemmArgs dn;
+      dn.W = ly.expert_dn;
+      dn.mode = kGemmDown;
+      dn.expert_tiles = d.H / kTileRows;
+      dn.X = act.p;
+      dn.ldx = d.I;
+      dn.group_off = offsets.p;
+      dn.groups = d.E + 1;
+      dn.Y = moe_y.p;
+      dn.ldy = d.H;
+      launch_qgemm(dn, s);
+      return;
+    }
+    launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
+    const int per_expert = (A + d.E) / (d.E + 1);
+    const int box = box_for(std::max(1, 2 * per_expert));
+    TcArgs gu;
     gu.W = ly.expert_gu;
     gu.mode = kGemmGateUp;
     gu.expert_tiles = 2 * d.I / kTileRows;
-    gu.X = hb.p;
-    gu.ldx = d.H;
-    gu.x_row = perm.p;
-    gu.x_div = d.top + 1;
-    gu.group_off = offsets.p;
     gu.groups = d.E + 1;
+    gu.group_off = offsets.p;
+    gu.box_rows = box;
     gu.Yb = act.p;
     gu.ldyb = d.I;
-    launch_qgemm(gu, s);
+    gu.err = err.p;
+    const int a_cap = max_tokens * (d.top + 1);
+    launch_qgemm_tc(act_map(xperm.p, a_cap, d.H, box), gu, sm_count, s);
     stage(12);  // MoeDown
-    GemmArgs dn;
+    TcArgs dn;
     dn.W = ly.expert_dn;
     dn.mode = kGemmDown;
     dn.expert_tiles = d.H / kTileRows;
-    dn.X = act.p;
-    dn.ldx = d.I;
-    dn.group_off = offsets.p;
     dn.groups = d.E + 1;
+    dn.group_off = offsets.p;
+    dn.box_rows = box;
     dn.Y = moe_y.p;
     dn.ldy = d.H;
-    launch_qgemm(dn, s);
+    dn.err = err.p;
+    launch_qgemm_tc(act_map(act.p, a_cap, d.I, box), dn, sm_count, s);
   }
 };
 
@@ -1000,6 +1053,55 @@ int rs_qwen_device_mtp_verify_accept(void* session, size_t, const StateId*, cons
   return checked(error, capacity, [&] {
     (void)S(session);
     throw std::runtime_error("MTP verify not available in this build");
+  });
+}
+
+int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, size_t T, float* y, size_t y_count,
+                       int engine, double* ms, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!x || !y || !T || T > size_t(s->max_tokens)) throw std::invalid_argument("debug gemm descriptor");
+    if (layer < 0 || layer >= s->d.L) throw std::invalid_argument("debug gemm layer");
+    const LayerDev& ly = s->store->model.layers[layer];
+    const QMat& W = which == 0 ? ly.in_proj : which == 1 ? ly.out_proj : which == 2 ? ly.router : s->store->model.lm_head;
+    if (which < 0 || which > 3) throw std::invalid_argument("debug gemm matrix");
+    if (y_count != T * size_t(W.rows)) throw std::invalid_argument("debug gemm output capacity");
+    s->set_device();
+    __nv_bfloat16* xin = which == 1 ? s->hb2.p : which == 3 ? s->hb_out.p : s->hb.p;
+    if (which == 3 && T > size_t(s->max_rows)) throw std::invalid_argument("debug gemm rows");
+    QWEN_CUDA(cudaMemcpyAsync(xin, x, T * W.k * 2, cudaMemcpyHostToDevice, s->stream));
+    QWEN_CUDA(cudaMemsetAsync(s->err.p, 0, 4, s->stream));
+    const bool prev = s->simple_gemm;
+    s->simple_gemm = engine == 1;
+    const size_t stride = T * size_t(W.rows);
+    float* out = which == 3 ? s->logits.p : s->partial.p;
+    if (which == 3) s->logits.ensure(stride);
+    out = which == 3 ? s->logits.p : s->partial.p;
+    QWEN_CUDA(cudaEventRecord(s->ev_begin, s->stream));
+    int splits = 1;
+    try {
+      splits = s->dense(W, xin, which == 3 ? s->max_rows : s->max_tokens, int(T), out, W.rows, stride,
+                        which == 3 ? 1 : kMaxSplits, s->stream);
+    } catch (...) {
+      s->simple_gemm = prev;
+      throw;
+    }
+    s->simple_gemm = prev;
+    QWEN_CUDA(cudaEventRecord(s->ev_end, s->stream));
+    std::vector<float> part(stride * splits);
+    uint32_t h_err = 0;
+    QWEN_CUDA(cudaMemcpyAsync(part.data(), out, part.size() * 4, cudaMemcpyDeviceToHost, s->stream));
+    QWEN_CUDA(cudaMemcpyAsync(&h_err, s->err.p, 4, cudaMemcpyDeviceToHost, s->stream));
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    float fms = 0.f;
+    QWEN_CUDA(cudaEventElapsedTime(&fms, s->ev_begin, s->ev_end));
+    if (ms) *ms = fms;
+    if (h_err) throw std::runtime_error("debug gemm device error flag " + std::to_string(h_err));
+    for (size_t i = 0; i < stride; ++i) {
+      float v = 0.f;
+      for (int sp = 0; sp < splits; ++sp) v += part[sp * stride + i];
+      y[i] = v;
+    }
   });
 }
 

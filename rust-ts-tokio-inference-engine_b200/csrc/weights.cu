@@ -80,7 +80,7 @@ __global__ void synth_qmat_kernel(uint8_t* tiles, int k_chunks, long long rows, 
   for (int i = 0; i < 64; ++i) {
     float v = s > 0.0f ? rintf(__fdiv_rn(__fsub_rn(w[i], b), s)) : 0.0f;
     v = fminf(fmaxf(v, 0.0f), 15.0f);
-    words[i / 8] |= uint32_t(v) << (4 * (i % 8));
+    words[i / 8] |= uint32_t(v) << (4 * nibble_of_col(i % 8));
   }
   int drow = device_row(mode, row, row_offset, per_expert);
   uint8_t* tile = tiles + (size_t(drow / kTileRows) * k_chunks + g) * kTileBytes;
@@ -323,7 +323,11 @@ void WeightStore::export_bytes(const std::string& full, size_t offset, uint8_t* 
       const uint8_t* t = m.tile(drow / kTileRows, int(g));
       int lr = drow % kTileRows;
       if (part == ".weight") {
-        QWEN_CUDA(cudaMemcpy(rowbuf.data() + g * 32, t + lr * 32, 32, cudaMemcpyDeviceToHost));
+        uint32_t dev[8], canon[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        QWEN_CUDA(cudaMemcpy(dev, t + lr * 32, 32, cudaMemcpyDeviceToHost));
+        for (int w = 0; w < 8; ++w)
+          for (int i = 0; i < 8; ++i) canon[w] |= ((dev[w] >> (4 * i)) & 15u) << (4 * col_of_nibble(i));
+        std::memcpy(rowbuf.data() + g * 32, canon, 32);
       } else {
         uint16_t bits;
         size_t off = kTilePackedBytes + (part == ".scales" ? 0 : kTileRows * 2) + lr * 2;
