@@ -236,6 +236,18 @@ int rs_qwen_device_synthetic_state(void* session, size_t position, uint64_t seed
 int rs_qwen_device_set_capture(void* session, int routing, char* error, size_t capacity);
 int rs_qwen_device_debug_routing(void* session, int32_t* out, size_t count, char* error,
                                  size_t capacity);
+/* NEW diagnostic: the last step's device intermediates, as raw bytes.
+ * what: 0 router logits fp32 [moe layers][T][experts+1] (last column = shared
+ * gate), 1 expert offsets int32 [moe layers][experts+2], 2 sorted->flat
+ * permutation int32 [moe layers][T*(top+1)], 3 packing int32 blob
+ * {n, T, R, n_new, SeqDesc[n] (12 ints), new pages[n_new], cu_seqlens[n+1],
+ * token_seq[T], token_pos[T], slot_mapping[T] (low 32 bits), out_token[R]},
+ * 4 block-table rows int32 [n][pages] of the step's children (rows padded to
+ * the longest). Capture must be enabled before the step (routing != 0).
+ * count is the byte capacity of out; returns the byte count written in
+ * *written. */
+int rs_qwen_device_debug_capture(void* session, int what, void* out, size_t count, size_t* written,
+                                 char* error, size_t capacity);
 
 /* NEW diagnostic: device-side timing from CUDA events on the session stream.
  * profile != 0 additionally brackets every operator stage with events

@@ -66,6 +66,7 @@ def lib():
         P, D, F, I32, U32, SZ = (C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_float),
                                  C.POINTER(C.c_int32), C.POINTER(C.c_uint32), C.c_size_t)
         L.orc_last_error.restype = C.c_char_p
+        L.orc_set_routing_slack.argtypes = [C.c_double]
         L.orc_state_count.restype = SZ
         L.orc_state_count.argtypes = [C.POINTER(RsQwenConfig)]
         L.orc_model_create.restype = P
@@ -194,6 +195,10 @@ class Model:
                                     _p(logits, C.c_double), _p(hid, C.c_double),
                                     _p(forced, C.c_int32), 0 if forced is None else forced.size))
         return logits, hid
+
+
+def set_routing_slack(slack: float):
+    lib().orc_set_routing_slack(slack)
 
 
 def argmax(logits) -> int:

@@ -41,6 +41,7 @@
 namespace {
 
 thread_local std::string g_error;
+double g_routing_slack = 2e-3;
 
 template <class F>
 int guarded(F f) {
@@ -341,7 +342,7 @@ struct Forward {
           lo = std::min(lo, lt[sel[j]]);
         }
         for (size_t e = 0; e < E; ++e)
-          if (!seen[e] && lt[e] > lo + 2e-3 * (1. + std::abs(lo)))
+          if (!seen[e] && lt[e] > lo + g_routing_slack * (1. + std::abs(lo)))
             throw std::runtime_error("forced routing is not a top-k of the oracle logits");
       } else {
         std::vector<int32_t> order(E);
@@ -519,6 +520,10 @@ void validate(const rs_qwen_config& c) {
 extern "C" {
 
 const char* orc_last_error() { return g_error.c_str(); }
+
+// Slack (relative to 1+|logit|) allowed when a forced expert selection is
+// checked against the oracle's own FP64 router logits.
+void orc_set_routing_slack(double slack) { g_routing_slack = slack; }
 
 size_t orc_state_count(const rs_qwen_config* c) { return state_count(*c); }
 

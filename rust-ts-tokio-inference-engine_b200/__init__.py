@@ -97,6 +97,7 @@ SIGNATURES = {
     "rs_qwen_device_set_profile": (C.c_int, [_P, C.c_int, _ERR, _SZ]),
     "rs_qwen_device_timing": (C.c_int, [_P, C.POINTER(C.c_double), _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_routing": (C.c_int, [_P, _I32P, _SZ, _ERR, _SZ]),
+    "rs_qwen_device_debug_capture": (C.c_int, [_P, C.c_int, C.c_void_p, _SZ, C.POINTER(_SZ), _ERR, _SZ]),
     "rs_qwen_debug_gemm": (C.c_int, [_P, C.c_int, C.c_int, C.POINTER(C.c_uint16), _SZ, _F32P, _SZ, C.c_int,
                                      C.POINTER(C.c_double), _ERR, _SZ]),
 }
@@ -323,6 +324,13 @@ class DeviceSession:
         _call("rs_qwen_debug_gemm", self.h, which, layer, x.ctypes.data_as(C.POINTER(C.c_uint16)), T,
               _ptr(y, C.c_float), y.size, engine, C.byref(ms))
         return y, ms.value
+
+    def debug_capture(self, what: int, dtype=np.int32, capacity: int = 1 << 26):
+        """Raw last-step intermediates (see rs_qwen_device_debug_capture)."""
+        buf = np.zeros(capacity // np.dtype(dtype).itemsize, dtype)
+        n = C.c_size_t()
+        _call("rs_qwen_device_debug_capture", self.h, what, buf.ctypes.data_as(C.c_void_p), buf.nbytes, C.byref(n))
+        return buf[: n.value // np.dtype(dtype).itemsize].copy()
 
     def debug_routing(self, tokens: int):
         out = np.zeros((self.cfg.layers, tokens, self.cfg.top), np.int32)

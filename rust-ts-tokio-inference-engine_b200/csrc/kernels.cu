@@ -461,7 +461,7 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
 // (native/qwen_model.inc:77-79: softmax then divide by the selected sum);
 // slot `top` is the shared expert (id E) with weight sigmoid(shared gate).
 __global__ void route_kernel(const float* __restrict__ logits, int ld, int splits, size_t split_stride,
-                             int T, int E, int top, int32_t* ids, float* weights) {
+                             int T, int E, int top, int32_t* ids, float* weights, float* logits_out) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* lr = logits + size_t(warp) * ld;
@@ -482,6 +482,13 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int split
   if (lane == 0) {
     shared_logit = lr[E];
     for (int sp = 1; sp < splits; ++sp) shared_logit += lr[sp * split_stride + E];
+  }
+  if (logits_out) {  // diagnostic capture of the summed router logits
+    float* lo = logits_out + size_t(warp) * (E + 1);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+      if (i * 32 + lane < E) lo[i * 32 + lane] = v[i];
+    if (lane == 0) lo[E] = shared_logit;
   }
   float sel_val = 0.f, top_val = 0.f, denom = 0.f;
   int32_t* out_ids = ids + size_t(warp) * (top + 1);
@@ -769,10 +776,11 @@ void launch_attention(const Dims& d, const float* q, const float* gate, const in
 int attention_max_splits(int ctx) { return (ctx + kSplitTokens - 1) / kSplitTokens; }
 
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
-                  int32_t* ids, float* weights, cudaStream_t s) {
+                  int32_t* ids, float* weights, float* logits_out, cudaStream_t s) {
   if (E > 1024) throw std::invalid_argument("more than 1024 experts");
   if (T <= 0) return;
-  route_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, splits, split_stride, T, E, top, ids, weights);
+  route_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, splits, split_stride, T, E, top, ids, weights,
+                                           logits_out);
   count_launch();
 }
 

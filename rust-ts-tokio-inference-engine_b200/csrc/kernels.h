@@ -99,7 +99,7 @@ void launch_attention(const Dims& d, const float* q, const float* gate, const in
                       int bt_stride, KvPool kv, int kv_layer, int T, int max_len, float* ws,
                       int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
-                  int32_t* ids, float* weights, cudaStream_t s);
+                  int32_t* ids, float* weights, float* logits_out, cudaStream_t s);
 void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
                         int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s);
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,

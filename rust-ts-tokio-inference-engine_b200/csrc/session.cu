@@ -142,6 +142,7 @@ struct Session {
   DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
   int sm_count = 148;
+  int cur_layer = 0;
   bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
   std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
 
@@ -185,6 +186,11 @@ struct Session {
   PinBuf<uint8_t> staging;
   bool capture_routing = false;
   int captured_tokens = 0;
+  DevBuf<float> cap_logits;
+  DevBuf<int32_t> cap_offsets, cap_perm;
+  std::vector<SeqDesc> last_descs;
+  std::vector<int32_t> last_new_pages;
+  int last_n = 0, last_T = 0, last_R = 0;
 
   // device timing (CUDA events on `stream`)
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
@@ -526,6 +532,13 @@ struct Session {
       ev_marks.clear();
       open_stage = -1;
       QWEN_CUDA(cudaEventRecord(ev_begin, stream));
+      if (capture_routing) {
+        last_descs.assign(hd, hd + n);
+        last_new_pages = npages;
+        last_n = n;
+        last_T = T;
+        last_R = R;
+      }
       forward(n, T, R, max_len, keep_hidden, logits_out != nullptr);
       stage_close();
       QWEN_CUDA(cudaEventRecord(ev_end, stream));
@@ -592,8 +605,14 @@ struct Session {
     const int slots_per_tok = d.top + 1, A = T * slots_per_tok;
     const int splits_needed = (max_len + 255) / 256;
     attn_ws.ensure(size_t(T) * d.Hq * std::max(1, splits_needed) * (d.D + 2));
-    if (capture_routing) capture.ensure(size_t(d.L) * A);
+    if (capture_routing) {
+      capture.ensure(size_t(d.L) * A);
+      cap_logits.ensure(size_t(d.L) * T * (d.E + 1));
+      cap_offsets.ensure(size_t(d.L) * (d.E + 2));
+      cap_perm.ensure(size_t(d.L) * A);
+    }
     captured_tokens = T;
+    cur_layer = 0;
     const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
     const size_t proj_stride = size_t(T) * proj_w;
     for (int li = 0; li < d.L; ++li) {
@@ -620,9 +639,14 @@ struct Session {
       stage(9);  // ResidualNorm
       launch_residual_norm(x.p, partial.p, os, out_stride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0,
                            nullptr, s);
+      cur_layer = li;
       moe(ly, T, A, s);
-      if (capture_routing)
+      if (capture_routing) {
         QWEN_CUDA(cudaMemcpyAsync(capture.p + size_t(li) * A, ids.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
+        QWEN_CUDA(cudaMemcpyAsync(cap_offsets.p + size_t(li) * (d.E + 2), offsets.p, size_t(d.E + 2) * 4,
+                                  cudaMemcpyDeviceToDevice, s));
+        QWEN_CUDA(cudaMemcpyAsync(cap_perm.p + size_t(li) * A, perm.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
+      }
       const float* next_norm = li + 1 < d.L ? m.layers[li + 1].in_norm : nullptr;
       stage(13);  // MoeMixture (+ shared merge, residual, next input norm)
       launch_moe_combine(x.p, moe_y.p, inv.p, weights.p, T, d.H, slots_per_tok, next_norm, d.eps, hb.p,
@@ -645,7 +669,8 @@ struct Session {
     const int rw = d.E + 1;
     const size_t rstride = size_t(T) * rw;
     const int rs = dense(ly.router, hb.p, max_tokens, T, partial.p, rw, rstride, kMaxSplits, s);
-    launch_route(partial.p, rw, rs, rstride, T, d.E, d.top, ids.p, weights.p, s);
+    launch_route(partial.p, rw, rs, rstride, T, d.E, d.top, ids.p, weights.p,
+                 capture_routing ? cap_logits.p + size_t(cur_layer) * T * (d.E + 1) : nullptr, s);
     launch_expert_sort(ids.p, A, d.E + 1, counts.p, offsets.p, perm.p, inv.p, s);
     stage(11);  // MoeUpGate
     if (simple_gemm) {
@@ -1018,6 +1043,68 @@ int rs_qwen_device_debug_routing(void* session, int32_t* out, size_t count, char
     for (int l = 0; l < s->d.L; ++l)
       for (int t = 0; t < T; ++t)
         for (int j = 0; j < K; ++j) out[(size_t(l) * T + t) * K + j] = all[size_t(l) * A + t * (K + 1) + j];
+  });
+}
+
+int rs_qwen_device_debug_capture(void* session, int what, void* out, size_t count, size_t* written, char* error,
+                                 size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!s->capture_routing || !out || !written) throw std::invalid_argument("capture disabled or no output");
+    s->set_device();
+    QWEN_CUDA(cudaStreamSynchronize(s->stream));
+    const int T = s->captured_tokens, A = T * (s->d.top + 1), L = s->d.L, E = s->d.E;
+    auto copy = [&](const void* src, size_t bytes) {
+      if (bytes > count) throw std::invalid_argument("capture capacity");
+      QWEN_CUDA(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost));
+      *written = bytes;
+    };
+    if (what == 0) return copy(s->cap_logits.p, size_t(L) * T * (E + 1) * 4);
+    if (what == 1) return copy(s->cap_offsets.p, size_t(L) * (E + 2) * 4);
+    if (what == 2) return copy(s->cap_perm.p, size_t(L) * A * 4);
+    if (what == 3) {
+      const int n = s->last_n, TT = s->last_T, R = s->last_R, nn = int(s->last_new_pages.size());
+      std::vector<int32_t> blob;
+      blob.insert(blob.end(), {n, TT, R, nn});
+      for (const auto& sd : s->last_descs) {
+        const int32_t* f = reinterpret_cast<const int32_t*>(&sd);
+        blob.insert(blob.end(), f, f + sizeof(SeqDesc) / 4);
+      }
+      blob.insert(blob.end(), s->last_new_pages.begin(), s->last_new_pages.end());
+      std::vector<int32_t> tmp(std::max(n + 1, TT));
+      auto pull = [&](const int32_t* src, int cnt) {
+        QWEN_CUDA(cudaMemcpy(tmp.data(), src, size_t(cnt) * 4, cudaMemcpyDeviceToHost));
+        blob.insert(blob.end(), tmp.begin(), tmp.begin() + cnt);
+      };
+      pull(s->cu_seqlens.p, n + 1);
+      pull(s->token_seq.p, TT);
+      pull(s->token_pos.p, TT);
+      std::vector<int64_t> sm(TT);
+      QWEN_CUDA(cudaMemcpy(sm.data(), s->slot_mapping.p, size_t(TT) * 8, cudaMemcpyDeviceToHost));
+      for (auto v : sm) blob.push_back(int32_t(v));
+      pull(s->out_token.p, R);
+      if (blob.size() * 4 > count) throw std::invalid_argument("capture capacity");
+      std::memcpy(out, blob.data(), blob.size() * 4);
+      *written = blob.size() * 4;
+      return;
+    }
+    if (what == 4) {
+      int maxp = 0;
+      for (const auto& sd : s->last_descs) maxp = std::max(maxp, sd.n_shared + sd.n_new);
+      std::vector<int32_t> rows(size_t(s->last_n) * maxp, -1);
+      for (int i = 0; i < s->last_n; ++i) {
+        const auto& sd = s->last_descs[i];
+        const int np = sd.n_shared + sd.n_new;
+        if (np)
+          QWEN_CUDA(cudaMemcpy(rows.data() + size_t(i) * maxp, s->block_table.p + size_t(sd.child) * s->bt_stride,
+                               size_t(np) * 4, cudaMemcpyDeviceToHost));
+      }
+      if (rows.size() * 4 > count) throw std::invalid_argument("capture capacity");
+      std::memcpy(out, rows.data(), rows.size() * 4);
+      *written = rows.size() * 4;
+      return;
+    }
+    throw std::invalid_argument("unknown capture selector");
   });
 }
 
