@@ -122,30 +122,50 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
 // Row r: t = out_token ? out_token[r] : r. x[t] += sum of split partials
 // (only when partial != null); then hb[r] = bf16(rms(x[t]) * w) and optionally
 // hidden[r] = fp32 normalized row.
-__global__ void residual_norm_kernel(float* x, const float* __restrict__ partial, int splits,
+__global__ void residual_norm_kernel(float* __restrict__ x, const float* __restrict__ partial, int splits,
                                      size_t split_stride, int H, const float* __restrict__ norm_w,
-                                     float eps, __nv_bfloat16* hb, const int32_t* __restrict__ out_token,
-                                     float* hidden) {
+                                     float eps, __nv_bfloat16* __restrict__ hb,
+                                     const int32_t* __restrict__ out_token, float* __restrict__ hidden) {
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int t = out_token ? out_token[r] : r;
   float* xr = x + size_t(t) * H;
+  constexpr int kMaxPer = 8;  // columns per thread (H <= 8 * blockDim)
+  float v[kMaxPer];
   float ss = 0.f;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float v = xr[c];
-    if (partial) {
-      for (int s = 0; s < splits; ++s) v += partial[s * split_stride + size_t(t) * H + c];
-      xr[c] = v;
-    }
-    ss += v * v;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    v[k] = c < H ? xr[c] : 0.f;
   }
+  if (partial) {
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* ps = partial + sp * split_stride + size_t(t) * H;
+#pragma unroll
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int c = threadIdx.x + k * blockDim.x;
+        if (c < H) v[k] += ps[c];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxPer; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < H) xr[c] = v[k];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) ss += v[k] * v[k];
   const float tot = block_sum(ss, red);
   if (!norm_w) return;
   const float inv = rsqrtf(tot / H + eps);
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    const float y = xr[c] * inv * norm_w[c];
-    hb[size_t(r) * H + c] = __float2bfloat16_rn(y);
-    if (hidden) hidden[size_t(r) * H + c] = y;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < H) {
+      const float y = v[k] * inv * norm_w[c];
+      hb[size_t(r) * H + c] = __float2bfloat16_rn(y);
+      if (hidden) hidden[size_t(r) * H + c] = y;
+    }
   }
 }
 
@@ -375,67 +395,6 @@ __global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int spl
   }
 }
 
-// Split-KV paged attention: CTA (split, kv head, token); warp w serves q head
-// kvh*G + w with an online softmax over keys [split*SPL, min(len, ...)).
-template <int DPL>  // head_dim / 32
-__global__ void attention_kernel(const float* __restrict__ q, const int32_t* __restrict__ token_seq,
-                                 const int32_t* __restrict__ token_pos, const SeqDesc* __restrict__ descs,
-                                 const int32_t* __restrict__ block_table, int stride, KvPool kv,
-                                 int layer, int Hq, int spl, int max_splits, float* ws) {
-  constexpr int D = DPL * 32;
-  const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = blockDim.x >> 5;
-  const int h = g * G + warp;
-  const int len = token_pos[t] + 1;
-  const int k0 = split * spl;
-  if (k0 >= len) return;
-  const int k1 = min(len, k0 + spl);
-  const int32_t* row = block_table + size_t(descs[token_seq[t]].child) * stride;
-  const float scale = rsqrtf(float(D));
-  float qv[DPL], acc[DPL];
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) {
-    qv[i] = q[(size_t(t) * Hq + h) * D + lane * DPL + i] * scale;
-    acc[i] = 0.f;
-  }
-  float m = -FLT_MAX, l = 0.f;
-  const int Hkv = kv.Hkv;
-  for (int j = k0; j < k1; ++j) {
-    const __nv_bfloat16* pg = kv.page(layer, row[j / kPageTokens]);
-    const __nv_bfloat16* kr = pg + (size_t(g) * kPageTokens + j % kPageTokens) * D + lane * DPL;
-    const __nv_bfloat16* vr = pg + (size_t(Hkv + g) * kPageTokens + j % kPageTokens) * D + lane * DPL;
-    float kf[DPL], vf[DPL];
-    if constexpr (DPL == 8) {
-      const uint4 ku = *reinterpret_cast<const uint4*>(kr), vu = *reinterpret_cast<const uint4*>(vr);
-      const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&ku);
-      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vu);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = __bfloat1622float2(k2[i]), b = __bfloat1622float2(v2[i]);
-        kf[2 * i] = a.x; kf[2 * i + 1] = a.y; vf[2 * i] = b.x; vf[2 * i + 1] = b.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) { kf[i] = __bfloat162float(kr[i]); vf[i] = __bfloat162float(vr[i]); }
-    }
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) s += qv[i] * kf[i];
-    s = warp_sum(s);
-    const float mn = fmaxf(m, s);
-    const float corr = __expf(m - mn), p = __expf(s - mn);
-    l = l * corr + p;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = acc[i] * corr + p * vf[i];
-    m = mn;
-  }
-  float* o = ws + ((size_t(t) * Hq + h) * max_splits + split) * (D + 2);
-  if (lane == 0) { o[0] = m; o[1] = l; }
-#pragma unroll
-  for (int i = 0; i < DPL; ++i) o[2 + lane * DPL + i] = acc[i];
-}
-
 // Merge split partials, apply the output gate sigmoid(gate), write bf16.
 __global__ void attention_merge_kernel(const float* __restrict__ ws, const float* __restrict__ gate,
                                        const int32_t* __restrict__ token_pos, int Hq, int D, int spl,
@@ -469,14 +428,12 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int split
   float v[MAXV];
   uint32_t taken = 0;
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int e = i * 32 + lane;
-    float x = 0.f;
-    if (e < E) {
-      x = lr[e];
-      for (int sp = 1; sp < splits; ++sp) x += lr[sp * split_stride + e];
-    }
-    v[i] = x;
+  for (int i = 0; i < MAXV; ++i) v[i] = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {  // split-K partials: independent loads per slice
+    const float* ls = lr + sp * split_stride;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i)
+      if (i * 32 + lane < E) v[i] += ls[i * 32 + lane];
   }
   float shared_logit = 0.f;
   if (lane == 0) {
@@ -530,61 +487,127 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int split
   }
 }
 
-// Stable counting sort of assignments by expert id (single CTA): counts,
-// exclusive offsets [E+1 .. +1], perm (sorted -> flat), inv (flat -> sorted).
-// Stability: every thread owns experts e = tid (mod blockDim) and scans the
-// flat assignment list in order.
-__global__ void expert_sort_kernel(const int32_t* __restrict__ ids, int n, int n_experts,
-                                   int32_t* counts, int32_t* offsets, int32_t* perm, int32_t* inv) {
+// Stable counting sort of assignments by expert id (single CTA, 1024 threads):
+// counts, exclusive offsets [n_experts + 1], perm (sorted -> flat) and inv
+// (flat -> sorted). Ranks are stable by flat index: assignments are taken in
+// rounds of 1024 in index order; inside a round a warp ranks equal keys with
+// match_any, and a per-(warp, key) count table scanned over warps orders the
+// warps.
+__global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __restrict__ ids, int n,
+                                                           int n_experts, int32_t* counts, int32_t* offsets,
+                                                           int32_t* perm, int32_t* inv) {
   extern __shared__ int32_t smi[];
-  int32_t* sid = smi;             // [n]
-  int32_t* cnt = smi + n;         // [n_experts]
-  int32_t* off = cnt + n_experts; // [n_experts + 1]
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sid[i] = ids[i];
+  int32_t* cnt = smi;                 // [n_experts]
+  int32_t* cursor = cnt + n_experts;  // [n_experts]
+  int32_t* tot = cursor + n_experts;  // [n_experts]
+  uint16_t* table = reinterpret_cast<uint16_t*>(tot + n_experts);  // [32][n_experts]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[sid[i]], 1);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[ids[i]], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int e = 0; e < n_experts; ++e) { off[e] = acc; acc += cnt[e]; }
-    off[n_experts] = acc;
+  if (warp == 0) {  // exclusive scan over experts (one warp, chunks of 32)
+    int carry = 0;
+    for (int base = 0; base < n_experts; base += 32) {
+      const int e = base + lane;
+      const int c = e < n_experts ? cnt[e] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (e < n_experts) cursor[e] = carry + incl - c;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) offsets[n_experts] = carry;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e <= n_experts; e += blockDim.x) {
-    offsets[e] = off[e];
-    if (e < n_experts) counts[e] = cnt[e];
-  }
   for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
-    if (!cnt[e]) continue;
-    int cur = off[e];
-    for (int i = 0; i < n; ++i)
-      if (sid[i] == e) { perm[cur] = i; inv[i] = cur; ++cur; }
+    offsets[e] = cursor[e];
+    counts[e] = cnt[e];
+  }
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int base = 0; base < n; base += blockDim.x) {
+    for (int k = threadIdx.x; k < 32 * n_experts; k += blockDim.x) table[k] = 0;
+    __syncthreads();
+    const int i = base + threadIdx.x;
+    const int key = i < n ? ids[i] : -1;
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & lt);
+    if (key >= 0 && rank == 0) table[warp * n_experts + key] = uint16_t(__popc(peers));
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+      int acc = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = table[w * n_experts + e];
+        table[w * n_experts + e] = uint16_t(acc);
+        acc += c;
+      }
+      tot[e] = acc;
+    }
+    __syncthreads();
+    if (key >= 0) {
+      const int pos = cursor[key] + table[warp * n_experts + key] + rank;
+      perm[pos] = i;
+      inv[i] = pos;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cursor[e] += tot[e];
+    __syncthreads();
   }
 }
 
 // x[t] += sum_j w[t][j] * y[inv[t*slots+j]] (fixed slot order, deterministic);
 // then optional hb[t] = bf16(rms(x[t]) * norm_w).
-__global__ void moe_combine_kernel(float* x, const float* __restrict__ y, const int32_t* __restrict__ inv,
-                                   const float* __restrict__ weights, int H, int slots,
-                                   const float* __restrict__ norm_w, float eps, __nv_bfloat16* hb) {
+__global__ void moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
+                                   const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
+                                   int slots, const float* __restrict__ norm_w, float eps,
+                                   __nv_bfloat16* __restrict__ hb) {
   __shared__ float red[32];
+  __shared__ float sw[64];
+  __shared__ int32_t srow[64];
   const int t = blockIdx.x;
+  if (threadIdx.x < slots) {
+    sw[threadIdx.x] = weights[size_t(t) * slots + threadIdx.x];
+    srow[threadIdx.x] = inv[size_t(t) * slots + threadIdx.x];
+  }
+  __syncthreads();
   float* xr = x + size_t(t) * H;
+  constexpr int kMaxPer = 8;
+  float v[kMaxPer];
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    v[k] = 0.f;
+  }
+  for (int j = 0; j < slots; ++j) {  // fixed slot order: deterministic sum
+    const float wj = sw[j];
+    const float* yr = y + size_t(srow[j]) * H;
+#pragma unroll
+    for (int k = 0; k < kMaxPer; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < H) v[k] += wj * yr[c];
+    }
+  }
   float ss = 0.f;
-  for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    float v = 0.f;
-    for (int j = 0; j < slots; ++j)
-      v += weights[size_t(t) * slots + j] * y[size_t(inv[size_t(t) * slots + j]) * H + c];
-    const float nx = xr[c] + v;
-    xr[c] = nx;
-    ss += nx * nx;
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < H) {
+      v[k] += xr[c];
+      xr[c] = v[k];
+      ss += v[k] * v[k];
+    }
   }
   const float tot = block_sum(ss, red);
   if (!norm_w) return;
   const float inv_r = rsqrtf(tot / H + eps);
-  for (int c = threadIdx.x; c < H; c += blockDim.x)
-    hb[size_t(t) * H + c] = __float2bfloat16_rn(xr[c] * inv_r * norm_w[c]);
+#pragma unroll
+  for (int k = 0; k < kMaxPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < H) hb[size_t(t) * H + c] = __float2bfloat16_rn(v[k] * inv_r * norm_w[c]);
+  }
 }
 
 // X_perm[p] = X[perm[p] / slots]: expert-sorted copy of the MoE input rows
@@ -705,7 +728,8 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
                           const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   const int n = out_token ? rows : T;
   if (n <= 0) return;
-  residual_norm_kernel<<<n, 256, 0, s>>>(x, partial, splits, split_stride, H, norm_w, eps, hb,
+  if (H > 8 * 1024) throw std::invalid_argument("hidden width above 8192");
+  residual_norm_kernel<<<n, std::min(1024, std::max(32, (H + 7) / 8 / 32 * 32)), 0, s>>>(x, partial, splits, split_stride, H, norm_w, eps, hb,
                                          out_token, hidden_f32);
   count_launch();
 }
@@ -746,34 +770,15 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
 
 static constexpr int kSplitTokens = 256;
 
-void launch_attention(const Dims& d, const float* q, const float* gate, const int32_t* token_seq,
-                      const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table,
-                      int bt_stride, KvPool kv, int kv_layer, int T, int max_len, float* ws,
-                      int max_splits, __nv_bfloat16* out, cudaStream_t s) {
+int attention_max_splits(int ctx) { return (ctx + kSplitTokens - 1) / kSplitTokens; }
+
+void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
+                            int max_splits, __nv_bfloat16* out, cudaStream_t s) {
   if (T <= 0) return;
-  const int G = d.Hq / d.Hkv;
-  if (G > 32) throw std::invalid_argument("more than 32 query heads per KV head");
-  const int splits = (max_len + kSplitTokens - 1) / kSplitTokens;
-  if (splits > max_splits) throw std::invalid_argument("attention split workspace too small");
-  dim3 grid(splits, d.Hkv, T);
-  if (d.D == 256)
-    attention_kernel<8><<<grid, 32 * G, 0, s>>>(q, token_seq, token_pos, descs, block_table, bt_stride,
-                                                kv, kv_layer, d.Hq, kSplitTokens, max_splits, ws);
-  else if (d.D == 128)
-    attention_kernel<4><<<grid, 32 * G, 0, s>>>(q, token_seq, token_pos, descs, block_table, bt_stride,
-                                                kv, kv_layer, d.Hq, kSplitTokens, max_splits, ws);
-  else if (d.D == 64)
-    attention_kernel<2><<<grid, 32 * G, 0, s>>>(q, token_seq, token_pos, descs, block_table, bt_stride,
-                                                kv, kv_layer, d.Hq, kSplitTokens, max_splits, ws);
-  else
-    throw std::invalid_argument("head_dim must be 64, 128 or 256");
-  count_launch();
-  attention_merge_kernel<<<dim3(T, d.Hq), 128, 0, s>>>(ws, gate, token_pos, d.Hq, d.D, kSplitTokens,
-                                                       max_splits, out);
+  attention_merge_kernel<<<dim3(T, d.Hq), 128, 0, s>>>(ws, gate, token_pos, d.Hq, d.D, kSplitTokens, max_splits,
+                                                       out);
   count_launch();
 }
-
-int attention_max_splits(int ctx) { return (ctx + kSplitTokens - 1) / kSplitTokens; }
 
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
                   int32_t* ids, float* weights, float* logits_out, cudaStream_t s) {
@@ -786,7 +791,7 @@ void launch_route(const float* logits, int ld, int splits, size_t split_stride, 
 
 void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
                         int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s) {
-  const size_t smem = size_t(n_assign + 2 * n_experts + 1) * sizeof(int32_t);
+  const size_t smem = size_t(3 * n_experts) * 4 + size_t(32) * n_experts * 2;
   if (smem > 200 * 1024) throw std::invalid_argument("expert sort exceeds shared memory");
   static bool configured = false;
   if (!configured) {
@@ -803,7 +808,9 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
                         const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
-  moe_combine_kernel<<<T, 256, 0, s>>>(x, y_sorted, inv, weights, H, slots, norm_w, eps, hb);
+  if (slots > 64 || H > 8 * 1024) throw std::invalid_argument("combine geometry");
+  moe_combine_kernel<<<T, std::min(1024, std::max(64, (H + 7) / 8 / 32 * 32)), 0, s>>>(x, y_sorted, inv, weights,
+                                                                                    H, slots, norm_w, eps, hb);
   count_launch();
 }
 

@@ -94,10 +94,6 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);
-void launch_attention(const Dims& d, const float* q, const float* gate, const int32_t* token_seq,
-                      const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table,
-                      int bt_stride, KvPool kv, int kv_layer, int T, int max_len, float* ws,
-                      int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
                   int32_t* ids, float* weights, float* logits_out, cudaStream_t s);
 void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,

@@ -10,7 +10,9 @@
 //           an S-stage shared-memory ring (mbarrier complete_tx);
 //   warp 1  MMA issuer: allocates TMEM, issues tcgen05.mma (A from TMEM, B from
 //           shared memory) and tcgen05.commit to release stages;
-//   warps 2-5 dequantise: each thread owns one weight row, turns its 64 nibbles
+//   warps 2-9 dequantise (two warpgroups taking alternate chunks, so the
+//           per-chunk latency chain of one group overlaps the other's): each
+//           thread owns one weight row, turns its 64 nibbles
 //           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
 //           them into TMEM with tcgen05.st (the A operand); they also run the
 //           epilogue (tcgen05.ld of the fp32 accumulator, split-K partial
@@ -30,10 +32,12 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
-constexpr int kWarps = 6;
+constexpr int kDequantGroups = 2;    // dequant warpgroups, alternating chunks
+constexpr int kWarps = 2 + 4 * kDequantGroups;
 constexpr int kThreads = kWarps * 32;
-constexpr int kAStages = 4;          // TMEM A stages (32 columns each)
-constexpr int kDCol0 = kAStages * 32;  // accumulators start here (2 x 128 columns)
+constexpr int kAStages = 4;          // TMEM A stages per warpgroup (32 columns each)
+constexpr int kDCol0 = kDequantGroups * kAStages * 32;  // accumulators (2 x 128 columns)
+constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
 constexpr int kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at 1.9 GHz
 
@@ -136,6 +140,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -171,7 +181,7 @@ __device__ __forceinline__ int n_items(const TcArgs& a) {
   return a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
 }
 
-__device__ __forceinline__ Work item_at(const TcArgs& a, int i) {
+__device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* goff) {
   Work w;
   const int kc = a.W.k_chunks();
   if (a.mode == kGemmStoreF32) {
@@ -189,8 +199,8 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i) {
     w.rt = w.g * a.expert_tiles + w.rt_local;
     w.c0 = 0;
     w.c1 = kc;
-    w.p0 = a.group_off[w.g];
-    w.p1 = a.group_off[w.g + 1];
+    w.p0 = goff[w.g];
+    w.p1 = goff[w.g + 1];
   }
   w.valid = w.p1 > w.p0 && w.c1 > w.c0;
   return w;
@@ -206,22 +216,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_bytes = uint32_t(box) * 128;
   uint8_t* ring_b = base;
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
-  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [64][box+1]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * (box + 1));
+  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [groups][64][box+1]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + kDequantGroups * 64 * (box + 1));
+  constexpr int NA = kDequantGroups * kAStages;
   uint64_t* full = bars;                 // [S]
   uint64_t* empty = full + S;            // [S]
-  uint64_t* a_full = empty + S;          // [kAStages]
-  uint64_t* a_empty = a_full + kAStages; // [kAStages]
-  uint64_t* acc_full = a_empty + kAStages;  // [2]
-  uint64_t* acc_empty = acc_full + 2;       // [2]
+  uint64_t* a_full = empty + S;          // [NA]
+  uint64_t* a_empty = a_full + NA;       // [NA]
+  uint64_t* acc_full = a_empty + NA;     // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
+  int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < kAStages; ++s) { mbar_init(&a_full[s], 4); mbar_init(&a_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
+    for (int s = 0; s < NA; ++s) { mbar_init(&a_full[s], 4); mbar_init(&a_empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4 * kDequantGroups); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -230,6 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  if (a.mode != kGemmStoreF32)
+    for (int g = threadIdx.x; g <= a.groups; g += blockDim.x) goff[g] = a.group_off[g];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -241,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
-        const Work w = item_at(a, i);
+        const Work w = item_at(a, i, goff);
         if (!w.valid) continue;
         for (int tb = w.p0; tb < w.p1; tb += box) {
           for (int c = w.c0; c < w.c1; ++c, ++it) {
@@ -261,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0, acc_it = 0;
       const uint32_t idesc = idesc_bf16(box);
       for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
-        const Work w = item_at(a, i);
+        const Work w = item_at(a, i, goff);
         if (!w.valid) continue;
         for (int tb = w.p0; tb < w.p1; tb += box, ++acc_it) {
           const int d = acc_it & 1;
@@ -269,9 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem + kDCol0 + d * 128;
           for (int c = w.c0; c < w.c1; ++c, ++it) {
-            const int s = it % S, sa = it % kAStages;
+            const int s = it % S;
+            const int wg = it % kDequantGroups, k_in = it / kDequantGroups;
+            const int sa = wg * kAStages + k_in % kAStages;
             if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) break;
-            if (!mbar_wait(&a_full[sa], (it / kAStages) & 1, abort_flag, a.err)) break;
+            if (!mbar_wait(&a_full[sa], (k_in / kAStages) & 1, abort_flag, a.err)) break;
             tc_fence_after();
             const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(s) * b_bytes));
 #pragma unroll
@@ -285,75 +301,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- dequantise + epilogue (warps 2..5) ----------------
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int r = quad * 32 + lane;  // weight row within the tile
+    // ---------------- dequantise + epilogue (warps 2..9) ----------------
+    const int wg = (warp - 2) >> 2;        // dequant warpgroup
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    const int half = box / kDequantGroups;  // epilogue columns per warpgroup
     uint32_t it = 0, acc_it = 0;
-    for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i);
+    bool ok = true;
+    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
-      for (int tb = w.p0; tb < w.p1; tb += box, ++acc_it) {
+      for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
         for (int c = w.c0; c < w.c1; ++c, ++it) {
-          const int s = it % S, sa = it % kAStages;
-          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) break;
+          if (int(it % kDequantGroups) != wg) continue;
+          const int s = it % S;
+          const int k_in = it / kDequantGroups;
+          const int sa = wg * kAStages + k_in % kAStages;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) { ok = false; break; }
           const uint8_t* tile = ring_w + size_t(s) * kTileBytes;
           const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
           const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
-          const uint16_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
-          const uint16_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
-          const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+          const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
+          const uint32_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
           __nv_bfloat162 s2, b2;
           {
-            const uint32_t sv = uint32_t(sb) | (uint32_t(sb) << 16), bv = uint32_t(bb) | (uint32_t(bb) << 16);
+            const uint32_t sv = sb | (sb << 16), bv = bb | (bb << 16);
             s2 = *reinterpret_cast<const __nv_bfloat162*>(&sv);
             b2 = *reinterpret_cast<const __nv_bfloat162*>(&bv);
           }
           uint32_t v[32];
-#pragma unroll
-          for (int wd = 0; wd < 8; ++wd)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              v[wd * 4 + j] = deq_pair(((words[wd] >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
-          if (!mbar_wait(&a_empty[sa], ((it / kAStages) & 1) ^ 1, abort_flag, a.err)) break;
+#define QWEN_DEQ_WORD(WD, W)                                                            \
+  _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
+      deq_pair((((W) >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
+          QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
+          QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
+#undef QWEN_DEQ_WORD
+          if (!mbar_wait(&a_empty[sa], ((k_in / kAStages) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
           tmem_st32(tmem + lane_addr + sa * 32, v);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[sa]);
         }
-        // epilogue for token block [tb, tb + box)
+        if (!ok) break;
+        // epilogue for token block [tb, tb + box): this warpgroup owns columns
+        // [wg*half, (wg+1)*half)
         const int d = acc_it & 1;
-        if (!mbar_wait(&acc_full[d], (acc_it >> 1) & 1, abort_flag, a.err)) break;
+        if (!mbar_wait(&acc_full[d], (acc_it >> 1) & 1, abort_flag, a.err)) { ok = false; break; }
         tc_fence_after();
         const int nvalid = min(box, w.p1 - tb);
         const int n_glob = w.rt * kTileRows + r;
-        for (int j0 = 0; j0 < box; j0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(tmem + lane_addr + kDCol0 + d * 128 + j0, v);
+        for (int j0 = wg * half; j0 < (wg + 1) * half; j0 += 8) {
+          uint32_t v[8];
+          tmem_ld8(tmem + lane_addr + kDCol0 + d * 128 + j0, v);
           tmem_wait_ld();
           if (a.mode == kGemmStoreF32) {
             if (n_glob < a.W.rows) {
               float* y = a.Y + size_t(w.g) * a.split_stride;
-              for (int j = 0; j < 16 && j0 + j < nvalid; ++j)
-                y[size_t(tb + j0 + j) * a.ldy + n_glob] = __uint_as_float(v[j]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (j0 + j < nvalid) y[size_t(tb + j0 + j) * a.ldy + n_glob] = __uint_as_float(v[j]);
             }
           } else if (a.mode == kGemmDown) {
             const int n = w.rt_local * kTileRows + r;
-            for (int j = 0; j < 16 && j0 + j < nvalid; ++j)
-              a.Y[size_t(tb + j0 + j) * a.ldy + n] = __uint_as_float(v[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (j0 + j < nvalid) a.Y[size_t(tb + j0 + j) * a.ldy + n] = __uint_as_float(v[j]);
           } else {
-            if (r >= 64)
-              for (int j = 0; j < 16; ++j) xchg[(r - 64) * (box + 1) + j0 + j] = __uint_as_float(v[j]);
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            float* xg = xchg + wg * 64 * (box + 1);
+            if (r >= 64) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) xg[(r - 64) * (box + 1) + j0 + j] = __uint_as_float(v[j]);
+            }
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
             if (r < 64) {
               const int jj = w.rt_local * 64 + r;
-              for (int j = 0; j < 16 && j0 + j < nvalid; ++j) {
-                const float gv = __uint_as_float(v[j]), uv = xchg[r * (box + 1) + j0 + j];
-                a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
-              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (j0 + j < nvalid) {
+                  const float gv = __uint_as_float(v[j]), uv = xg[r * (box + 1) + j0 + j];
+                  a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
+                }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
           }
         }
         tc_fence_before();
@@ -374,8 +405,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 size_t qgemm_tc_smem(int box_rows, int stages) {
-  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) + 64 * size_t(box_rows + 1) * 4 +
-         (2 * size_t(stages) + 2 * kAStages + 4) * 8 + 16;
+  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) +
+         kDequantGroups * 64 * size_t(box_rows + 1) * 4 +
+         (2 * size_t(stages) + 2 * kDequantGroups * kAStages + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
 }
 
 int qgemm_tc_stages(int box_rows) {
@@ -389,6 +421,7 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
     throw std::invalid_argument("tcgen05 GEMM box rows must be 16, 32, 64 or 128");
   if (a.mode == kGemmStoreF32 && a.n_tokens <= 0) return;
+  if (a.mode != kGemmStoreF32 && a.groups > kMaxGroups) throw std::invalid_argument("too many GEMM groups");
   a.stages = qgemm_tc_stages(a.box_rows);
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
   static bool configured = false;
@@ -432,6 +465,21 @@ CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows) {
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+CUtensorMap make_kv_map(const KvPool& kv, int layer) {
+  CUtensorMap m;
+  const void* base = kv.page(layer, 0);
+  const cuuint64_t rows = cuuint64_t(kv.n_pages) * 2 * kv.Hkv * kPageTokens;
+  const cuuint64_t dims[2] = {cuuint64_t(kv.D), rows};
+  const cuuint64_t strides[1] = {cuuint64_t(kv.D) * 2};
+  const cuuint32_t box[2] = {64, cuuint32_t(kPageTokens)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (KV) failed: " + std::to_string(int(r)));
   return m;
 }
 

@@ -28,6 +28,14 @@ struct TcArgs {
 // Tensor map over a row-major bf16 activation matrix [rows, k] with a
 // (64 columns x box_rows) box and 128-byte swizzle (the UMMA K-major layout).
 CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows);
+// Tensor map over one attention layer's KV page pool: rows
+// ((page*2 + k_or_v)*Hkv + head)*16 + token, D columns, 16x64 128B-swizzled box.
+CUtensorMap make_kv_map(const KvPool& kv, int layer);
+void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_seq,
+                        const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
+                        int T, int max_len, float* ws, int max_splits, uint32_t* err, cudaStream_t s);
+void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
+                            int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
 size_t qgemm_tc_smem(int box_rows, int stages);
 int qgemm_tc_stages(int box_rows);

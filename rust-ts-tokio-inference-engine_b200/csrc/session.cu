@@ -145,6 +145,7 @@ struct Session {
   int cur_layer = 0;
   bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
   std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
+  std::vector<CUtensorMap> kv_maps;  // one per attention layer
 
   const CUtensorMap& act_map(const void* p, int rows, int k, int box) {
     auto key = std::make_tuple(p, rows, k, box);
@@ -368,6 +369,7 @@ struct Session {
     kv.layers = d.n_attn;
     kv.Hkv = d.Hkv;
     kv.D = d.D;
+    for (int l = 0; l < d.n_attn && budget_pages > 0; ++l) kv_maps.push_back(make_kv_map(kv, l));
     free_pages.resize(budget_pages);
     for (size_t i = 0; i < budget_pages; ++i) free_pages[i] = int32_t(budget_pages - 1 - i);
     page_ref.assign(budget_pages, 0);
@@ -629,8 +631,9 @@ struct Session {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
         launch_attn_prep(d, ly, partial.p, proj_w, ps, proj_stride, token_pos.p, slot_mapping.p, T, kv,
                          ly.type_index, q.p, gate.p, s);
-        launch_attention(d, q.p, gate.p, token_seq.p, token_pos.p, descs.p, block_table.p, bt_stride, kv,
-                         ly.type_index, T, max_len, attn_ws.p, std::max(1, splits_needed), hb2.p, s);
+        launch_attn_decode(kv_maps[ly.type_index], d, q.p, token_seq.p, token_pos.p, descs.p, block_table.p,
+                           bt_stride, T, max_len, attn_ws.p, std::max(1, splits_needed), err.p, s);
+        launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, std::max(1, splits_needed), hb2.p, s);
         stage(8);  // AttentionOutput
       }
       const size_t out_stride = size_t(T) * d.H;

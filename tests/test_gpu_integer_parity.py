@@ -18,7 +18,7 @@ def wide(pkg, O):
         pytest.skip("no CUDA device")
     cfg = pkg.config1(layers=4, context=2048)
     store = pkg.WeightStore().synthetic(cfg, 5)
-    sess = pkg.DeviceSession(store, cfg, slots=64, budget_bytes=8 << 30)
+    sess = pkg.DeviceSession(store, cfg, slots=160, budget_bytes=16 << 30)
     yield pkg, cfg, store, sess
     sess.close()
     store.close()
