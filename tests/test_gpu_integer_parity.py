@@ -95,7 +95,7 @@ def test_packing_bit_exact(wide, O):
     rows1 = sess.debug_capture(4)
     n1, T1, R1, d1, pages1, *_ = _unpack(blob1)
     maxp1 = rows1.size // n1
-    bt = np.full((64, 2048 // 16 + 1), -7, np.int32)
+    bt = np.full((160, 2048 // 16 + 1), -7, np.int32)
     for i in range(n1):
         np_i = int(d1[i, 4] + d1[i, 6])
         bt[d1[i, 3], :np_i] = rows1.reshape(n1, maxp1)[i, :np_i]
