@@ -50,14 +50,18 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 }
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err) {
   if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (clock64() - t0 > kAttnWaitCycles) {
-      atomicOr(err, kErrTimeout);
-      return false;
+  long long t0 = -1;
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try(bar, parity)) return true;
+    if ((n & 255u) == 0) {
+      const long long now = clock64();
+      if (t0 < 0) t0 = now;
+      else if (now - t0 > kAttnWaitCycles) {
+        atomicOr(err, kErrTimeout);
+        return false;
+      }
     }
   }
-  return true;
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -66,21 +66,35 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and flags the error) after ~1 s.
+// Bounded wait: returns false (and flags the error) after ~1 s. The clock is
+// read once per 256 polls so spinning warps stay off the XU pipe.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint32_t* err) {
   if (mbar_try(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      *abort = 1;
-      atomicOr(err, kErrTimeout);
-      return false;
+  long long t0 = -1;
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try(bar, parity)) return true;
+    if ((n & 255u) == 0) {
+      if (*abort) return false;
+      const long long now = clock64();
+      if (t0 < 0) t0 = now;
+      else if (now - t0 > kWaitCycles) {
+        *abort = 1;
+        atomicOr(err, kErrTimeout);
+        return false;
+      }
     }
   }
-  return true;
 }
+
+// Ring position: stage index and phase parity, advanced without division.
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) { s = 0; ph ^= 1u; }
+  }
+};
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -253,18 +267,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      uint32_t it = 0;
+      Ring ring;
       for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
         const Work w = item_at(a, i, goff);
         if (!w.valid) continue;
-        for (int tb = w.p0; tb < w.p1; tb += box) {
-          for (int c = w.c0; c < w.c1; ++c, ++it) {
-            const int s = it % S;
-            const uint32_t ph = (it / S) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, a.err)) break;
-            mbar_expect_tx(&full[s], kTileBytes + b_bytes);
-            bulk_load(ring_w + size_t(s) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[s]);
-            tma_load_2d(ring_b + size_t(s) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[s]);
+        bool ok = true;
+        for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
+          for (int c = w.c0; c < w.c1; ++c, ring.next(S)) {
+            if (!mbar_wait(&empty[ring.s], ring.ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+            mbar_expect_tx(&full[ring.s], kTileBytes + b_bytes);
+            bulk_load(ring_w + size_t(ring.s) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[ring.s]);
+            tma_load_2d(ring_b + size_t(ring.s) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[ring.s]);
           }
         }
       }
@@ -272,31 +285,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t it = 0, acc_it = 0;
+      Ring ring;
+      Ring astage[kDequantGroups];
+      uint32_t acc_it = 0;
+      int wg = 0;
       const uint32_t idesc = idesc_bf16(box);
-      for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
+      bool ok = true;
+      for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
         const Work w = item_at(a, i, goff);
         if (!w.valid) continue;
-        for (int tb = w.p0; tb < w.p1; tb += box, ++acc_it) {
+        for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
           const int d = acc_it & 1;
-          if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+          if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_tmem = tmem + kDCol0 + d * 128;
-          for (int c = w.c0; c < w.c1; ++c, ++it) {
-            const int s = it % S;
-            const int wg = it % kDequantGroups, k_in = it / kDequantGroups;
-            const int sa = wg * kAStages + k_in % kAStages;
-            if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) break;
-            if (!mbar_wait(&a_full[sa], (k_in / kAStages) & 1, abort_flag, a.err)) break;
+          for (int c = w.c0; c < w.c1; ++c, ring.next(S)) {
+            const int sa = wg * kAStages + astage[wg].s;
+            if (!mbar_wait(&full[ring.s], ring.ph, abort_flag, a.err)) { ok = false; break; }
+            if (!mbar_wait(&a_full[sa], astage[wg].ph, abort_flag, a.err)) { ok = false; break; }
             tc_fence_after();
-            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(s) * b_bytes));
+            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(ring.s) * b_bytes));
 #pragma unroll
             for (int k = 0; k < kTileK / 16; ++k)
               mma_ts(d_tmem, tmem + sa * 32 + k * 8, bdesc + uint64_t(k * 2), idesc, (c > w.c0 || k > 0) ? 1u : 0u);
-            mma_commit(&empty[s]);
+            mma_commit(&empty[ring.s]);
             mma_commit(&a_empty[sa]);
+            astage[wg].next(kAStages);
+            wg = (wg + 1) % kDequantGroups;
           }
-          mma_commit(&acc_full[d]);
+          if (ok) mma_commit(&acc_full[d]);
         }
       }
     }
@@ -307,19 +324,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const int half = box / kDequantGroups;  // epilogue columns per warpgroup
-    uint32_t it = 0, acc_it = 0;
+    uint32_t acc_it = 0;
+    Ring ring, astage;
+    int turn = 0;  // warpgroup owning the next chunk
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
-        for (int c = w.c0; c < w.c1; ++c, ++it) {
-          if (int(it % kDequantGroups) != wg) continue;
-          const int s = it % S;
-          const int k_in = it / kDequantGroups;
-          const int sa = wg * kAStages + k_in % kAStages;
-          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag, a.err)) { ok = false; break; }
-          const uint8_t* tile = ring_w + size_t(s) * kTileBytes;
+        for (int c = w.c0; c < w.c1; ++c, ring.next(S), turn = (turn + 1) % kDequantGroups) {
+          if (turn != wg) continue;
+          const int sa = wg * kAStages + astage.s;
+          if (!mbar_wait(&full[ring.s], ring.ph, abort_flag, a.err)) { ok = false; break; }
+          const uint8_t* tile = ring_w + size_t(ring.s) * kTileBytes;
           const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
           const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
           const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
@@ -337,12 +354,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
           QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
 #undef QWEN_DEQ_WORD
-          if (!mbar_wait(&a_empty[sa], ((k_in / kAStages) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
+          if (!mbar_wait(&a_empty[sa], astage.ph ^ 1, abort_flag, a.err)) { ok = false; break; }
           tmem_st32(tmem + lane_addr + sa * 32, v);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[sa]);
+          astage.next(kAStages);
         }
         if (!ok) break;
         // epilogue for token block [tb, tb + box): this warpgroup owns columns
