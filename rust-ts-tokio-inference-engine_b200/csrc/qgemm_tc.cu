@@ -8,17 +8,21 @@
 //   warp 0  producer: cp.async.bulk of each 4608-byte weight tile and a TMA
 //           (128B-swizzled) load of the matching 64-column activation tile into
 //           an S-stage shared-memory ring (mbarrier complete_tx);
-//   warp 1  MMA issuer: allocates TMEM, issues tcgen05.mma (A from TMEM, B from
-//           shared memory) and tcgen05.commit to release stages;
-//   warps 2-9 dequantise (two warpgroups taking alternate chunks, so the
-//           per-chunk latency chain of one group overlaps the other's): each
+//   warp 1  MMA issuer (converged warp, one elected lane issues): allocates
+//           TMEM, issues tcgen05.mma (A from TMEM, B from shared memory) and one
+//           tcgen05.commit per two chunks, releasing a pair of stages (a commit
+//           costs several MMA issues, so they are batched);
+//   warps 2-13 dequantise (three warpgroups taking chunks round-robin, so the
+//           per-chunk latency chain of one group overlaps the others'): each
 //           thread owns one weight row, turns its 64 nibbles
 //           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
 //           them into TMEM with tcgen05.st (the A operand); they also run the
 //           epilogue (tcgen05.ld of the fp32 accumulator, split-K partial
 //           store / SwiGLU / fp32 store).
-// The dequantised weights never touch shared memory. Every mbarrier wait is
-// bounded (~1 s); on expiry the kernel raises kErrTimeout and drains out.
+// The dequantised weights never touch shared memory. Stage i of the 8-stage
+// shared-memory ring pairs with TMEM A stage i; both are released by the same
+// commit. Every mbarrier wait is bounded (~1 s); on expiry the kernel raises
+// kErrTimeout and drains out.
 #include <cuda.h>
 
 #include <atomic>
@@ -32,11 +36,11 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
-constexpr int kDequantGroups = 2;    // dequant warpgroups, alternating chunks
+constexpr int kDequantGroups = 3;    // dequant warpgroups, round-robin over chunks
 constexpr int kWarps = 2 + 4 * kDequantGroups;
 constexpr int kThreads = kWarps * 32;
-constexpr int kAStages = 4;          // TMEM A stages per warpgroup (32 columns each)
-constexpr int kDCol0 = kDequantGroups * kAStages * 32;  // accumulators (2 x 128 columns)
+constexpr int kStages = 8;           // shared-memory ring = TMEM A stages (32 columns each)
+constexpr int kDCol0 = kStages * 32; // accumulators (2 x 128 columns)
 constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
 constexpr int kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at 1.9 GHz
@@ -109,6 +113,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "[%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(p));
+  return p != 0;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -220,34 +232,39 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* g
   return w;
 }
 
+__device__ unsigned long long* g_trace = nullptr;  // [5][512] clock64 stamps of CTA 0 (diagnostic)
+#define QTRACE(kind, idx)                                                          \
+  do {                                                                             \
+    if (trace && (idx) < 512) trace[(kind) * 512 + (idx)] = clock64(); \
+  } while (0)
+
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // carve: [B ring (1024-aligned)] [W ring] [exchange] [barriers]
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = a.stages;
+  constexpr int S = kStages;
   const int box = a.box_rows;
   const uint32_t b_bytes = uint32_t(box) * 128;
   uint8_t* ring_b = base;
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
   float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [groups][64][box+1]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + kDequantGroups * 64 * (box + 1));
-  constexpr int NA = kDequantGroups * kAStages;
-  uint64_t* full = bars;                 // [S]
-  uint64_t* empty = full + S;            // [S]
-  uint64_t* a_full = empty + S;          // [NA]
-  uint64_t* a_empty = a_full + NA;       // [NA]
-  uint64_t* acc_full = a_empty + NA;     // [2]
-  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* full = bars;              // [S]   data landed (producer tx)
+  uint64_t* a_full = full + S;        // [S]   A stage written (4 dequant warps)
+  uint64_t* empty = a_full + S;       // [S/2] stage pair consumed by the MMAs (commit)
+  uint64_t* acc_full = empty + S / 2; // [2]   accumulator complete (commit)
+  uint64_t* acc_empty = acc_full + 2; // [2]   accumulator drained (all dequant warps)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
   int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long* const trace = blockIdx.x == 0 ? g_trace : nullptr;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < NA; ++s) { mbar_init(&a_full[s], 4); mbar_init(&a_empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4 * kDequantGroups); }
+    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&a_full[i], 4); }
+    for (int i = 0; i < S / 2; ++i) mbar_init(&empty[i], 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4 * kDequantGroups); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -265,78 +282,92 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = n_items(a);
 
   if (warp == 0) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      Ring ring;
-      for (int i = blockIdx.x; i < total && !*abort_flag; i += gridDim.x) {
-        const Work w = item_at(a, i, goff);
-        if (!w.valid) continue;
-        bool ok = true;
-        for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
-          for (int c = w.c0; c < w.c1; ++c, ring.next(S)) {
-            if (!mbar_wait(&empty[ring.s], ring.ph ^ 1, abort_flag, a.err)) { ok = false; break; }
-            mbar_expect_tx(&full[ring.s], kTileBytes + b_bytes);
-            bulk_load(ring_w + size_t(ring.s) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[ring.s]);
-            tma_load_2d(ring_b + size_t(ring.s) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[ring.s]);
+    // ---------------- producer (converged warp, elected lane issues) ----------------
+    uint32_t it = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i, goff);
+      if (!w.valid) continue;
+      for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
+        for (int c = w.c0; c < w.c1; ++c, ++it) {
+          const int st = it & (S - 1);
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&empty[st >> 1], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          if (elect_one()) {
+            QTRACE(0, it);
+            mbar_expect_tx(&full[st], kTileBytes + b_bytes);
+            bulk_load(ring_w + size_t(st) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[st]);
+            tma_load_2d(ring_b + size_t(st) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[st]);
           }
+          __syncwarp();
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      Ring ring;
-      Ring astage[kDequantGroups];
-      uint32_t acc_it = 0;
-      int wg = 0;
-      const uint32_t idesc = idesc_bf16(box);
-      bool ok = true;
-      for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-        const Work w = item_at(a, i, goff);
-        if (!w.valid) continue;
-        for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
-          const int d = acc_it & 1;
-          if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d_tmem = tmem + kDCol0 + d * 128;
-          for (int c = w.c0; c < w.c1; ++c, ring.next(S)) {
-            const int sa = wg * kAStages + astage[wg].s;
-            if (!mbar_wait(&full[ring.s], ring.ph, abort_flag, a.err)) { ok = false; break; }
-            if (!mbar_wait(&a_full[sa], astage[wg].ph, abort_flag, a.err)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(ring.s) * b_bytes));
-#pragma unroll
-            for (int k = 0; k < kTileK / 16; ++k)
-              mma_ts(d_tmem, tmem + sa * 32 + k * 8, bdesc + uint64_t(k * 2), idesc, (c > w.c0 || k > 0) ? 1u : 0u);
-            mma_commit(&empty[ring.s]);
-            mma_commit(&a_empty[sa]);
-            astage[wg].next(kAStages);
-            wg = (wg + 1) % kDequantGroups;
-          }
-          if (ok) mma_commit(&acc_full[d]);
-        }
-      }
-    }
-  } else {
-    // ---------------- dequantise + epilogue (warps 2..9) ----------------
-    const int wg = (warp - 2) >> 2;        // dequant warpgroup
-    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
-    const int r = quad * 32 + lane;        // weight row within the tile
-    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    const int half = box / kDequantGroups;  // epilogue columns per warpgroup
-    uint32_t acc_it = 0;
-    Ring ring, astage;
-    int turn = 0;  // warpgroup owning the next chunk
+    // ---------------- MMA issuer (converged warp, elected lane issues) ----------------
+    uint32_t it = 0, acc_it = 0;
+    const uint32_t idesc = idesc_bf16(box);
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
-        for (int c = w.c0; c < w.c1; ++c, ring.next(S), turn = (turn + 1) % kDequantGroups) {
+        const int d = acc_it & 1;
+        if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + kDCol0 + d * 128;
+        for (int c = w.c0; c < w.c1; ++c, ++it) {
+          const int st = it & (S - 1);
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[st], ph, abort_flag, a.err)) { ok = false; break; }
+          if (!mbar_wait(&a_full[st], ph, abort_flag, a.err)) { ok = false; break; }
+          tc_fence_after();
+          if (elect_one()) {
+            QTRACE(3, it);
+            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(st) * b_bytes));
+#pragma unroll
+            for (int k = 0; k < kTileK / 16; ++k)
+              mma_ts(d_tmem, tmem + st * 32 + k * 8, bdesc + uint64_t(k * 2), idesc, (c > w.c0 || k > 0) ? 1u : 0u);
+            if (st & 1) mma_commit(&empty[st >> 1]);  // releases stages st-1 and st
+          }
+          __syncwarp();
+        }
+        if (ok && elect_one()) mma_commit(&acc_full[d]);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ---------------- dequantise + epilogue (warps 2..13) ----------------
+    const int wg = (warp - 2) >> 2;        // dequant warpgroup
+    const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;        // weight row within the tile
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    uint32_t it = 0, acc_it = 0;
+    int turn = 0;  // warpgroup owning chunk `it`
+    bool ok = true;
+    // one chunk of lag: the TMEM store of chunk k completes while chunk k+1 is dequantised
+    int pend_st = -1;
+    auto finish_pending = [&]() {
+      if (pend_st >= 0) {
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[pend_st]);
+        pend_st = -1;
+      }
+    };
+    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i, goff);
+      if (!w.valid) continue;
+      for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
+        for (int c = w.c0; c < w.c1; ++c, ++it, turn = (turn == kDequantGroups - 1) ? 0 : turn + 1) {
           if (turn != wg) continue;
-          const int sa = wg * kAStages + astage.s;
-          if (!mbar_wait(&full[ring.s], ring.ph, abort_flag, a.err)) { ok = false; break; }
-          const uint8_t* tile = ring_w + size_t(ring.s) * kTileBytes;
+          const int st = it & (S - 1);
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_try(&full[st], ph)) finish_pending();  // don't hold chunk it-3 behind this wait
+          if (!mbar_wait(&full[st], ph, abort_flag, a.err)) { ok = false; break; }
+          if (quad == 0 && lane == 0) QTRACE(1, it);
+          const uint8_t* tile = ring_w + size_t(st) * kTileBytes;
           const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
           const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
           const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
@@ -354,23 +385,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
           QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
 #undef QWEN_DEQ_WORD
-          if (!mbar_wait(&a_empty[sa], astage.ph ^ 1, abort_flag, a.err)) { ok = false; break; }
-          tmem_st32(tmem + lane_addr + sa * 32, v);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[sa]);
-          astage.next(kAStages);
+          finish_pending();
+          // the MMAs that read this TMEM stage last time (chunk it - S) must be done
+          if (!mbar_wait(&empty[st >> 1], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          tc_fence_after();
+          tmem_st32(tmem + lane_addr + st * 32, v);
+          pend_st = st;
+          if (quad == 0 && lane == 0) QTRACE(2, it);
         }
+        finish_pending();
         if (!ok) break;
-        // epilogue for token block [tb, tb + box): this warpgroup owns columns
-        // [wg*half, (wg+1)*half)
+        // epilogue for token block [tb, tb + box): warpgroup wg owns 8-column
+        // slices j0 = 8*wg, 8*wg + 8*groups, ...
         const int d = acc_it & 1;
         if (!mbar_wait(&acc_full[d], (acc_it >> 1) & 1, abort_flag, a.err)) { ok = false; break; }
         tc_fence_after();
         const int nvalid = min(box, w.p1 - tb);
         const int n_glob = w.rt * kTileRows + r;
-        for (int j0 = wg * half; j0 < (wg + 1) * half; j0 += 8) {
+        for (int j0 = wg * 8; j0 < box; j0 += 8 * kDequantGroups) {
           uint32_t v[8];
           tmem_ld8(tmem + lane_addr + kDCol0 + d * 128 + j0, v);
           tmem_wait_ld();
@@ -410,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_empty[d]);
       }
     }
+    finish_pending();
   }
   // teardown: every warp reaches here (bounded waits); free TMEM
   tc_fence_before();
@@ -422,18 +455,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t qgemm_tc_smem(int box_rows, int stages) {
-  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) +
-         kDequantGroups * 64 * size_t(box_rows + 1) * 4 +
-         (2 * size_t(stages) + 2 * kDequantGroups * kAStages + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
+const void* g_trace_sym() { return reinterpret_cast<const void*>(&g_trace); }
+void qgemm_tc_set_trace(unsigned long long* buf) {
+  QWEN_CUDA(cudaMemcpyToSymbol(g_trace, &buf, sizeof(buf)));
 }
 
-int qgemm_tc_stages(int box_rows) {
-  const size_t budget = 200 * 1024;
-  int s = 12;
-  while (s > 2 && qgemm_tc_smem(box_rows, s) > budget) --s;
-  return s;
+size_t qgemm_tc_smem(int box_rows, int stages) {
+  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) +
+         kDequantGroups * 64 * size_t(box_rows + 1) * 4 + (2 * size_t(stages) + stages / 2 + 4) * 8 + 16 +
+         (kMaxGroups + 1) * 4;
 }
+
+int qgemm_tc_stages(int) { return kStages; }
 
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {
   if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
