@@ -314,6 +314,7 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
     attn_decode_kernel<DD><<<grid, kAttnWarps * 32, smem, s>>>(kvmap, q, token_seq, token_pos, descs,      \
                                                                block_table, bt_stride, d.Hq, d.Hkv, G,      \
                                                                max_splits, ws, err);                        \
+    QWEN_CUDA(cudaGetLastError());                                                                          \
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);                                              \
     return;                                                                                                 \
   }

@@ -248,8 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_bytes = uint32_t(box) * 128;
   uint8_t* ring_b = base;
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
-  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [groups][64][box+1]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + kDequantGroups * 64 * (box + 1));
+  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [groups][64][9]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + kDequantGroups * 64 * 9);
   uint64_t* full = bars;              // [S]   data landed (producer tx)
   uint64_t* a_full = full + S;        // [S]   A stage written (4 dequant warps)
   uint64_t* empty = a_full + S;       // [S/2] stage pair consumed by the MMAs (commit)
@@ -419,10 +419,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 8; ++j)
               if (j0 + j < nvalid) a.Y[size_t(tb + j0 + j) * a.ldy + n] = __uint_as_float(v[j]);
           } else {
-            float* xg = xchg + wg * 64 * (box + 1);
+            float* xg = xchg + wg * 64 * 9;  // this 8-column slice, rows of the up half
             if (r >= 64) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) xg[(r - 64) * (box + 1) + j0 + j] = __uint_as_float(v[j]);
+              for (int j = 0; j < 8; ++j) xg[(r - 64) * 9 + j] = __uint_as_float(v[j]);
             }
             asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
             if (r < 64) {
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 8; ++j)
                 if (j0 + j < nvalid) {
-                  const float gv = __uint_as_float(v[j]), uv = xg[r * (box + 1) + j0 + j];
+                  const float gv = __uint_as_float(v[j]), uv = xg[r * 9 + j];
                   a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
                 }
             }
@@ -462,7 +462,7 @@ void qgemm_tc_set_trace(unsigned long long* buf) {
 
 size_t qgemm_tc_smem(int box_rows, int stages) {
   return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) +
-         kDequantGroups * 64 * size_t(box_rows + 1) * 4 + (2 * size_t(stages) + stages / 2 + 4) * 8 + 16 +
+         kDequantGroups * 64 * 9 * 4 + (2 * size_t(stages) + stages / 2 + 4) * 8 + 16 +
          (kMaxGroups + 1) * 4;
 }
 
@@ -482,7 +482,9 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   }
   const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
   const int grid = std::max(1, std::min(items, sm_count));
+  if (smem > 227 * 1024) throw std::invalid_argument("tcgen05 GEMM shared memory above 227 KB");
   qgemm_tc_kernel<<<grid, kThreads, smem, s>>>(bmap, a);
+  QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
