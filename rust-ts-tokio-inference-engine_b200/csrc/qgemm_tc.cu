@@ -9,20 +9,22 @@
 //           (128B-swizzled) load of the matching 64-column activation tile into
 //           an S-stage shared-memory ring (mbarrier complete_tx);
 //   warp 1  MMA issuer (converged warp, one elected lane issues): allocates
-//           TMEM, issues tcgen05.mma (A from TMEM, B from shared memory) and one
-//           tcgen05.commit per two chunks, releasing a pair of stages (a commit
-//           costs several MMA issues, so they are batched);
-//   warps 2-13 dequantise (three warpgroups taking chunks round-robin, so the
-//           per-chunk latency chain of one group overlaps the others'): each
-//           thread owns one weight row, turns its 64 nibbles
+//           TMEM and works in units of U (= 4, 2 or 1) chunks: one mbarrier
+//           wait, 4U tcgen05.mma (A from TMEM, B from shared memory) and one
+//           tcgen05.commit per unit. Measured on B200, an MMA issue costs ~26
+//           cycles, an mbarrier wait ~80 and a commit ~200 unless ~16 MMAs
+//           separate commits, so units amortise the fixed costs;
+//   warps 2-13 dequantise (three warpgroups taking whole units round-robin):
+//           each thread owns one weight row, turns its 64 nibbles per chunk
 //           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
-//           them into TMEM with tcgen05.st (the A operand); they also run the
-//           epilogue (tcgen05.ld of the fp32 accumulator, split-K partial
-//           store / SwiGLU / fp32 store).
-// The dequantised weights never touch shared memory. Stage i of the 8-stage
-// shared-memory ring pairs with TMEM A stage i; both are released by the same
-// commit. Every mbarrier wait is bounded (~1 s); on expiry the kernel raises
-// kErrTimeout and drains out.
+//           them into TMEM with tcgen05.st (the A operand);
+//   warps 14-17 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
+//           partial store / SwiGLU (bf16) / fp32 store.
+// The dequantised weights never touch shared memory. Stage i of the
+// shared-memory ring pairs with TMEM A stage i; a unit's stages are released
+// together by its commit. Units never straddle work items (split-K ranges are
+// multiples of U). Every mbarrier wait is bounded (~1 s); on expiry the kernel
+// raises kErrTimeout and drains out.
 #include <cuda.h>
 
 #include <atomic>
@@ -36,11 +38,11 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
-constexpr int kDequantGroups = 3;    // dequant warpgroups, round-robin over chunks
-constexpr int kWarps = 2 + 4 * kDequantGroups;
+constexpr int kDequantGroups = 3;    // dequant warpgroups, round-robin over units
+constexpr int kEpiWarp0 = 2 + 4 * kDequantGroups;  // first warp of the epilogue warpgroup
+constexpr int kWarps = kEpiWarp0 + 4;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 8;           // shared-memory ring = TMEM A stages (32 columns each)
-constexpr int kDCol0 = kStages * 32; // accumulators (2 x 128 columns)
+constexpr int kMaxStages = 12;       // shared-memory ring = TMEM A stages (32 columns each)
 constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
 constexpr int kTmemCols = 512;
 constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at 1.9 GHz
@@ -243,18 +245,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // carve: [B ring (1024-aligned)] [W ring] [exchange] [barriers]
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int S = kStages;
+  const int S = a.stages;         // ring depth in chunks (multiple of U)
+  const int U = a.unit;           // chunks per unit (4, 2 or 1)
+  const int ushift = U == 4 ? 2 : (U == 2 ? 1 : 0);
+  const int NS = S / U;           // unit slots
   const int box = a.box_rows;
+  const int d_col0 = S * 32;      // accumulators after the A stages
+  const int d_stride = box <= 64 ? 64 : 128;
   const uint32_t b_bytes = uint32_t(box) * 128;
   uint8_t* ring_b = base;
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
-  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [groups][64][9]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + kDequantGroups * 64 * 9);
-  uint64_t* full = bars;              // [S]   data landed (producer tx)
-  uint64_t* a_full = full + S;        // [S]   A stage written (4 dequant warps)
-  uint64_t* empty = a_full + S;       // [S/2] stage pair consumed by the MMAs (commit)
-  uint64_t* acc_full = empty + S / 2; // [2]   accumulator complete (commit)
-  uint64_t* acc_empty = acc_full + 2; // [2]   accumulator drained (all dequant warps)
+  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [64][9]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * 9);
+  uint64_t* full = bars;                // [S]   chunk landed (producer tx)
+  uint64_t* a_full = full + S;          // [NS]  unit's A stages written (4 dequant warps)
+  uint64_t* empty = a_full + NS;        // [NS]  unit consumed by the MMAs (commit)
+  uint64_t* acc_full = empty + NS;      // [2]   accumulator complete (commit)
+  uint64_t* acc_empty = acc_full + 2;   // [2]   accumulator drained (4 epilogue warps)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
   int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
@@ -262,9 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long* const trace = blockIdx.x == 0 ? g_trace : nullptr;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&a_full[i], 4); }
-    for (int i = 0; i < S / 2; ++i) mbar_init(&empty[i], 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4 * kDequantGroups); }
+    for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < NS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -283,16 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- producer (converged warp, elected lane issues) ----------------
-    uint32_t it = 0;
+    int st = 0;
+    uint32_t ph = 0, it = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
         for (int c = w.c0; c < w.c1; ++c, ++it) {
-          const int st = it & (S - 1);
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&empty[st >> 1], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          if ((st & (U - 1)) == 0 && !mbar_wait(&empty[st >> ushift], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
           if (elect_one()) {
             QTRACE(0, it);
             mbar_expect_tx(&full[st], kTileBytes + b_bytes);
@@ -300,12 +306,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(ring_b + size_t(st) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[st]);
           }
           __syncwarp();
+          if (++st == S) { st = 0; ph ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (converged warp, elected lane issues) ----------------
-    uint32_t it = 0, acc_it = 0;
+    int st = 0;
+    uint32_t ph = 0, acc_it = 0, it = 0;
     const uint32_t idesc = idesc_bf16(box);
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
@@ -315,96 +323,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d = acc_it & 1;
         if (!mbar_wait(&acc_empty[d], ((acc_it >> 1) & 1) ^ 1, abort_flag, a.err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + kDCol0 + d * 128;
-        for (int c = w.c0; c < w.c1; ++c, ++it) {
-          const int st = it & (S - 1);
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_wait(&full[st], ph, abort_flag, a.err)) { ok = false; break; }
-          if (!mbar_wait(&a_full[st], ph, abort_flag, a.err)) { ok = false; break; }
+        const uint32_t d_tmem = tmem + d_col0 + d * d_stride;
+        for (int c = w.c0; c < w.c1; c += U) {
+          const int slot = st >> ushift;
+          if (!mbar_wait(&a_full[slot], ph, abort_flag, a.err)) { ok = false; break; }
           tc_fence_after();
           if (elect_one()) {
             QTRACE(3, it);
-            const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(st) * b_bytes));
+            for (int u = 0; u < U; ++u) {
+              const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(st + u) * b_bytes));
 #pragma unroll
-            for (int k = 0; k < kTileK / 16; ++k)
-              mma_ts(d_tmem, tmem + st * 32 + k * 8, bdesc + uint64_t(k * 2), idesc, (c > w.c0 || k > 0) ? 1u : 0u);
-            if (st & 1) mma_commit(&empty[st >> 1]);  // releases stages st-1 and st
+              for (int k = 0; k < kTileK / 16; ++k)
+                mma_ts(d_tmem, tmem + (st + u) * 32 + k * 8, bdesc + uint64_t(k * 2), idesc,
+                       (c + u > w.c0 || k > 0) ? 1u : 0u);
+            }
+            mma_commit(&empty[slot]);
           }
           __syncwarp();
+          it += U;
+          st += U;
+          if (st == S) { st = 0; ph ^= 1; }
         }
         if (ok && elect_one()) mma_commit(&acc_full[d]);
         __syncwarp();
       }
     }
-  } else {
-    // ---------------- dequantise + epilogue (warps 2..13) ----------------
-    const int wg = (warp - 2) >> 2;        // dequant warpgroup
+  } else if (warp < kEpiWarp0) {
+    // ---------------- dequantise (warps 2..13), whole units round-robin ----------------
+    const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    uint32_t it = 0, acc_it = 0;
-    int turn = 0;  // warpgroup owning chunk `it`
+    int st = 0, turn = 0;
+    uint32_t ph = 0, it = 0;
     bool ok = true;
-    // one chunk of lag: the TMEM store of chunk k completes while chunk k+1 is dequantised
-    int pend_st = -1;
-    auto finish_pending = [&]() {
-      if (pend_st >= 0) {
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[pend_st]);
-        pend_st = -1;
+    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i, goff);
+      if (!w.valid) continue;
+      for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
+        for (int c = w.c0; c < w.c1; c += U) {
+          if (turn == wg) {
+            const int slot = st >> ushift;
+            // the MMAs that read these TMEM stages last round must be done
+            if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+            tc_fence_after();
+            for (int u = 0; u < U; ++u) {
+              if (!mbar_wait(&full[st + u], ph, abort_flag, a.err)) { ok = false; break; }
+              if (quad == 0 && lane == 0) QTRACE(1, it + u);
+              const uint8_t* tile = ring_w + size_t(st + u) * kTileBytes;
+              const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
+              const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
+              const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
+              const uint32_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
+              __nv_bfloat162 s2, b2;
+              {
+                const uint32_t sv = sb | (sb << 16), bv = bb | (bb << 16);
+                s2 = *reinterpret_cast<const __nv_bfloat162*>(&sv);
+                b2 = *reinterpret_cast<const __nv_bfloat162*>(&bv);
+              }
+              uint32_t v[32];
+#define QWEN_DEQ_WORD(WD, W)                                                            \
+  _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
+      deq_pair((((W) >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
+              QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
+              QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
+#undef QWEN_DEQ_WORD
+              tmem_st32(tmem + lane_addr + (st + u) * 32, v);
+            }
+            if (!ok) break;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[slot]);
+            if (quad == 0 && lane == 0) QTRACE(2, it);
+          }
+          turn = (turn == kDequantGroups - 1) ? 0 : turn + 1;
+          it += U;
+          st += U;
+          if (st == S) { st = 0; ph ^= 1; }
+        }
       }
-    };
+    }
+  } else {
+    // ---------------- epilogue (warps 14..17) ----------------
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_addr = uint32_t(quad * 32) << 16;
+    uint32_t acc_it = 0;
+    bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
-        for (int c = w.c0; c < w.c1; ++c, ++it, turn = (turn == kDequantGroups - 1) ? 0 : turn + 1) {
-          if (turn != wg) continue;
-          const int st = it & (S - 1);
-          const uint32_t ph = (it / S) & 1;
-          if (!mbar_try(&full[st], ph)) finish_pending();  // don't hold chunk it-3 behind this wait
-          if (!mbar_wait(&full[st], ph, abort_flag, a.err)) { ok = false; break; }
-          if (quad == 0 && lane == 0) QTRACE(1, it);
-          const uint8_t* tile = ring_w + size_t(st) * kTileBytes;
-          const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
-          const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
-          const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
-          const uint32_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
-          __nv_bfloat162 s2, b2;
-          {
-            const uint32_t sv = sb | (sb << 16), bv = bb | (bb << 16);
-            s2 = *reinterpret_cast<const __nv_bfloat162*>(&sv);
-            b2 = *reinterpret_cast<const __nv_bfloat162*>(&bv);
-          }
-          uint32_t v[32];
-#define QWEN_DEQ_WORD(WD, W)                                                            \
-  _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
-      deq_pair((((W) >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
-          QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
-          QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
-#undef QWEN_DEQ_WORD
-          finish_pending();
-          // the MMAs that read this TMEM stage last time (chunk it - S) must be done
-          if (!mbar_wait(&empty[st >> 1], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
-          tc_fence_after();
-          tmem_st32(tmem + lane_addr + st * 32, v);
-          pend_st = st;
-          if (quad == 0 && lane == 0) QTRACE(2, it);
-        }
-        finish_pending();
-        if (!ok) break;
-        // epilogue for token block [tb, tb + box): warpgroup wg owns 8-column
-        // slices j0 = 8*wg, 8*wg + 8*groups, ...
         const int d = acc_it & 1;
         if (!mbar_wait(&acc_full[d], (acc_it >> 1) & 1, abort_flag, a.err)) { ok = false; break; }
         tc_fence_after();
         const int nvalid = min(box, w.p1 - tb);
         const int n_glob = w.rt * kTileRows + r;
-        for (int j0 = wg * 8; j0 < box; j0 += 8 * kDequantGroups) {
+        for (int j0 = 0; j0 < box && j0 < nvalid; j0 += 8) {
           uint32_t v[8];
-          tmem_ld8(tmem + lane_addr + kDCol0 + d * 128 + j0, v);
+          tmem_ld8(tmem + lane_addr + d_col0 + d * d_stride + j0, v);
           tmem_wait_ld();
           if (a.mode == kGemmStoreF32) {
             if (n_glob < a.W.rows) {
@@ -419,22 +437,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 8; ++j)
               if (j0 + j < nvalid) a.Y[size_t(tb + j0 + j) * a.ldy + n] = __uint_as_float(v[j]);
           } else {
-            float* xg = xchg + wg * 64 * 9;  // this 8-column slice, rows of the up half
             if (r >= 64) {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) xg[(r - 64) * 9 + j] = __uint_as_float(v[j]);
+              for (int j = 0; j < 8; ++j) xchg[(r - 64) * 9 + j] = __uint_as_float(v[j]);
             }
-            asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
             if (r < 64) {
               const int jj = w.rt_local * 64 + r;
 #pragma unroll
               for (int j = 0; j < 8; ++j)
                 if (j0 + j < nvalid) {
-                  const float gv = __uint_as_float(v[j]), uv = xg[r * 9 + j];
+                  const float gv = __uint_as_float(v[j]), uv = xchg[r * 9 + j];
                   a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
                 }
             }
-            asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
           }
         }
         tc_fence_before();
@@ -442,7 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&acc_empty[d]);
       }
     }
-    finish_pending();
   }
   // teardown: every warp reaches here (bounded waits); free TMEM
   tc_fence_before();
@@ -461,12 +477,13 @@ void qgemm_tc_set_trace(unsigned long long* buf) {
 }
 
 size_t qgemm_tc_smem(int box_rows, int stages) {
-  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) +
-         kDequantGroups * 64 * 9 * 4 + (2 * size_t(stages) + stages / 2 + 4) * 8 + 16 +
-         (kMaxGroups + 1) * 4;
+  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) + 64 * 9 * 4 +
+         (size_t(stages) + 2 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
 }
 
-int qgemm_tc_stages(int) { return kStages; }
+// Ring depth (chunks): A stages (32 TMEM columns each) plus two accumulators
+// (64 or 128 columns) fit in 512 columns.
+int qgemm_tc_stages(int box_rows) { return box_rows <= 64 ? 12 : 8; }
 
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {
   if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
@@ -474,6 +491,14 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   if (a.mode == kGemmStoreF32 && a.n_tokens <= 0) return;
   if (a.mode != kGemmStoreF32 && a.groups > kMaxGroups) throw std::invalid_argument("too many GEMM groups");
   a.stages = qgemm_tc_stages(a.box_rows);
+  {  // unit: largest of 4, 2, 1 dividing every item's chunk count and the ring depth
+    const int kc = a.W.k_chunks();
+    const int per = a.mode == kGemmStoreF32 ? (kc + a.splits - 1) / a.splits : kc;
+    const bool even_split = a.mode != kGemmStoreF32 || per * a.splits == kc;
+    a.unit = 1;
+    for (int u : {4, 2})
+      if (per % u == 0 && even_split && a.stages % u == 0) { a.unit = u; break; }
+  }
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
   static bool configured = false;
   if (!configured) {

@@ -18,6 +18,7 @@ struct TcArgs {
   int b_row0 = 0;      // first activation row of the B tensor map
   int box_rows = 16;   // N tile: 16, 32, 64 or 128 (the tensor map's box height)
   int stages = 0;      // shared-memory ring depth (set by the launcher)
+  int unit = 1;        // chunks per MMA unit (set by the launcher)
   float* Y = nullptr;
   int ldy = 0;
   __nv_bfloat16* Yb = nullptr;

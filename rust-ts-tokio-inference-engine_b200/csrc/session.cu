@@ -176,7 +176,11 @@ struct Session {
     a.n_tokens = T;
     a.box_rows = box_for(std::min(T, 128));
     const int kc = W.k_chunks();
-    int splits = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc / 2}));
+    // split-K: enough items for ~2 waves, slices of whole 4-chunk units when possible
+    const int want = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc}));
+    int splits = 1;
+    for (int sp = want; sp >= 1; --sp)
+      if (kc % sp == 0 && (kc / sp) % 4 == 0) { splits = sp; break; }
     a.splits = splits;
     a.split_stride = split_stride;
     a.Y = Y;
