@@ -482,8 +482,11 @@ size_t qgemm_tc_smem(int box_rows, int stages) {
 }
 
 // Ring depth (chunks): A stages (32 TMEM columns each) plus two accumulators
-// (64 or 128 columns) fit in 512 columns.
-int qgemm_tc_stages(int box_rows) { return box_rows <= 64 ? 12 : 8; }
+// (64 or 128 columns) fit in 512 columns. The number of unit slots
+// (stages / unit) must be a multiple of the dequant warpgroup count, so every
+// round of a slot belongs to the same warpgroup: a warpgroup then can never
+// wait on a slot more than one phase ahead (mbarrier parity would alias).
+int qgemm_tc_stages(int box_rows) { return box_rows <= 64 ? 12 : 6; }
 
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {
   if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
@@ -497,7 +500,11 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
     const bool even_split = a.mode != kGemmStoreF32 || per * a.splits == kc;
     a.unit = 1;
     for (int u : {4, 2})
-      if (per % u == 0 && even_split && a.stages % u == 0) { a.unit = u; break; }
+      if (per % u == 0 && even_split && a.stages % u == 0 && (a.stages / u) % kDequantGroups == 0) {
+        a.unit = u;
+        break;
+      }
+    if ((a.stages / a.unit) % kDequantGroups) throw std::logic_error("GEMM unit slots not a multiple of warpgroups");
   }
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
   static bool configured = false;
