@@ -125,6 +125,14 @@ __device__ __forceinline__ bool elect_one() {
   return p != 0;
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -257,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
   float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [64][9]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * 9);
-  uint64_t* full = bars;                // [S]   chunk landed (producer tx)
-  uint64_t* a_full = full + S;          // [NS]  unit's A stages written (4 dequant warps)
+  uint64_t* full = bars;                // [NS]  unit's tiles landed (producer tx)
+  uint64_t* a_full = full + NS;         // [NS]  unit's A stages written (4 dequant warps)
   uint64_t* empty = a_full + NS;        // [NS]  unit consumed by the MMAs (commit)
   uint64_t* acc_full = empty + NS;      // [2]   accumulator complete (commit)
   uint64_t* acc_empty = acc_full + 2;   // [2]   accumulator drained (4 epilogue warps)
@@ -269,8 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long* const trace = blockIdx.x == 0 ? g_trace : nullptr;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
-    for (int i = 0; i < NS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -290,6 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- producer (converged warp, elected lane issues) ----------------
+    // one bulk copy of the unit's U contiguous weight tiles and one 3-D TMA of
+    // its U activation tiles ([U][box rows][64 columns], 128B-swizzled)
     int st = 0;
     uint32_t ph = 0, it = 0;
     bool ok = true;
@@ -297,16 +306,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
-        for (int c = w.c0; c < w.c1; ++c, ++it) {
-          if ((st & (U - 1)) == 0 && !mbar_wait(&empty[st >> ushift], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+        for (int c = w.c0; c < w.c1; c += U, it += U) {
+          const int slot = st >> ushift;
+          if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
           if (elect_one()) {
             QTRACE(0, it);
-            mbar_expect_tx(&full[st], kTileBytes + b_bytes);
-            bulk_load(ring_w + size_t(st) * kTileBytes, a.W.tile(w.rt, c), kTileBytes, &full[st]);
-            tma_load_2d(ring_b + size_t(st) * b_bytes, &bmap, c * kTileK, a.b_row0 + tb, &full[st]);
+            mbar_expect_tx(&full[slot], uint32_t(U) * (kTileBytes + b_bytes));
+            bulk_load(ring_w + size_t(st) * kTileBytes, a.W.tile(w.rt, c), uint32_t(U) * kTileBytes, &full[slot]);
+            tma_load_3d(ring_b + size_t(st) * b_bytes, &bmap, 0, a.b_row0 + tb, c, &full[slot]);
           }
           __syncwarp();
-          if (++st == S) { st = 0; ph ^= 1; }
+          st += U;
+          if (st == S) { st = 0; ph ^= 1; }
         }
       }
     }
@@ -366,10 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int slot = st >> ushift;
             // the MMAs that read these TMEM stages last round must be done
             if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+            if (!mbar_wait(&full[slot], ph, abort_flag, a.err)) { ok = false; break; }
             tc_fence_after();
+            if (quad == 0 && lane == 0) QTRACE(1, it);
             for (int u = 0; u < U; ++u) {
-              if (!mbar_wait(&full[st + u], ph, abort_flag, a.err)) { ok = false; break; }
-              if (quad == 0 && lane == 0) QTRACE(1, it + u);
               const uint8_t* tile = ring_w + size_t(st + u) * kTileBytes;
               const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
               const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
@@ -478,7 +489,7 @@ void qgemm_tc_set_trace(unsigned long long* buf) {
 
 size_t qgemm_tc_smem(int box_rows, int stages) {
   return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) + 64 * 9 * 4 +
-         (size_t(stages) + 2 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
+         (3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
 }
 
 // Ring depth (chunks): A stages (32 TMEM columns each) plus two accumulators
@@ -488,24 +499,24 @@ size_t qgemm_tc_smem(int box_rows, int stages) {
 // wait on a slot more than one phase ahead (mbarrier parity would alias).
 int qgemm_tc_stages(int box_rows) { return box_rows <= 64 ? 12 : 6; }
 
+int qgemm_tc_unit(const TcArgs& a) {
+  const int stages = qgemm_tc_stages(a.box_rows);
+  const int kc = a.W.k_chunks();
+  const int per = a.mode == kGemmStoreF32 ? (kc + a.splits - 1) / a.splits : kc;
+  const bool even_split = a.mode != kGemmStoreF32 || per * a.splits == kc;
+  for (int u : {4, 2})
+    if (per % u == 0 && even_split && stages % u == 0 && (stages / u) % kDequantGroups == 0) return u;
+  return 1;
+}
+
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {
   if (a.box_rows != 16 && a.box_rows != 32 && a.box_rows != 64 && a.box_rows != 128)
     throw std::invalid_argument("tcgen05 GEMM box rows must be 16, 32, 64 or 128");
   if (a.mode == kGemmStoreF32 && a.n_tokens <= 0) return;
   if (a.mode != kGemmStoreF32 && a.groups > kMaxGroups) throw std::invalid_argument("too many GEMM groups");
   a.stages = qgemm_tc_stages(a.box_rows);
-  {  // unit: largest of 4, 2, 1 dividing every item's chunk count and the ring depth
-    const int kc = a.W.k_chunks();
-    const int per = a.mode == kGemmStoreF32 ? (kc + a.splits - 1) / a.splits : kc;
-    const bool even_split = a.mode != kGemmStoreF32 || per * a.splits == kc;
-    a.unit = 1;
-    for (int u : {4, 2})
-      if (per % u == 0 && even_split && a.stages % u == 0 && (a.stages / u) % kDequantGroups == 0) {
-        a.unit = u;
-        break;
-      }
-    if ((a.stages / a.unit) % kDequantGroups) throw std::logic_error("GEMM unit slots not a multiple of warpgroups");
-  }
+  a.unit = qgemm_tc_unit(a);  // largest of 4, 2, 1 dividing the items and the ring (slots % groups == 0)
+  if ((a.stages / a.unit) % kDequantGroups) throw std::logic_error("GEMM unit slots not a multiple of warpgroups");
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
   static bool configured = false;
   if (!configured) {
@@ -550,6 +561,22 @@ CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows) {
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+CUtensorMap make_act_map3d(const void* base, int rows, int k, int box_rows, int unit) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k * 2) % 16 || k % kTileK)
+    throw std::invalid_argument("activation tensor map alignment");
+  CUtensorMap m;
+  // X[rows][k] viewed as [k/64 chunks][rows][64]: one box = `unit` chunk tiles
+  const cuuint64_t dims[3] = {cuuint64_t(kTileK), cuuint64_t(rows), cuuint64_t(k / kTileK)};
+  const cuuint64_t strides[2] = {cuuint64_t(k) * 2, cuuint64_t(kTileK) * 2};
+  const cuuint32_t box[3] = {cuuint32_t(kTileK), cuuint32_t(box_rows), cuuint32_t(unit)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D activations) failed: " + std::to_string(int(r)));
   return m;
 }
 

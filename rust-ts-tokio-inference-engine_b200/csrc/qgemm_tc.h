@@ -29,6 +29,11 @@ struct TcArgs {
 // Tensor map over a row-major bf16 activation matrix [rows, k] with a
 // (64 columns x box_rows) box and 128-byte swizzle (the UMMA K-major layout).
 CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows);
+// The same matrix viewed as [k/64 chunks][rows][64]: one box brings `unit`
+// consecutive 64-column tiles (the B operand of one MMA unit).
+CUtensorMap make_act_map3d(const void* base, int rows, int k, int box_rows, int unit);
+// Chunks per MMA unit the launcher will use for these arguments (4, 2 or 1).
+int qgemm_tc_unit(const TcArgs& a);
 // Tensor map over one attention layer's KV page pool: rows
 // ((page*2 + k_or_v)*Hkv + head)*16 + token, D columns, 16x64 128B-swizzled box.
 CUtensorMap make_kv_map(const KvPool& kv, int layer);

@@ -145,14 +145,17 @@ struct Session {
   int sm_count = 148;
   int cur_layer = 0;
   bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
-  std::map<std::tuple<const void*, int, int, int>, CUtensorMap> maps;
+  std::map<std::tuple<const void*, int, int, int, int>, CUtensorMap> maps;
   std::vector<CUtensorMap> kv_maps;  // one per attention layer
 
-  const CUtensorMap& act_map(const void* p, int rows, int k, int box) {
-    auto key = std::make_tuple(p, rows, k, box);
+  const CUtensorMap& act_map(const void* p, int rows, int k, int box, int unit) {
+    auto key = std::make_tuple(p, rows, k, box, unit);
     auto it = maps.find(key);
-    if (it == maps.end()) it = maps.emplace(key, make_act_map(p, rows, k, box)).first;
+    if (it == maps.end()) it = maps.emplace(key, make_act_map3d(p, rows, k, box, unit)).first;
     return it->second;
+  }
+  void launch_tc(const void* X, int rows_cap, TcArgs& a, cudaStream_t s) {
+    launch_qgemm_tc(act_map(X, rows_cap, a.W.k, a.box_rows, qgemm_tc_unit(a)), a, sm_count, s);
   }
   static int box_for(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
 
@@ -186,7 +189,7 @@ struct Session {
     a.Y = Y;
     a.ldy = ldy;
     a.err = err.p;
-    launch_qgemm_tc(act_map(X, rows_cap, W.k, a.box_rows), a, sm_count, s);
+    launch_tc(X, rows_cap, a, s);
     return splits;
   }
   PinBuf<uint8_t> staging;
@@ -728,7 +731,7 @@ struct Session {
     gu.ldyb = d.I;
     gu.err = err.p;
     const int a_cap = max_tokens * (d.top + 1);
-    launch_qgemm_tc(act_map(xperm.p, a_cap, d.H, box), gu, sm_count, s);
+    launch_tc(xperm.p, a_cap, gu, s);
     stage(12);  // MoeDown
     TcArgs dn;
     dn.W = ly.expert_dn;
@@ -740,7 +743,7 @@ struct Session {
     dn.Y = moe_y.p;
     dn.ldy = d.H;
     dn.err = err.p;
-    launch_qgemm_tc(act_map(act.p, a_cap, d.I, box), dn, sm_count, s);
+    launch_tc(act.p, a_cap, dn, s);
   }
 };
 
