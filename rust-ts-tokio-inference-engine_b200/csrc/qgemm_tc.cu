@@ -5,20 +5,24 @@
 // Weight rows are the MMA's M dimension (128 per tile), tokens are N (16..128),
 // so the tiny token counts of decode (1-10 rows per expert) cost one N=16 MMA.
 // Per CTA (persistent, one per SM), warp-specialised:
-//   warp 0  producer: cp.async.bulk of each 4608-byte weight tile and a TMA
-//           (128B-swizzled) load of the matching 64-column activation tile into
-//           an S-stage shared-memory ring (mbarrier complete_tx);
+//   warp 0  weight producer: one cp.async.bulk per unit of U contiguous
+//           4608-byte weight tiles into a deep ring (kWSlots units) that the
+//           dequant warps release as soon as they have read it, so HBM reads
+//           run far ahead of the tensor cores;
+//   warp 2  activation producer: one 3-D TMA per unit (U 64-column tiles,
+//           128B-swizzled) into a ring tied to the TMEM stages (released by the
+//           MMA commit; the activations are L2-resident);
 //   warp 1  MMA issuer (converged warp, one elected lane issues): allocates
 //           TMEM and works in units of U (= 4, 2 or 1) chunks: one mbarrier
 //           wait, 4U tcgen05.mma (A from TMEM, B from shared memory) and one
 //           tcgen05.commit per unit. Measured on B200, an MMA issue costs ~26
 //           cycles, an mbarrier wait ~80 and a commit ~200 unless ~16 MMAs
 //           separate commits, so units amortise the fixed costs;
-//   warps 2-13 dequantise (three warpgroups taking whole units round-robin):
+//   warps 3-14 dequantise (three warpgroups taking whole units round-robin):
 //           each thread owns one weight row, turns its 64 nibbles per chunk
 //           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
 //           them into TMEM with tcgen05.st (the A operand);
-//   warps 14-17 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
+//   warps 15-18 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
 //           partial store / SwiGLU (bf16) / fp32 store.
 // The dequantised weights never touch shared memory. Stage i of the
 // shared-memory ring pairs with TMEM A stage i; a unit's stages are released
@@ -39,7 +43,8 @@ extern std::atomic<uint64_t> g_kernel_launches;
 namespace {
 
 constexpr int kDequantGroups = 3;    // dequant warpgroups, round-robin over units
-constexpr int kEpiWarp0 = 2 + 4 * kDequantGroups;  // first warp of the epilogue warpgroup
+constexpr int kWSlots = 6;           // weight ring depth (units); a multiple of kDequantGroups
+constexpr int kEpiWarp0 = 3 + 4 * kDequantGroups;  // first warp of the epilogue warpgroup
 constexpr int kWarps = kEpiWarp0 + 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 12;       // shared-memory ring = TMEM A stages (32 columns each)
@@ -253,23 +258,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // carve: [B ring (1024-aligned)] [W ring] [exchange] [barriers]
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = a.stages;         // ring depth in chunks (multiple of U)
+  const int S = a.stages;         // TMEM A stages = B ring depth in chunks (multiple of U)
   const int U = a.unit;           // chunks per unit (4, 2 or 1)
   const int ushift = U == 4 ? 2 : (U == 2 ? 1 : 0);
-  const int NS = S / U;           // unit slots
+  const int NS = S / U;           // TMEM/B unit slots (multiple of kDequantGroups)
   const int box = a.box_rows;
   const int d_col0 = S * 32;      // accumulators after the A stages
   const int d_stride = box <= 64 ? 64 : 128;
   const uint32_t b_bytes = uint32_t(box) * 128;
+  const uint32_t w_unit = uint32_t(U) * kTileBytes;
   uint8_t* ring_b = base;
   uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
-  float* xchg = reinterpret_cast<float*>(ring_w + size_t(S) * kTileBytes);  // [64][9]
+  float* xchg = reinterpret_cast<float*>(ring_w + size_t(kWSlots) * w_unit);  // [64][9]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * 9);
-  uint64_t* full = bars;                // [NS]  unit's tiles landed (producer tx)
-  uint64_t* a_full = full + NS;         // [NS]  unit's A stages written (4 dequant warps)
-  uint64_t* empty = a_full + NS;        // [NS]  unit consumed by the MMAs (commit)
-  uint64_t* acc_full = empty + NS;      // [2]   accumulator complete (commit)
-  uint64_t* acc_empty = acc_full + 2;   // [2]   accumulator drained (4 epilogue warps)
+  uint64_t* w_full = bars;              // [kWSlots] unit weights landed (tx)
+  uint64_t* w_empty = w_full + kWSlots; // [kWSlots] unit weights read (4 dequant warps)
+  uint64_t* b_full = w_empty + kWSlots; // [NS] unit activations landed (tx)
+  uint64_t* a_full = b_full + NS;       // [NS] unit A stages written (4 dequant warps)
+  uint64_t* empty = a_full + NS;        // [NS] unit consumed by the MMAs (commit)
+  uint64_t* acc_full = empty + NS;      // [2]  accumulator complete (commit)
+  uint64_t* acc_empty = acc_full + 2;   // [2]  accumulator drained (4 epilogue warps)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
   int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
@@ -277,7 +285,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long* const trace = blockIdx.x == 0 ? g_trace : nullptr;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NS; ++i) { mbar_init(&full[i], 1); mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < kWSlots; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
+    for (int i = 0; i < NS; ++i) { mbar_init(&b_full[i], 1); mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -296,24 +305,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total = n_items(a);
 
   if (warp == 0) {
-    // ---------------- producer (converged warp, elected lane issues) ----------------
-    // one bulk copy of the unit's U contiguous weight tiles and one 3-D TMA of
-    // its U activation tiles ([U][box rows][64 columns], 128B-swizzled)
-    int st = 0;
-    uint32_t ph = 0, it = 0;
+    // ---------------- weight producer ----------------
+    int ws = 0;
+    uint32_t wph = 0, it = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
         for (int c = w.c0; c < w.c1; c += U, it += U) {
+          if (!mbar_wait(&w_empty[ws], wph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          if (elect_one()) {
+            QTRACE(0, it);
+            mbar_expect_tx(&w_full[ws], w_unit);
+            bulk_load(ring_w + size_t(ws) * w_unit, a.W.tile(w.rt, c), w_unit, &w_full[ws]);
+          }
+          __syncwarp();
+          if (++ws == kWSlots) { ws = 0; wph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------- activation producer ----------------
+    int st = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
+      const Work w = item_at(a, i, goff);
+      if (!w.valid) continue;
+      for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
+        for (int c = w.c0; c < w.c1; c += U) {
           const int slot = st >> ushift;
           if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
           if (elect_one()) {
-            QTRACE(0, it);
-            mbar_expect_tx(&full[slot], uint32_t(U) * (kTileBytes + b_bytes));
-            bulk_load(ring_w + size_t(st) * kTileBytes, a.W.tile(w.rt, c), uint32_t(U) * kTileBytes, &full[slot]);
-            tma_load_3d(ring_b + size_t(st) * b_bytes, &bmap, 0, a.b_row0 + tb, c, &full[slot]);
+            mbar_expect_tx(&b_full[slot], uint32_t(U) * b_bytes);
+            tma_load_3d(ring_b + size_t(st) * b_bytes, &bmap, 0, a.b_row0 + tb, c, &b_full[slot]);
           }
           __syncwarp();
           st += U;
@@ -337,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem + d_col0 + d * d_stride;
         for (int c = w.c0; c < w.c1; c += U) {
           const int slot = st >> ushift;
+          if (!mbar_wait(&b_full[slot], ph, abort_flag, a.err)) { ok = false; break; }
           if (!mbar_wait(&a_full[slot], ph, abort_flag, a.err)) { ok = false; break; }
           tc_fence_after();
           if (elect_one()) {
@@ -360,13 +387,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < kEpiWarp0) {
-    // ---------------- dequantise (warps 2..13), whole units round-robin ----------------
-    const int wg = (warp - 2) >> 2;
+    // ---------------- dequantise (warps 3..14), whole units round-robin ----------------
+    const int wg = (warp - 3) >> 2;
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    int st = 0, turn = 0;
-    uint32_t ph = 0, it = 0;
+    int st = 0, ws = 0, turn = 0;
+    uint32_t ph = 0, wph = 0, it = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff);
@@ -375,13 +402,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = w.c0; c < w.c1; c += U) {
           if (turn == wg) {
             const int slot = st >> ushift;
+            if (!mbar_wait(&w_full[ws], wph, abort_flag, a.err)) { ok = false; break; }
+            if (quad == 0 && lane == 0) QTRACE(1, it);
             // the MMAs that read these TMEM stages last round must be done
             if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
-            if (!mbar_wait(&full[slot], ph, abort_flag, a.err)) { ok = false; break; }
             tc_fence_after();
-            if (quad == 0 && lane == 0) QTRACE(1, it);
             for (int u = 0; u < U; ++u) {
-              const uint8_t* tile = ring_w + size_t(st + u) * kTileBytes;
+              const uint8_t* tile = ring_w + size_t(ws) * w_unit + size_t(u) * kTileBytes;
               const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
               const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
               const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
@@ -401,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #undef QWEN_DEQ_WORD
               tmem_st32(tmem + lane_addr + (st + u) * 32, v);
             }
-            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_empty[ws]);  // weights read: the producer may refill
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -412,11 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           it += U;
           st += U;
           if (st == S) { st = 0; ph ^= 1; }
+          if (++ws == kWSlots) { ws = 0; wph ^= 1; }
         }
       }
     }
   } else {
-    // ---------------- epilogue (warps 14..17) ----------------
+    // ---------------- epilogue (warps 15..18) ----------------
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
@@ -487,9 +516,9 @@ void qgemm_tc_set_trace(unsigned long long* buf) {
   QWEN_CUDA(cudaMemcpyToSymbol(g_trace, &buf, sizeof(buf)));
 }
 
-size_t qgemm_tc_smem(int box_rows, int stages) {
-  return 1024 + size_t(stages) * (size_t(box_rows) * 128 + kTileBytes) + 64 * 9 * 4 +
-         (3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
+size_t qgemm_tc_smem(int box_rows, int stages, int unit) {
+  return 1024 + size_t(stages) * size_t(box_rows) * 128 + size_t(kWSlots) * unit * kTileBytes + 64 * 9 * 4 +
+         (2 * size_t(kWSlots) + 3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
 }
 
 // Ring depth (chunks): A stages (32 TMEM columns each) plus two accumulators
@@ -517,7 +546,7 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   a.stages = qgemm_tc_stages(a.box_rows);
   a.unit = qgemm_tc_unit(a);  // largest of 4, 2, 1 dividing the items and the ring (slots % groups == 0)
   if ((a.stages / a.unit) % kDequantGroups) throw std::logic_error("GEMM unit slots not a multiple of warpgroups");
-  const size_t smem = qgemm_tc_smem(a.box_rows, a.stages);
+  const size_t smem = qgemm_tc_smem(a.box_rows, a.stages, a.unit);
   static bool configured = false;
   if (!configured) {
     QWEN_CUDA(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));

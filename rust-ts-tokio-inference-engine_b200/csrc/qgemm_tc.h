@@ -43,7 +43,7 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
                             int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
-size_t qgemm_tc_smem(int box_rows, int stages);
+size_t qgemm_tc_smem(int box_rows, int stages, int unit);
 void qgemm_tc_set_trace(unsigned long long* buf);
 const void* g_trace_sym();
 int qgemm_tc_stages(int box_rows);
