@@ -1,7 +1,10 @@
 // Paged GQA attention for decode and chunked prefill (flash-decoding).
 //
-// CTA = (KV split, kv head g, query token t), 4 warps. The split's 16-token
-// pages are dealt round-robin to the warps; each warp streams its pages
+// CTA = (work item, kv head g), 4 warps. A work item is one (query token t,
+// KV split) pair from a host-built list holding only the splits that token
+// attends, so no CTA is launched for keys beyond a token's position; a split
+// covers `split_pages` consecutive 16-token pages (chosen per step). The
+// split's pages are dealt round-robin to the warps; each warp streams its pages
 // through a private 2-stage shared-memory ring filled by TMA (one 128B-swizzled
 // 16x64 box per 64 head dims, K and V), computes S = Q K^T and O += P V with
 // mma.sync (bf16 operands, fp32 accumulators; the G query heads of kv head g are
@@ -23,7 +26,6 @@ extern std::atomic<uint64_t> g_kernel_launches;
 namespace {
 
 constexpr int kAttnWarps = 4;
-constexpr int kPagesPerSplit = 16;  // 256 keys per split
 constexpr int kKvStages = 2;
 constexpr long long kAttnWaitCycles = 2000000000ll;
 
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     attn_decode_kernel(const __grid_constant__ CUtensorMap kvmap, const float* __restrict__ q,
                        const int32_t* __restrict__ token_seq, const int32_t* __restrict__ token_pos,
                        const SeqDesc* __restrict__ descs, const int32_t* __restrict__ block_table, int stride,
-                       int Hq, int Hkv, int G, int max_splits, float* __restrict__ ws, uint32_t* err) {
+                       const int2* __restrict__ items, int split_pages, int Hq, int Hkv, int G, int max_splits,
+                       float* __restrict__ ws, uint32_t* err) {
   constexpr int KS = D / 16;     // k-steps of Q K^T
   constexpr int NT = D / 8;      // n-tiles of O
   constexpr int TILE = 16 * D * 2;  // bytes of one 16-row tile
@@ -117,13 +120,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   float* obuf = red + kAttnWarps * 16 * 2;                 // [16][D] merge buffer
   uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + 16 * D);  // [warps][stages]
 
-  const int split = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
+  const int2 item = items[blockIdx.x];
+  const int t = item.x, split = item.y, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = token_pos[t] + 1;
   const int n_pages = (len + kPageTokens - 1) / kPageTokens;
-  const int p0 = split * kPagesPerSplit;
-  if (p0 >= n_pages) return;
-  const int p1 = min(n_pages, p0 + kPagesPerSplit);
+  const int p0 = split * split_pages;
+  if (p0 >= n_pages || split >= max_splits) return;
+  const int p1 = min(n_pages, p0 + split_pages);
   const int32_t* row = block_table + size_t(descs[token_seq[t]].child) * stride;
 
   // Q tile: rows 0..G-1 = heads g*G.., scaled by log2(e)/sqrt(D); rows >= G zero.
@@ -290,18 +294,17 @@ size_t attn_decode_smem(int D) {
          kAttnWarps * kKvStages * 8;
 }
 
-int attn_pages_per_split() { return kPagesPerSplit; }
-
 CUtensorMap make_kv_map(const KvPool& kv, int layer);
 
 void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_seq,
                         const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
-                        int T, int max_len, float* ws, int max_splits, uint32_t* err, cudaStream_t s) {
+                        const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
+                        cudaStream_t s) {
   const int G = d.Hq / d.Hkv;
   if (G > 16) throw std::invalid_argument("attention kernel supports up to 16 query heads per KV head");
-  const int splits = (max_len + kPagesPerSplit * kPageTokens - 1) / (kPagesPerSplit * kPageTokens);
-  if (splits > max_splits) throw std::invalid_argument("attention split workspace too small");
-  dim3 grid(splits, d.Hkv, T);
+  if (n_items <= 0) return;
+  if (split_pages < 1) throw std::invalid_argument("attention split must cover at least one page");
+  dim3 grid(n_items, d.Hkv);
   const size_t smem = attn_decode_smem(d.D);
 #define QWEN_ATTN(DD)                                                                                         \
   if (d.D == DD) {                                                                                          \
@@ -312,8 +315,8 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
       cfg = true;                                                                                           \
     }                                                                                                       \
     attn_decode_kernel<DD><<<grid, kAttnWarps * 32, smem, s>>>(kvmap, q, token_seq, token_pos, descs,      \
-                                                               block_table, bt_stride, d.Hq, d.Hkv, G,      \
-                                                               max_splits, ws, err);                        \
+                                                               block_table, bt_stride, items, split_pages,  \
+                                                               d.Hq, d.Hkv, G, max_splits, ws, err);        \
     QWEN_CUDA(cudaGetLastError());                                                                          \
     g_kernel_launches.fetch_add(1, std::memory_order_relaxed);                                              \
     return;                                                                                                 \

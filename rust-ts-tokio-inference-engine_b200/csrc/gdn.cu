@@ -1,0 +1,245 @@
+// Gated-DeltaNet mixer (native/qwen_model.inc:154-206, native/operator_reference.h:19-45)
+// as two kernels per layer:
+//
+//  gdn_prep:   CTA = (sequence, key head). Causal depthwise conv1d (K taps,
+//              tap 0 oldest) over [conv history; new qkv rows] + SiLU for the key
+//              head's q/k channels and its value heads' v channels; q and k
+//              RMS-normalised and scaled (q/dk, k/sqrt(dk)); decay
+//              g = exp(-exp(A_log) * softplus(a + dt_bias)) and beta = sigmoid(b).
+//              Each channel is owned by one thread, which reads the parent's
+//              conv history before writing the child's, so the update is safe
+//              in place (consumed parents).
+//  gdn_update: CTA = (sequence, value head), 8 warps. The head's fp32 state
+//              S[dv][dk] stays in registers for the step (warp w owns rows
+//              [w*dv/8, (w+1)*dv/8), lane l columns [l*dk/32, ...), loaded and
+//              stored as 16-byte vectors); per token S *= g; m = S k;
+//              delta = beta (v - m); S += delta k^T; o = S q; then the gated
+//              RMSNorm y = rms(o) * w * silu(z) is written as bf16.
+// The state read + write (2 x 64 KiB per head for dk = dv = 128) is the
+// HBM traffic that bounds the layer.
+#include <atomic>
+
+#include "kernels.h"
+
+namespace qwen {
+
+extern std::atomic<uint64_t> g_kernel_launches;
+
+namespace {
+
+template <int DK, int DV, int R>
+__global__ void __launch_bounds__(2 * DK + R * DV)
+    gdn_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
+                    const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
+                    int hk, int hv, int conv, const float* __restrict__ conv_w, const float* __restrict__ a_log,
+                    const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
+                    float* __restrict__ gb_out) {
+  constexpr int NC = 2 * DK + R * DV;
+  __shared__ float qs[DK], ks[DK];
+  __shared__ float qk_scale[2];
+  const int seq = blockIdx.x, kh = blockIdx.y;
+  const SeqDesc d = descs[seq];
+  const int t0 = cu_seqlens[seq];
+  const int kd = hk * DK, vd = hv * DV, cd = 2 * kd + vd;
+  const int c = threadIdx.x, lane = threadIdx.x & 31;
+  const int gc = c < DK ? kh * DK + c : (c < 2 * DK ? kd + kh * DK + (c - DK) : 2 * kd + kh * R * DV + (c - 2 * DK));
+  const size_t cl = size_t(conv - 1) * cd;
+  const float* src_conv = d.parent >= 0 ? pool.conv + (size_t(d.parent) * pool.n_gdn + li) * cl : nullptr;
+  float* dst_conv = pool.conv + (size_t(d.child) * pool.n_gdn + li) * cl;
+  // taps[j] = input j+1 steps before the newest tap; indices stay static so
+  // both arrays live in registers (conv <= 8).
+  float taps[7], cw[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cw[j] = j < conv ? conv_w[size_t(gc) * conv + j] : 0.f;
+#pragma unroll
+  for (int j = 0; j < 7; ++j) taps[j] = (j < conv - 1 && src_conv) ? src_conv[size_t(j) * cd + gc] : 0.f;
+  float cw_last = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (j == conv - 1) cw_last = cw[j];
+  auto P = [&](const float* pr, int col) {
+    float v = pr[col];
+    for (int s = 1; s < splits; ++s) v += pr[s * split_stride + col];
+    return v;
+  };
+  for (int i = 0; i < d.count; ++i) {
+    const int t = t0 + i;
+    const float* pr = proj + size_t(t) * ld;
+    const float cur = P(pr, gc);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 7; ++j)
+      if (j < conv - 1) acc += taps[j] * cw[j];
+    acc += cur * cw_last;
+#pragma unroll
+    for (int j = 0; j < 7; ++j)
+      if (j < conv - 1) taps[j] = j + 1 < conv - 1 ? taps[j + 1] : cur;
+    const float act = siluf_(acc);
+    if (c < DK) qs[c] = act;
+    else if (c < 2 * DK) ks[c - DK] = act;
+    else v_out[size_t(t) * vd + kh * R * DV + (c - 2 * DK)] = act;
+    if (c < R) {
+      const int h = kh * R + c;
+      const float av = P(pr, cd + vd + h) + dt_bias[h];
+      const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
+      gb_out[(size_t(t) * hv + h) * 2 + 0] = expf(-expf(a_log[h]) * sp);
+      gb_out[(size_t(t) * hv + h) * 2 + 1] = sigmoidf_(P(pr, cd + vd + hv + h));
+    }
+    __syncthreads();
+    if (c < 64) {  // warps 0/1: q / k inverse RMS, folded with the 1/dk and 1/sqrt(dk) scales
+      const float* v = c < 32 ? qs : ks;
+      float ss = 0.f;
+      for (int j = lane; j < DK; j += 32) ss += v[j] * v[j];
+      ss = warp_sum(ss);
+      if (lane == 0) {
+        const float rinv = rsqrtf(ss / DK + 1e-6f);
+        qk_scale[c >> 5] = c < 32 ? rinv / DK : rinv * rsqrtf(float(DK));
+      }
+    }
+    __syncthreads();
+    if (c < 2 * DK) {
+      float* dst = qk_out + ((size_t(t) * hk + kh) * 2) * DK;
+      if (c < DK) dst[c] = qs[c] * qk_scale[0];
+      else dst[DK + (c - DK)] = ks[c - DK] * qk_scale[1];
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 7; ++j)
+    if (j < conv - 1) dst_conv[size_t(j) * cd + gc] = taps[j];
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(256)
+    gdn_update_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
+                      int hk, int hv, const float* __restrict__ qk, const float* __restrict__ vv,
+                      const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
+                      size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
+                      __nv_bfloat16* __restrict__ out, uint32_t* err) {
+  constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
+  constexpr int RPW = DV / 8;   // rows per warp
+  using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
+  __shared__ float os[DV];
+  __shared__ float red[8];
+  const int seq = blockIdx.x, head = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const SeqDesc d = descs[seq];
+  const int t0 = cu_seqlens[seq];
+  const int kh = head / (hv / hk);
+  const int vd = hv * DV;
+  const size_t sl = size_t(hv) * DV * DK;
+  const float* src = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl + size_t(head) * DV * DK
+                                   : nullptr;
+  float* dst = pool.state + (size_t(d.child) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
+  float S[RPW][CPL];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int r = warp * RPW + i;
+    if (src) {
+      const Vec v = *reinterpret_cast<const Vec*>(src + size_t(r) * DK + lane * CPL);
+      const float* f = reinterpret_cast<const float*>(&v);
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) S[i][j] = f[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) S[i][j] = 0.f;
+    }
+  }
+  for (int it = 0; it < d.count; ++it) {
+    const int t = t0 + it;
+    const float* qkt = qk + ((size_t(t) * hk + kh) * 2) * DK;
+    float qq[CPL], kq[CPL];
+    {
+      const Vec qv = *reinterpret_cast<const Vec*>(qkt + lane * CPL);
+      const Vec kv = *reinterpret_cast<const Vec*>(qkt + DK + lane * CPL);
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        qq[j] = reinterpret_cast<const float*>(&qv)[j];
+        kq[j] = reinterpret_cast<const float*>(&kv)[j];
+      }
+    }
+    const float g = gb[(size_t(t) * hv + head) * 2], beta = gb[(size_t(t) * hv + head) * 2 + 1];
+    const float* vt = vv + size_t(t) * vd + head * DV;
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) {
+      const int r = warp * RPW + i;
+      float mem = 0.f;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        S[i][j] *= g;
+        mem += S[i][j] * kq[j];
+      }
+      mem = warp_sum(mem);
+      const float delta = (vt[r] - mem) * beta;
+      float rd = 0.f;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        S[i][j] += delta * kq[j];
+        rd += S[i][j] * qq[j];
+      }
+      rd = warp_sum(rd);
+      if (lane == 0) os[r] = rd;
+    }
+    __syncthreads();
+    // gated RMSNorm over dv (native/qwen_model.inc:203-204)
+    float o = threadIdx.x < DV ? os[threadIdx.x] : 0.f;
+    float ss = warp_sum(o * o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x < DV) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) tot += red[w];
+      const float* pr = proj + size_t(t) * ld + cd + head * DV + threadIdx.x;
+      float z = pr[0];
+      for (int sp = 1; sp < splits; ++sp) z += pr[sp * split_stride];
+      const float y = o * rsqrtf(tot / DV + eps) * gnorm[threadIdx.x] * siluf_(z);
+      out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
+    }
+    __syncthreads();
+  }
+  bool finite = true;
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int r = warp * RPW + i;
+    Vec v;
+    float* f = reinterpret_cast<float*>(&v);
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      f[j] = S[i][j];
+      finite &= isfinite(S[i][j]);
+    }
+    *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = v;
+  }
+  if (!finite) atomicOr(err, kErrNonFinite);
+}
+
+}  // namespace
+
+void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
+                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool, int gdn_index,
+                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, cudaStream_t s) {
+  const int R = d.hv / d.hk;
+  if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
+  bool done = false;
+#define QWEN_GDN(DK_, DV_, R_)                                                                                    \
+  if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \
+    gdn_prep_kernel<DK_, DV_, R_><<<dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s>>>(                              \
+        proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
+        ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf);                                                            \
+    gdn_update_kernel<DK_, DV_><<<dim3(n_seq, d.hv), 256, 0, s>>>(descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
+                                                                qk_buf, v_buf, gb_buf, proj, ld_proj, splits,    \
+                                                                split_stride, d.cd, ly.gnorm, d.eps, out, err);  \
+    done = true;                                                                                                 \
+  }
+  QWEN_GDN(128, 128, 2)
+  QWEN_GDN(64, 64, 2)
+  QWEN_GDN(128, 128, 1)
+  QWEN_GDN(64, 64, 1)
+#undef QWEN_GDN
+  if (!done) throw std::invalid_argument("DeltaNet geometry unsupported (dk = dv in {64,128}, hv/hk in {1,2})");
+  QWEN_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(2, std::memory_order_relaxed);
+}
+
+}  // namespace qwen

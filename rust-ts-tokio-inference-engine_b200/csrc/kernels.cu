@@ -169,169 +169,6 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
   }
 }
 
-// ------------------------------------------------------------ Gated-DeltaNet --
-// One CTA per (sequence, key head); R = hv/hk value heads share the key head,
-// 256 threads per value head. Each value head's state S[dv][dk] (fp32) lives
-// in registers for the whole step: warp w owns rows [w*DV/8, (w+1)*DV/8),
-// lane l owns columns [l*DK/32, (l+1)*DK/32). Tokens of the sequence are
-// processed in order (native/operator_reference.h:28-41):
-//   conv1d(K) + SiLU over [conv_state; qkv]  ->  q = rms(q)/dk, k = rms(k)/sqrt(dk)
-//   S *= g; m = S.k; delta = beta*(v - m); S += delta (x) k; o = S.q
-//   y = rms(o, norm.weight) * silu(z)   (native/qwen_model.inc:203-204)
-template <int DK, int DV, int R>
-__global__ void __launch_bounds__(256 * R) gdn_kernel(
-    const float* __restrict__ proj, int ld, int splits, size_t split_stride,
-    const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
-    int hk, int hv, int conv,
-    float eps, const float* __restrict__ conv_w, const float* __restrict__ a_log,
-    const float* __restrict__ dt_bias, const float* __restrict__ gnorm, __nv_bfloat16* out,
-    uint32_t* err) {
-  constexpr int CPL = DK / 32;  // columns per lane
-  constexpr int RPW = DV / 8;   // rows per warp
-  constexpr int NC = 2 * DK + R * DV;
-  __shared__ float qs[DK], ks[DK], vs[R * DV], os[R * DV];
-  __shared__ float red[2][R * 8];
-  __shared__ float gs[R], bs[R], qk_scale[2];
-  const int seq = blockIdx.x, kh = blockIdx.y;
-  const SeqDesc d = descs[seq];
-  const int t0 = cu_seqlens[seq];
-  const int kd = hk * DK, vd = hv * DV, cd = 2 * kd + vd;
-  const int grp = threadIdx.x / 256, tig = threadIdx.x % 256;
-  const int warp = tig >> 5, lane = tig & 31;
-  const int head = kh * R + grp;
-  const size_t sl = size_t(hv) * DV * DK;  // state elems per layer per slot
-  const float* src_state = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl : nullptr;
-  float* dst_state = pool.state + (size_t(d.child) * pool.n_gdn + li) * sl;
-  const size_t cl = size_t(conv - 1) * cd;
-  const float* src_conv = d.parent >= 0 ? pool.conv + (size_t(d.parent) * pool.n_gdn + li) * cl : nullptr;
-  float* dst_conv = pool.conv + (size_t(d.child) * pool.n_gdn + li) * cl;
-
-  // conv channel owned by this thread (one per thread; NC <= blockDim)
-  int gc = -1;
-  if (threadIdx.x < NC) {
-    const int c = threadIdx.x;
-    gc = c < DK ? kh * DK + c : (c < 2 * DK ? kd + kh * DK + (c - DK) : 2 * kd + kh * R * DV + (c - 2 * DK));
-  }
-  float taps[8];
-  float cw[8];
-  if (gc >= 0) {
-    for (int j = 0; j < conv; ++j) cw[j] = conv_w[size_t(gc) * conv + j];
-    for (int j = 0; j < conv - 1; ++j) taps[j] = src_conv ? src_conv[size_t(j) * cd + gc] : 0.f;
-  }
-
-  float S[RPW][CPL];
-  {
-    const float* base = src_state ? src_state + size_t(head) * DV * DK : nullptr;
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int r = warp * RPW + i;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) S[i][j] = base ? base[size_t(r) * DK + lane * CPL + j] : 0.f;
-    }
-  }
-
-  auto P = [&](const float* pr, int col) {
-    float v = pr[col];
-    for (int s = 1; s < splits; ++s) v += pr[s * split_stride + col];
-    return v;
-  };
-  for (int i = 0; i < d.count; ++i) {
-    const int t = t0 + i;
-    const float* pr = proj + size_t(t) * ld;
-    if (gc >= 0) {
-      const float cur = P(pr, gc);
-      float acc = 0.f;
-      for (int j = 0; j < conv - 1; ++j) acc += taps[j] * cw[j];
-      acc += cur * cw[conv - 1];
-      for (int j = 0; j < conv - 2; ++j) taps[j] = taps[j + 1];
-      taps[conv - 2] = cur;
-      const float a = siluf_(acc);
-      const int c = threadIdx.x;
-      if (c < DK) qs[c] = a;
-      else if (c < 2 * DK) ks[c - DK] = a;
-      else vs[c - 2 * DK] = a;
-    }
-    if (threadIdx.x < R) {
-      const int h = kh * R + threadIdx.x;
-      const float av = P(pr, cd + vd + h) + dt_bias[h];
-      const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
-      gs[threadIdx.x] = expf(-expf(a_log[h]) * sp);
-      bs[threadIdx.x] = sigmoidf_(P(pr, cd + vd + hv + h));
-    }
-    __syncthreads();
-    if (threadIdx.x < 64) {  // warps 0/1: squared norms of q / k
-      const float* v = threadIdx.x < 32 ? qs : ks;
-      float ss = 0.f;
-      for (int j = lane; j < DK; j += 32) ss += v[j] * v[j];
-      ss = warp_sum(ss);
-      if (lane == 0) {
-        const float rinv = rsqrtf(ss / DK + 1e-6f);
-        qk_scale[threadIdx.x >> 5] = threadIdx.x < 32 ? rinv / DK : rinv * rsqrtf(float(DK));
-      }
-    }
-    __syncthreads();
-    float kq[CPL], qq[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      kq[j] = ks[lane * CPL + j] * qk_scale[1];
-      qq[j] = qs[lane * CPL + j] * qk_scale[0];
-    }
-    const float g = gs[grp], beta = bs[grp];
-#pragma unroll
-    for (int ii = 0; ii < RPW; ++ii) {
-      const int r = warp * RPW + ii;
-      float mem = 0.f;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        S[ii][j] *= g;
-        mem += S[ii][j] * kq[j];
-      }
-      mem = warp_sum(mem);
-      const float delta = (vs[grp * DV + r] - mem) * beta;
-      float rd = 0.f;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        S[ii][j] += delta * kq[j];
-        rd += S[ii][j] * qq[j];
-      }
-      rd = warp_sum(rd);
-      if (lane == 0) os[grp * DV + r] = rd;
-    }
-    __syncthreads();
-    // gated RMSNorm per value head over dv
-    {
-      const float o = tig < DV ? os[grp * DV + tig] : 0.f;
-      float ss = warp_sum(o * o);
-      if (lane == 0) red[0][grp * 8 + warp] = ss;
-      __syncthreads();
-      if (tig < DV) {
-        float tot = 0.f;
-        for (int w = 0; w < 8; ++w) tot += red[0][grp * 8 + w];
-        const float z = P(pr, cd + head * DV + tig);
-        const float y = o * rsqrtf(tot / DV + eps) * gnorm[tig] * siluf_(z);
-        out[size_t(t) * vd + head * DV + tig] = __float2bfloat16_rn(y);
-      }
-    }
-    __syncthreads();
-  }
-  // publish the child state
-  bool finite = true;
-  {
-    float* base = dst_state + size_t(head) * DV * DK;
-#pragma unroll
-    for (int i = 0; i < RPW; ++i) {
-      const int r = warp * RPW + i;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        finite &= isfinite(S[i][j]);
-        base[size_t(r) * DK + lane * CPL + j] = S[i][j];
-      }
-    }
-  }
-  if (gc >= 0)
-    for (int j = 0; j < conv - 1; ++j) dst_conv[size_t(j) * cd + gc] = taps[j];
-  if (!finite) atomicOr(err, kErrNonFinite);
-}
 
 // ----------------------------------------------------------------- attention --
 // Per token: q/k RMSNorm (q_norm/k_norm), partial rotate-half RoPE on the
@@ -734,29 +571,6 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
   count_launch();
 }
 
-void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
-                size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
-                int gdn_index, __nv_bfloat16* out, uint32_t* err, cudaStream_t s) {
-  const int R = d.hv / d.hk;
-  if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
-  dim3 grid(n_seq, d.hk);
-#define QWEN_GDN(DK_, DV_, R_)                                                                    \
-  if (d.dk == DK_ && d.dv == DV_ && R == R_) {                                                   \
-    gdn_kernel<DK_, DV_, R_><<<grid, 256 * R_, 0, s>>>(proj, ld_proj, splits, split_stride, descs, \
-                                                       cu_seqlens, pool,                         \
-                                                       gdn_index, d.hk, d.hv, d.conv, d.eps,     \
-                                                       ly.conv_w, ly.a_log, ly.dt_bias, ly.gnorm, \
-                                                       out, err);      \
-    count_launch();                                                                               \
-    return;                                                                                       \
-  }
-  QWEN_GDN(128, 128, 2)
-  QWEN_GDN(64, 64, 2)
-  QWEN_GDN(128, 128, 1)
-  QWEN_GDN(64, 64, 1)
-#undef QWEN_GDN
-  throw std::invalid_argument("DeltaNet geometry unsupported (dk = dv in {64,128}, hv/hk in {1,2})");
-}
 
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
@@ -768,15 +582,11 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
   count_launch();
 }
 
-static constexpr int kSplitTokens = 256;
-
-int attention_max_splits(int ctx) { return (ctx + kSplitTokens - 1) / kSplitTokens; }
-
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int max_splits, __nv_bfloat16* out, cudaStream_t s) {
+                            int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s) {
   if (T <= 0) return;
-  attention_merge_kernel<<<dim3(T, d.Hq), 128, 0, s>>>(ws, gate, token_pos, d.Hq, d.D, kSplitTokens, max_splits,
-                                                       out);
+  attention_merge_kernel<<<dim3(T, d.Hq), 128, 0, s>>>(ws, gate, token_pos, d.Hq, d.D, split_pages * kPageTokens,
+                                                       max_splits, out);
   count_launch();
 }
 

@@ -90,7 +90,8 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
 void launch_qgemm(const GemmArgs& a, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                 size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
-                int gdn_index, __nv_bfloat16* out, uint32_t* err, cudaStream_t s);
+                int gdn_index, __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
+                cudaStream_t s);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);

@@ -39,9 +39,10 @@ int qgemm_tc_unit(const TcArgs& a);
 CUtensorMap make_kv_map(const KvPool& kv, int layer);
 void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_seq,
                         const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
-                        int T, int max_len, float* ws, int max_splits, uint32_t* err, cudaStream_t s);
+                        const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
+                        cudaStream_t s);
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int max_splits, __nv_bfloat16* out, cudaStream_t s);
+                            int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
 size_t qgemm_tc_smem(int box_rows, int stages, int unit);
 void qgemm_tc_set_trace(unsigned long long* buf);

@@ -140,6 +140,9 @@ struct Session {
   DevBuf<int64_t> slot_mapping;
   DevBuf<uint32_t> tokens, sampled, err;
   DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
+  DevBuf<float> gdn_qk, gdn_v, gdn_gb;  // DeltaNet prepared q/k, v, (decay, beta) per token
+  DevBuf<int2> attn_items;              // attention work list: (token, KV split) pairs
+  int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
   DevBuf<unsigned long long> trace_buf;
   int sm_count = 148;
@@ -338,6 +341,9 @@ struct Session {
     const int hbw = std::max({d.H, d.vd, d.Hq * d.D});
     hb.ensure(size_t(T) * hbw);
     hb2.ensure(size_t(T) * hbw);
+    gdn_qk.ensure(size_t(T) * std::max(1, d.hk * 2 * d.dk));
+    gdn_v.ensure(size_t(T) * std::max(1, d.vd));
+    gdn_gb.ensure(size_t(T) * std::max(1, d.hv * 2));
     q.ensure(size_t(T) * d.Hq * d.D);
     gate.ensure(size_t(T) * d.Hq * d.D);
     ids.ensure(A);
@@ -422,6 +428,27 @@ struct Session {
       max_len = std::max<int>(max_len, int(s.position + s.count));
     }
     if (T > max_tokens) throw std::invalid_argument("ragged step exceeds the token budget");
+    // Attention work list. A split spans enough pages to amortise its CTA's
+    // query load and warp merge (16..64 pages) while leaving at least four
+    // CTAs per SM; each token gets one item per split its keys reach.
+    std::vector<int2> items;
+    if (d.n_attn > 0) {
+      int64_t page_heads = 0;
+      for (const auto& s : seqs)
+        for (uint32_t j = 0; j < s.count; ++j) page_heads += (int64_t(s.position) + j + kPageTokens) / kPageTokens;
+      page_heads *= d.Hkv;
+      int sp = 16;
+      while (sp < 64 && page_heads / (2 * sp) >= int64_t(sm_count) * 4) sp *= 2;
+      attn_split_pages = sp;
+      attn_splits = std::max(1, (max_len + sp * kPageTokens - 1) / (sp * kPageTokens));
+      int t = 0;
+      for (const auto& s : seqs)
+        for (uint32_t j = 0; j < s.count; ++j, ++t) {
+          const int pages = int((int64_t(s.position) + j + kPageTokens) / kPageTokens);
+          for (int k = 0; k * sp < pages; ++k) items.push_back(make_int2(t, k));
+        }
+      attn_n_items = int(items.size());
+    }
     if (R > max_rows) throw std::invalid_argument("ragged step exceeds the output-row budget");
     // parents must be distinct when consumed
     std::vector<const Version*> par(n, nullptr);
@@ -437,7 +464,7 @@ struct Session {
     if (!consume && table->residents() + size_t(n) > slots) throw std::runtime_error("combined resident budget exhausted");
 
     // page planning (host), descriptors
-    staging.ensure(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64);
+    staging.ensure(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64 + items.size() * 8);
     SeqDesc* hd = reinterpret_cast<SeqDesc*>(staging.p);
     std::vector<int32_t> npages;
     std::vector<std::vector<int32_t>> child_pages(n);
@@ -535,13 +562,19 @@ struct Session {
     std::memcpy(hp, npages.data(), npages.size() * 4);
     uint32_t* ht = reinterpret_cast<uint32_t*>(hp + npages.size());
     for (int i = 0; i < n; ++i) std::memcpy(ht + tok_off[i], seqs[i].tokens, seqs[i].count * 4);
+    int2* hi = reinterpret_cast<int2*>((reinterpret_cast<uintptr_t>(ht + T) + 7) & ~uintptr_t(7));
+    if (!items.empty()) std::memcpy(hi, items.data(), items.size() * 8);
     try {
       QWEN_CUDA(cudaMemcpyAsync(descs.p, hd, sizeof(SeqDesc) * n, cudaMemcpyHostToDevice, stream));
       if (!npages.empty())
         QWEN_CUDA(cudaMemcpyAsync(new_pages.p, hp, npages.size() * 4, cudaMemcpyHostToDevice, stream));
       QWEN_CUDA(cudaMemcpyAsync(tokens.p, ht, size_t(T) * 4, cudaMemcpyHostToDevice, stream));
       QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, stream));
-      uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4;
+      if (!items.empty()) {
+        attn_items.ensure(items.size());
+        QWEN_CUDA(cudaMemcpyAsync(attn_items.p, hi, items.size() * 8, cudaMemcpyHostToDevice, stream));
+      }
+      uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4 + items.size() * 8;
       const uint64_t t_graph = now_ns();
       ev_used = 0;
       ev_marks.clear();
@@ -618,8 +651,7 @@ struct Session {
     if (d.n_attn > 0) launch_cow(kv, descs.p, n, new_pages.p, s);
     launch_embed_norm(m.embed, tokens.p, T, m.layers[0].in_norm, d.eps, x.p, hb.p, s);
     const int slots_per_tok = d.top + 1, A = T * slots_per_tok;
-    const int splits_needed = (max_len + 255) / 256;
-    attn_ws.ensure(size_t(T) * d.Hq * std::max(1, splits_needed) * (d.D + 2));
+    if (d.n_attn > 0) attn_ws.ensure(size_t(T) * d.Hq * attn_splits * (d.D + 2));
     if (capture_routing) {
       capture.ensure(size_t(d.L) * A);
       cap_logits.ensure(size_t(d.L) * T * (d.E + 1));
@@ -638,15 +670,16 @@ struct Session {
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
         launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, gdn, ly.type_index,
-                   hb2.p, err.p, s);
+                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, s);
         stage(5);  // RecurrentOutput
       } else {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
         launch_attn_prep(d, ly, partial.p, proj_w, ps, proj_stride, token_pos.p, slot_mapping.p, T, kv,
                          ly.type_index, q.p, gate.p, s);
         launch_attn_decode(kv_maps[ly.type_index], d, q.p, token_seq.p, token_pos.p, descs.p, block_table.p,
-                           bt_stride, T, max_len, attn_ws.p, std::max(1, splits_needed), err.p, s);
-        launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, std::max(1, splits_needed), hb2.p, s);
+                           bt_stride, attn_items.p, attn_n_items, attn_split_pages, attn_ws.p, attn_splits, err.p,
+                           s);
+        launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, attn_split_pages, attn_splits, hb2.p, s);
         stage(8);  // AttentionOutput
       }
       const size_t out_stride = size_t(T) * d.H;
