@@ -266,6 +266,28 @@ int rs_qwen_device_timing(void* session, double* out, size_t count, char* error,
 int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, size_t T, float* y,
                        size_t y_count, int engine, double* ms, char* error, size_t capacity);
 
+/* Allocation-free dense projection. No counterpart in the reference: it exists
+ * for callers that must not allocate device memory while they run, e.g. a
+ * server that has handed the device to the session's KV page pool and
+ * DeltaNet state slots (the pool takes what the byte budget leaves, so a
+ * later cudaMalloc can fail), or a latency-critical loop where cudaMalloc /
+ * cudaFree would synchronise the device. It allocates nothing, on the device
+ * or the host, when it succeeds.
+ *
+ * y_device (fp32, T x rows, device) = x_device (bf16 bits, T x k, device,
+ * 16-byte aligned) times the selected matrix; `which` and `layer` select it
+ * as in rs_qwen_debug_gemm (tcgen05 engine). The split-K partials live in a
+ * fixed 16 MiB static device array per device, so T x rows may not exceed
+ * 4,194,240 floats; larger calls return -1 with an error naming the limit.
+ * Work is enqueued on `stream` (NULL: the session's stream), and the call
+ * returns once it has finished. The first call on each device resolves the
+ * scratch address (a one-time set-up); make that call before any stream
+ * capture begins. Every call on a device shares the one array: calls that
+ * overlap in time (several host threads, or several sessions on one device)
+ * race and corrupt each other's results, so serialise them. Returns 0/-1. */
+int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_device, size_t T,
+                            float* y_device, size_t y_count, void* stream, char* error, size_t capacity);
+
 /* Number of floats of a version's reference-layout snapshot
  * (native/qwen_model.inc:268-271 qwen_state_count). */
 size_t rs_qwen_state_count(const rs_qwen_config* config);

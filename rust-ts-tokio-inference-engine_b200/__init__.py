@@ -100,6 +100,8 @@ SIGNATURES = {
     "rs_qwen_device_debug_capture": (C.c_int, [_P, C.c_int, C.c_void_p, _SZ, C.POINTER(_SZ), _ERR, _SZ]),
     "rs_qwen_debug_gemm": (C.c_int, [_P, C.c_int, C.c_int, C.POINTER(C.c_uint16), _SZ, _F32P, _SZ, C.c_int,
                                      C.POINTER(C.c_double), _ERR, _SZ]),
+    "rs_qwen_project_noalloc": (C.c_int, [_P, C.c_int, C.c_int, C.c_void_p, _SZ, C.c_void_p, _SZ, C.c_void_p,
+                                          _ERR, _SZ]),
 }
 
 _lib = None
@@ -324,6 +326,14 @@ class DeviceSession:
         _call("rs_qwen_debug_gemm", self.h, which, layer, x.ctypes.data_as(C.POINTER(C.c_uint16)), T,
               _ptr(y, C.c_float), y.size, engine, C.byref(ms))
         return y, ms.value
+
+    def project_noalloc(self, which: int, layer: int, x_device_ptr: int, T: int, y_device_ptr: int, y_count: int,
+                        stream_ptr: int = 0):
+        """Allocation-free dense projection on device buffers (rs_qwen_project_noalloc):
+        y (fp32 [T][rows]) = x (bf16 [T][k]) . W; raises on error, including T x rows
+        beyond the 16 MiB static scratch."""
+        _call("rs_qwen_project_noalloc", self.h, which, layer, C.c_void_p(x_device_ptr), T,
+              C.c_void_p(y_device_ptr), y_count, C.c_void_p(stream_ptr or None))
 
     def debug_capture(self, what: int, dtype=np.int32, capacity: int = 1 << 26):
         """Raw last-step intermediates (see rs_qwen_device_debug_capture)."""

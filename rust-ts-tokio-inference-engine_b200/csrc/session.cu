@@ -19,6 +19,7 @@
 #include <tuple>
 
 #include "kernels.h"
+#include "noalloc.h"
 #include "qgemm_tc.h"
 #include "state_table.h"
 
@@ -1254,6 +1255,33 @@ int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, s
       y[i] = v;
     }
   });
+}
+
+int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_device, size_t T, float* y_device,
+                            size_t y_count, void* stream, char* error, size_t capacity) {
+  if (!session) {
+    report(error, capacity, "no-alloc projection: null session");
+    return -1;
+  }
+  Session* s = static_cast<Session*>(session);
+  if (which < 0 || which > 3 || layer < 0 || layer >= s->d.L) {
+    report(error, capacity, "no-alloc projection: matrix selector or layer out of range");
+    return -1;
+  }
+  const LayerDev& ly = s->store->model.layers[layer];
+  const QMat& W = which == 0 ? ly.in_proj : which == 1 ? ly.out_proj : which == 2 ? ly.router : s->store->model.lm_head;
+  if (T == 0 || T > size_t(INT32_MAX) / size_t(W.rows) || y_count != T * size_t(W.rows)) {
+    report(error, capacity, "no-alloc projection: output capacity must be T x rows of the selected matrix");
+    return -1;
+  }
+  const cudaError_t rc = cudaSetDevice(s->device);
+  if (rc != cudaSuccess) {
+    report(error, capacity, cudaGetErrorString(rc));
+    return -1;
+  }
+  return project_noalloc(W, which == 3 ? 1 : kMaxSplits, static_cast<const __nv_bfloat16*>(x_device), int(T),
+                         y_device, s->sm_count, stream ? static_cast<cudaStream_t>(stream) : s->stream, error,
+                         capacity);
 }
 
 int rs_qwen_device_set_profile(void* session, int profile, char* error, size_t capacity) {
