@@ -19,6 +19,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import re
 import math
 import os
 import statistics
@@ -165,6 +166,21 @@ def barrier(world):
         dist.barrier()
 
 
+# Launches per 48-layer step of each stage's dominant kernel.
+LAUNCHES_PER_STEP = {"MoeUpGate": 48, "MoeDown": 48, "RecurrentUpdate": 36, "AttentionReduction": 12}
+# ncu DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum), read from the committed
+# profile summary of that stage's kernel on the same per-layer shapes.
+PROFILE_FILES = {"MoeUpGate": "qgemm_tc_moe_gateup_cfg1.md", "MoeDown": "qgemm_tc_moe_down_cfg1.md"}
+
+
+def profiled_traffic(stage):
+    f = Path(__file__).resolve().parent / "profiles" / PROFILE_FILES.get(stage, "-")
+    if not f.is_file():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
 def cpu_reference(cfg_kw, ctx, steps, warmup, cores_note=None):
     """The oracle port timed on the host cores: one sequence's decode token
     through a 4-layer slice of the configs[1] model (3 DeltaNet + 1 attention
@@ -256,6 +272,7 @@ def main():
     sess.set_profile(True)
     _, total0, n0, stage0 = sess.timing()
     step_ms = []
+    launches0 = sess.stats()[16]
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
@@ -266,6 +283,7 @@ def main():
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     barrier(world)
+    launches = int(sess.stats()[16] - launches0)
     _, total1, n1, stage1 = sess.timing()
     sess.set_profile(False)
     sess.set_capture(True)
@@ -285,9 +303,6 @@ def main():
     bytes_per, mean_ue = stage_bytes(cfg, ctx, routing)
     dom = max(bytes_per, key=lambda k: stage_ms[STAGES.index(k)])
     dom_ms = stage_ms[STAGES.index(dom)]
-    launches_per_stage = {"RecurrentProjection": 36, "RecurrentUpdate": 36, "RecurrentOutput": 36,
-                          "AttentionProjection": 12, "AttentionReduction": 24, "AttentionOutput": 12,
-                          "MoeRouting": 144, "MoeUpGate": 48, "MoeDown": 48, "FinalProjection": 2}
     achieved = bytes_per[dom] / (dom_ms / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -297,10 +312,11 @@ def main():
         "config": config,
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": N_SEQ * (4 + 48) + N_SEQ * 4,
                 "d2h_bytes_per_step": N_SEQ * 4 + 4},
-        "gpu_launches": None,
+        "gpu_launches": launches,
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None, "peak_source": peak_kind,
-                     "bytes_per_step": bytes_per[dom], "ms_per_step": dom_ms},
+                     "frac": achieved / hbm, "traffic": profiled_traffic(dom), "peak_source": peak_kind,
+                     "bytes_per_step": bytes_per[dom], "ms_per_step": dom_ms,
+                     "algorithmic_bytes_per_launch": bytes_per[dom] / LAUNCHES_PER_STEP.get(dom, 1)},
         "stage_ms": {k: round(v, 4) for k, v in zip(STAGES, stage_ms) if v > 0},
         "stage_gbs": {k: round(bytes_per[k] / (stage_ms[STAGES.index(k)] / 1e3) / 1e9, 1)
                       for k in bytes_per if stage_ms[STAGES.index(k)] > 0},

@@ -1,6 +1,8 @@
-// Decode-step kernels for sm_100a: packing, embedding + norms, the
-// Gated-DeltaNet recurrence, paged GQA attention, MoE routing / sort /
-// combine and greedy selection. The 4-bit grouped GEMM lives in qgemm.cu.
+// Decode-step kernels for sm_100a: packing, embedding + norms, attention
+// prep and split merge, MoE routing / sort / combine and greedy selection.
+// The DeltaNet kernels live in gdn.cu, the paged attention kernel in
+// attention.cu and the 4-bit GEMMs in qgemm_tc.cu (qgemm.cu: CUDA-core
+// reference engine).
 #include <atomic>
 #include <cfloat>
 
@@ -126,45 +128,49 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
                                      size_t split_stride, int H, const float* __restrict__ norm_w,
                                      float eps, __nv_bfloat16* __restrict__ hb,
                                      const int32_t* __restrict__ out_token, float* __restrict__ hidden) {
+  // Thread i owns column pairs i, i + blockDim, ... (H <= 2 * kPer * blockDim);
+  // every load of the row is issued before the first add.
+  constexpr int kPer = 4, kSplits = 8;
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int t = out_token ? out_token[r] : r;
-  float* xr = x + size_t(t) * H;
-  constexpr int kMaxPer = 8;  // columns per thread (H <= 8 * blockDim)
-  float v[kMaxPer];
+  const int H2 = H >> 1;
+  float2* xr = reinterpret_cast<float2*>(x + size_t(t) * H);
+  float2 v[kPer];
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
+  for (int k = 0; k < kPer; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    v[k] = c < H ? xr[c] : 0.f;
+    v[k] = c < H2 ? xr[c] : make_float2(0.f, 0.f);
   }
   if (partial) {
-    for (int sp = 0; sp < splits; ++sp) {
-      const float* ps = partial + sp * split_stride + size_t(t) * H;
 #pragma unroll
-      for (int k = 0; k < kMaxPer; ++k) {
-        const int c = threadIdx.x + k * blockDim.x;
-        if (c < H) v[k] += ps[c];
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
+    for (int k = 0; k < kPer; ++k) {
       const int c = threadIdx.x + k * blockDim.x;
-      if (c < H) xr[c] = v[k];
+      if (c >= H2) continue;
+      float2 p[kSplits];
+#pragma unroll
+      for (int sp = 0; sp < kSplits; ++sp)
+        if (sp < splits) p[sp] = reinterpret_cast<const float2*>(partial + sp * split_stride + size_t(t) * H)[c];
+#pragma unroll
+      for (int sp = 0; sp < kSplits; ++sp)
+        if (sp < splits) { v[k].x += p[sp].x; v[k].y += p[sp].y; }
+      xr[c] = v[k];
     }
   }
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) ss += v[k] * v[k];
+  for (int k = 0; k < kPer; ++k) ss += v[k].x * v[k].x + v[k].y * v[k].y;
   const float tot = block_sum(ss, red);
   if (!norm_w) return;
   const float inv = rsqrtf(tot / H + eps);
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
+  for (int k = 0; k < kPer; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    if (c < H) {
-      const float y = v[k] * inv * norm_w[c];
-      hb[size_t(r) * H + c] = __float2bfloat16_rn(y);
-      if (hidden) hidden[size_t(r) * H + c] = y;
+    if (c < H2) {
+      const float2 w = reinterpret_cast<const float2*>(norm_w)[c];
+      const float y0 = v[k].x * inv * w.x, y1 = v[k].y * inv * w.y;
+      reinterpret_cast<__nv_bfloat162*>(hb + size_t(r) * H)[c] = __floats2bfloat162_rn(y0, y1);
+      if (hidden) reinterpret_cast<float2*>(hidden + size_t(r) * H)[c] = make_float2(y0, y1);
     }
   }
 }
@@ -173,18 +179,76 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
 // ----------------------------------------------------------------- attention --
 // Per token: q/k RMSNorm (q_norm/k_norm), partial rotate-half RoPE on the
 // first rope dims (angle in double precision), KV append into the paged cache.
-__global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
-                                 int Hq, int Hkv, int D,
-                                 int rope, double theta, float eps, const float* __restrict__ qn,
-                                 const float* __restrict__ kn, const int32_t* __restrict__ token_pos,
-                                 const int64_t* __restrict__ slots, KvPool kv, int layer, float* q,
-                                 float* gate) {
-  extern __shared__ float sm[];  // [warps][D]
+template <int E>
+__device__ __forceinline__ void load_lane(const float* p, float (&out)[E]) {
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p + e);
+      out[e] = v.x; out[e + 1] = v.y; out[e + 2] = v.z; out[e + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(p + e);
+      out[e] = v.x; out[e + 1] = v.y;
+    }
+  }
+}
+template <int E>
+__device__ __forceinline__ void store_lane(float* p, const float (&in)[E]) {
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) *reinterpret_cast<float4*>(p + e) = make_float4(in[e], in[e + 1], in[e + 2], in[e + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e += 2) *reinterpret_cast<float2*>(p + e) = make_float2(in[e], in[e + 1]);
+  }
+}
+// Sum of the split-K partials of E contiguous floats, in split order.
+template <int E>
+__device__ __forceinline__ void load_splits(const float* p, int splits, size_t split_stride, float (&out)[E]) {
+  load_lane<E>(p, out);
+#pragma unroll
+  for (int sp = 1; sp < 8; ++sp) {
+    if (sp < splits) {
+      float part[E];
+      load_lane<E>(p + sp * split_stride, part);
+#pragma unroll
+      for (int e = 0; e < E; ++e) out[e] += part[e];
+    }
+  }
+}
+
+// One warp per head vector (Hq query+gate heads, Hkv keys, Hkv values) of
+// token blockIdx.x; lane l owns D/32 contiguous dims. The RoPE cos/sin of the
+// token's position are computed once per CTA (double precision).
+template <int D>
+__global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict__ proj, int ld, int splits,
+                                                         size_t split_stride, int Hq, int Hkv, int rope,
+                                                         double theta, float eps, const float* __restrict__ qn,
+                                                         const float* __restrict__ kn,
+                                                         const int32_t* __restrict__ token_pos,
+                                                         const int64_t* __restrict__ slots, KvPool kv, int layer,
+                                                         float* q, float* gate) {
+  constexpr int E = D / 32;
+  __shared__ float sm[32][D];
+  __shared__ double rot[2][D / 2];
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
-  float* buf = sm + warp * D;
+  const int half = rope / 2;
+  {
+    const double pos = token_pos[t];
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+      double sn, cs;
+      sincos(pos * pow(theta, -2.0 * j / rope), &sn, &cs);
+      rot[0][j] = cs;
+      rot[1][j] = sn;
+    }
+  }
+  __syncthreads();
+  float* buf = sm[warp];
   const float* pr = proj + size_t(t) * ld;
-  const double pos = token_pos[t];
   const int64_t slot = slots[t];
   const int page = int(slot / kPageTokens), off = int(slot % kPageTokens);
   for (int v = warp; v < Hq + 2 * Hkv; v += nw) {
@@ -193,42 +257,46 @@ __global__ void attn_prep_kernel(const float* __restrict__ proj, int ld, int spl
     if (v < Hq) { src = pr + v * 2 * D; w = qn; }
     else if (v < Hq + Hkv) { src = pr + Hq * 2 * D + (v - Hq) * D; w = kn; }
     else src = pr + Hq * 2 * D + Hkv * D + (v - Hq - Hkv) * D;
-    float ss = 0.f;
-    for (int i = lane; i < D; i += 32) {
-      float v = src[i];
-      for (int sp = 1; sp < splits; ++sp) v += src[sp * split_stride + i];
-      buf[i] = v;
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    __syncwarp();
+    float val[E];
+    load_splits<E>(src + lane * E, splits, split_stride, val);
     if (w) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss += val[e] * val[e];
+      ss = warp_sum(ss);
       const float inv = rsqrtf(ss / D + eps);
-      for (int i = lane; i < D; i += 32) buf[i] = buf[i] * inv * w[i];
-      __syncwarp();
-      for (int j = lane; j < rope / 2; j += 32) {
-        double s, c;
-        sincos(pos * pow(theta, -2.0 * j / rope), &s, &c);
-        const float a = buf[j], b = buf[j + rope / 2];
-        buf[j] = float(a * c - b * s);
-        buf[j + rope / 2] = float(a * s + b * c);
+      float wv[E];
+      load_lane<E>(w + lane * E, wv);
+#pragma unroll
+      for (int e = 0; e < E; ++e) val[e] = val[e] * inv * wv[e];
+      if (half > 0) {
+        store_lane<E>(buf + lane * E, val);
+        __syncwarp();
+        for (int j = lane; j < half; j += 32) {
+          const double c = rot[0][j], sn = rot[1][j];
+          const float a = buf[j], b = buf[j + half];
+          buf[j] = float(a * c - b * sn);
+          buf[j + half] = float(a * sn + b * c);
+        }
+        __syncwarp();
+        load_lane<E>(buf + lane * E, val);
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (v < Hq) {
-      for (int i = lane; i < D; i += 32) {
-        q[(size_t(t) * Hq + v) * D + i] = buf[i];
-        float gv = src[D + i];
-        for (int sp = 1; sp < splits; ++sp) gv += src[sp * split_stride + D + i];
-        gate[(size_t(t) * Hq + v) * D + i] = gv;
-      }
+      store_lane<E>(q + (size_t(t) * Hq + v) * D + lane * E, val);
+      float gv[E];
+      load_splits<E>(src + D + lane * E, splits, split_stride, gv);
+      store_lane<E>(gate + (size_t(t) * Hq + v) * D + lane * E, gv);
     } else {
       const int g = v < Hq + Hkv ? v - Hq : v - Hq - Hkv;
       const int kvsel = v < Hq + Hkv ? 0 : 1;
-      __nv_bfloat16* dst = kv.page(layer, page) + (size_t(kvsel) * Hkv + g) * kPageTokens * D + size_t(off) * D;
-      for (int i = lane; i < D; i += 32) dst[i] = __float2bfloat16_rn(buf[i]);
+      __nv_bfloat16* dst =
+          kv.page(layer, page) + (size_t(kvsel) * Hkv + g) * kPageTokens * D + size_t(off) * D + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; e += 2)
+        *reinterpret_cast<__nv_bfloat162*>(dst + e) = __floats2bfloat162_rn(val[e], val[e + 1]);
     }
-    __syncwarp();
   }
 }
 
@@ -256,45 +324,47 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
 // asc) on the fp32 total order; weights renormalised over the selection
 // (native/qwen_model.inc:77-79: softmax then divide by the selected sum);
 // slot `top` is the shared expert (id E) with weight sigmoid(shared gate).
-__global__ void route_kernel(const float* __restrict__ logits, int ld, int splits, size_t split_stride,
-                             int T, int E, int top, int32_t* ids, float* weights, float* logits_out) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const float* lr = logits + size_t(warp) * ld;
-  constexpr int MAXV = 32;  // E <= 1024
-  float v[MAXV];
-  uint32_t taken = 0;
+__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int ld, int splits,
+                                                    size_t split_stride, int E, int top, int32_t* ids,
+                                                    float* weights, float* logits_out) {
+  // One CTA per token; thread i holds experts i, i+256, ... (E <= 1024).
+  constexpr int kPer = 4, kSplits = 8;
+  __shared__ uint64_t wbest[2][8];
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* lr = logits + size_t(t) * ld;
+  float v[kPer];
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) v[i] = 0.f;
-  for (int sp = 0; sp < splits; ++sp) {  // split-K partials: independent loads per slice
-    const float* ls = lr + sp * split_stride;
+  for (int k = 0; k < kPer; ++k) {
+    const int e = threadIdx.x + k * 256;
+    float part[kSplits];
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i)
-      if (i * 32 + lane < E) v[i] += ls[i * 32 + lane];
-  }
-  float shared_logit = 0.f;
-  if (lane == 0) {
-    shared_logit = lr[E];
-    for (int sp = 1; sp < splits; ++sp) shared_logit += lr[sp * split_stride + E];
+    for (int sp = 0; sp < kSplits; ++sp)  // split-K partials: independent loads, summed in split order
+      part[sp] = (e < E && sp < splits) ? lr[sp * split_stride + e] : 0.f;
+    float acc = part[0];
+#pragma unroll
+    for (int sp = 1; sp < kSplits; ++sp)
+      if (sp < splits) acc += part[sp];
+    v[k] = acc;
   }
   if (logits_out) {  // diagnostic capture of the summed router logits
-    float* lo = logits_out + size_t(warp) * (E + 1);
+    float* lo = logits_out + size_t(t) * (E + 1);
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i)
-      if (i * 32 + lane < E) lo[i * 32 + lane] = v[i];
-    if (lane == 0) lo[E] = shared_logit;
+    for (int k = 0; k < kPer; ++k)
+      if (threadIdx.x + k * 256 < E) lo[threadIdx.x + k * 256] = v[k];
   }
-  float sel_val = 0.f, top_val = 0.f, denom = 0.f;
-  int32_t* out_ids = ids + size_t(warp) * (top + 1);
-  float* out_w = weights + size_t(warp) * (top + 1);
+  uint32_t taken = 0;
+  float top_val = 0.f, denom = 0.f;
+  int32_t* out_ids = ids + size_t(t) * (top + 1);
+  float* out_w = weights + size_t(t) * (top + 1);
   for (int r = 0; r < top; ++r) {
+    // key = (logit on the fp32 total order, then lowest expert id): one max per round
     uint64_t best = 0;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && !(taken >> i & 1u)) {
-        const uint64_t k = (uint64_t(total_key(v[i])) << 32) | uint32_t(0xFFFFFFFFu - e);
-        best = k > best ? k : best;
+    for (int k = 0; k < kPer; ++k) {
+      const int e = threadIdx.x + k * 256;
+      if (e < E && !(taken >> k & 1u)) {
+        const uint64_t key = (uint64_t(total_key(v[k])) << 32) | uint32_t(0xFFFFFFFFu - e);
+        best = key > best ? key : best;
       }
     }
 #pragma unroll
@@ -302,22 +372,24 @@ __global__ void route_kernel(const float* __restrict__ logits, int ld, int split
       const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
-    if ((e & 31) == lane) taken |= 1u << (e >> 5);
-    {
-      float mine = 0.f;
+    if (lane == 0) wbest[r & 1][warp] = best;
+    __syncthreads();
+    best = wbest[r & 1][0];
 #pragma unroll
-      for (int i = 0; i < MAXV; ++i)
-        if (i == (e >> 5)) mine = v[i];
-      sel_val = __shfl_sync(0xffffffffu, mine, e & 31);
-    }
+    for (int w = 1; w < 8; ++w) best = wbest[r & 1][w] > best ? wbest[r & 1][w] : best;
+    const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
+    if ((e & 255) == threadIdx.x) taken |= 1u << (e >> 8);
+    const uint32_t tk = uint32_t(best >> 32);
+    const float sel_val = __uint_as_float((tk & 0x80000000u) ? (tk ^ 0x80000000u) : ~tk);
     if (r == 0) top_val = sel_val;
     const float w = expf(sel_val - top_val);
     denom += w;
-    if (lane == 0) { out_ids[r] = e; out_w[r] = w; }
+    if (threadIdx.x == 0) { out_ids[r] = e; out_w[r] = w; }
   }
-  __syncwarp();
-  if (lane == 0) {
+  if (threadIdx.x == 0) {
+    float shared_logit = lr[E];
+    for (int sp = 1; sp < splits; ++sp) shared_logit += lr[sp * split_stride + E];
+    if (logits_out) logits_out[size_t(t) * (E + 1) + E] = shared_logit;
     for (int r = 0; r < top; ++r) out_w[r] = out_w[r] / denom;
     out_ids[top] = E;
     out_w[top] = 1.f / (1.f + expf(-shared_logit));
@@ -401,6 +473,10 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
                                    const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
                                    int slots, const float* __restrict__ norm_w, float eps,
                                    __nv_bfloat16* __restrict__ hb) {
+  // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
+  // Thread i owns column pairs i, i + blockDim, ...; each slot's loads are
+  // issued in groups of kBatch before the ordered adds.
+  constexpr int kPer = 4, kBatch = 8;
   __shared__ float red[32];
   __shared__ float sw[64];
   __shared__ int32_t srow[64];
@@ -410,40 +486,44 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
     srow[threadIdx.x] = inv[size_t(t) * slots + threadIdx.x];
   }
   __syncthreads();
-  float* xr = x + size_t(t) * H;
-  constexpr int kMaxPer = 8;
-  float v[kMaxPer];
-#pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    v[k] = 0.f;
-  }
-  for (int j = 0; j < slots; ++j) {  // fixed slot order: deterministic sum
-    const float wj = sw[j];
-    const float* yr = y + size_t(srow[j]) * H;
-#pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
-      const int c = threadIdx.x + k * blockDim.x;
-      if (c < H) v[k] += wj * yr[c];
-    }
-  }
+  const int H2 = H >> 1;
+  float2* xr = reinterpret_cast<float2*>(x + size_t(t) * H);
+  float2 v[kPer];
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
+  for (int k = 0; k < kPer; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    if (c < H) {
-      v[k] += xr[c];
-      xr[c] = v[k];
-      ss += v[k] * v[k];
+    v[k] = make_float2(0.f, 0.f);
+    if (c >= H2) continue;
+    for (int j0 = 0; j0 < slots; j0 += kBatch) {  // fixed slot order: deterministic sum
+      float2 yv[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b)
+        if (j0 + b < slots) yv[b] = reinterpret_cast<const float2*>(y + size_t(srow[j0 + b]) * H)[c];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b)
+        if (j0 + b < slots) {
+          v[k].x += sw[j0 + b] * yv[b].x;
+          v[k].y += sw[j0 + b] * yv[b].y;
+        }
     }
+    const float2 xo = xr[c];
+    v[k].x += xo.x;
+    v[k].y += xo.y;
+    xr[c] = v[k];
+    ss += v[k].x * v[k].x + v[k].y * v[k].y;
   }
   const float tot = block_sum(ss, red);
   if (!norm_w) return;
   const float inv_r = rsqrtf(tot / H + eps);
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
+  for (int k = 0; k < kPer; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
-    if (c < H) hb[size_t(t) * H + c] = __float2bfloat16_rn(v[k] * inv_r * norm_w[c]);
+    if (c < H2) {
+      const float2 w = reinterpret_cast<const float2*>(norm_w)[c];
+      reinterpret_cast<__nv_bfloat162*>(hb + size_t(t) * H)[c] =
+          __floats2bfloat162_rn(v[k].x * inv_r * w.x, v[k].y * inv_r * w.y);
+    }
   }
 }
 
@@ -540,6 +620,9 @@ void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int positi
 // Number of kernels this library has launched (read by rs_qwen_device_stats).
 std::atomic<uint64_t> g_kernel_launches{0};
 uint64_t kernel_launches() { return g_kernel_launches.load(); }
+// Threads for the per-row kernels: one float2 column pair each up to 1024
+// threads (H <= 2048), then up to 4 pairs each.
+static inline int row_threads(int H) { return std::min(1024, std::max(32, (H / 2 + 31) / 32 * 32)); }
 static inline void count_launch(int n = 1) { g_kernel_launches.fetch_add(uint64_t(n), std::memory_order_relaxed); }
 
 void launch_pack(const SeqDesc* descs, int n_seq, const int32_t* new_pages, int32_t* block_table,
@@ -565,9 +648,10 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
                           const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   const int n = out_token ? rows : T;
   if (n <= 0) return;
-  if (H > 8 * 1024) throw std::invalid_argument("hidden width above 8192");
-  residual_norm_kernel<<<n, std::min(1024, std::max(32, (H + 7) / 8 / 32 * 32)), 0, s>>>(x, partial, splits, split_stride, H, norm_w, eps, hb,
-                                         out_token, hidden_f32);
+  if (H > 8 * 1024 || H % 2) throw std::invalid_argument("hidden width must be even and at most 8192");
+  if (splits > 8) throw std::invalid_argument("residual split-K above 8");
+  residual_norm_kernel<<<n, row_threads(H), 0, s>>>(x, partial, splits, split_stride, H, norm_w, eps, hb, out_token,
+                                                    hidden_f32);
   count_launch();
 }
 
@@ -576,10 +660,22 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s) {
   if (T <= 0) return;
-  attn_prep_kernel<<<T, 256, 8 * d.D * sizeof(float), s>>>(
-      proj, ld_proj, splits, split_stride, d.Hq, d.Hkv, d.D, d.rope, double(d.theta), d.eps, ly.q_norm, ly.k_norm,
-      token_pos, slot_mapping, kv, kv_layer, q, gate);
-  count_launch();
+  if (splits > 8) throw std::invalid_argument("attention projection split-K above 8");
+  if (d.rope > d.D || d.rope % 2) throw std::invalid_argument("rope dims must be even and at most head_dim");
+  const int threads = 32 * std::min(32, d.Hq + 2 * d.Hkv);
+#define QWEN_PREP(DD)                                                                                         \
+  if (d.D == DD) {                                                                                          \
+    attn_prep_kernel<DD><<<T, threads, 0, s>>>(proj, ld_proj, splits, split_stride, d.Hq, d.Hkv, d.rope,     \
+                                               double(d.theta), d.eps, ly.q_norm, ly.k_norm, token_pos,      \
+                                               slot_mapping, kv, kv_layer, q, gate);                         \
+    count_launch();                                                                                         \
+    return;                                                                                                 \
+  }
+  QWEN_PREP(256)
+  QWEN_PREP(128)
+  QWEN_PREP(64)
+#undef QWEN_PREP
+  throw std::invalid_argument("head_dim must be 64, 128 or 256");
 }
 
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
@@ -593,9 +689,9 @@ void launch_attention_merge(const Dims& d, const float* ws, const float* gate, c
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
                   int32_t* ids, float* weights, float* logits_out, cudaStream_t s) {
   if (E > 1024) throw std::invalid_argument("more than 1024 experts");
+  if (splits > 8) throw std::invalid_argument("router split-K above 8");
   if (T <= 0) return;
-  route_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, splits, split_stride, T, E, top, ids, weights,
-                                           logits_out);
+  route_kernel<<<T, 256, 0, s>>>(logits, ld, splits, split_stride, E, top, ids, weights, logits_out);
   count_launch();
 }
 
@@ -618,9 +714,9 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
                         const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
-  if (slots > 64 || H > 8 * 1024) throw std::invalid_argument("combine geometry");
-  moe_combine_kernel<<<T, std::min(1024, std::max(64, (H + 7) / 8 / 32 * 32)), 0, s>>>(x, y_sorted, inv, weights,
-                                                                                    H, slots, norm_w, eps, hb);
+  if (slots > 64 || H > 8 * 1024 || H % 2) throw std::invalid_argument("combine geometry");
+  moe_combine_kernel<<<T, std::max(64, row_threads(H)), 0, s>>>(x, y_sorted, inv, weights, H, slots, norm_w, eps,
+                                                                hb);
   count_launch();
 }
 

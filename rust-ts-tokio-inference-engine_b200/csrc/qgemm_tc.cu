@@ -77,23 +77,34 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and flags the error) after ~1 s. The clock is
-// read once per 256 polls so spinning warps stay off the XU pipe.
+// The same test with a suspend-time hint: a warp whose phase is not complete
+// sleeps in hardware until the phase completes or about `ns` nanoseconds pass,
+// instead of spinning through issue slots the dequantising warps need.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and flags the error) after ~1 s. Each failed
+// poll sleeps up to kWaitSleepNs, so the clock is read at most every few us.
+constexpr uint32_t kWaitSleepNs = 20000;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint32_t* err) {
   if (mbar_try(bar, parity)) return true;
-  long long t0 = -1;
-  for (uint32_t n = 1;; ++n) {
-    if (mbar_try(bar, parity)) return true;
-    if ((n & 255u) == 0) {
-      if (*abort) return false;
-      const long long now = clock64();
-      if (t0 < 0) t0 = now;
-      else if (now - t0 > kWaitCycles) {
-        *abort = 1;
-        atomicOr(err, kErrTimeout);
-        return false;
-      }
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_sleep(bar, parity, kWaitSleepNs)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      atomicOr(err, kErrTimeout);
+      return false;
     }
   }
 }
