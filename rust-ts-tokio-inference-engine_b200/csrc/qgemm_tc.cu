@@ -10,8 +10,10 @@
 //           dequant warps release as soon as they have read it, so HBM reads
 //           run far ahead of the tensor cores;
 //   warp 2  activation producer: one 3-D TMA per unit (U 64-column tiles,
-//           128B-swizzled) into a ring tied to the TMEM stages (released by the
-//           MMA commit; the activations are L2-resident);
+//           128B-swizzled) into its own ring of 96 KB (768 / box chunks, deeper
+//           than the TMEM stages so L2 round trips overlap); a slot is
+//           released by the dequant warpgroup that sees the MMAs reading it
+//           complete (the TMEM slot wait of the unit NS units later);
 //   warp 1  MMA issuer (converged warp, one elected lane issues): allocates
 //           TMEM and works in units of U (= 4, 2 or 1) chunks: one mbarrier
 //           wait, 4U tcgen05.mma (A from TMEM, B from shared memory) and one
@@ -24,9 +26,8 @@
 //           them into TMEM with tcgen05.st (the A operand);
 //   warps 15-18 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
 //           partial store / SwiGLU (bf16) / fp32 store.
-// The dequantised weights never touch shared memory. Stage i of the
-// shared-memory ring pairs with TMEM A stage i; a unit's stages are released
-// together by its commit. Units never straddle work items (split-K ranges are
+// The dequantised weights never touch shared memory. A unit's TMEM A stages
+// are released together by its commit. Units never straddle work items (split-K ranges are
 // multiples of U). Every mbarrier wait is bounded (~1 s); on expiry the kernel
 // raises kErrTimeout and drains out.
 #include <cuda.h>
@@ -210,14 +211,31 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Two bf16 (q0*s+b, q1*s+b) packed low/high, from the nibble pair (q0, q1)
-// already placed as 128+q in the low/high halves of `pair_bits`.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t pair_bits, __nv_bfloat162 s2, __nv_bfloat162 b2) {
-  const __nv_bfloat162 magic = __floats2bfloat162_rn(128.f, 128.f);
-  __nv_bfloat162 x = *reinterpret_cast<__nv_bfloat162*>(&pair_bits);
-  x = __hsub2(x, magic);        // exact: integers 0..15
-  x = __hfma2(x, s2, b2);       // one rounding of scale*q + bias
-  return *reinterpret_cast<uint32_t*>(&x);
+// Explicit shared-memory loads: the ring pointers come from aligned integer
+// arithmetic on the dynamic shared-memory base, so plain dereferences would
+// compile to generic loads.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+  return v;
+}
+
+// Two bf16 (q0*s+b, q1*s+b) packed low/high from the nibble pair (q0, q1) at
+// bits [0,4) and [16,20) of `w`: one lop3 places them as 128+q in bf16
+// ((w & 0x000F000F) | 0x43004300), add.rn subtracts 128 exactly and fma.rn
+// rounds scale*q + bias once. `mask` / `magic` / `neg128` live in registers.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t w, uint32_t mask, uint32_t magic, uint32_t neg128,
+                                             uint32_t s2, uint32_t b2) {
+  uint32_t x, q, y;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(x) : "r"(w), "r"(mask), "r"(magic));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(x), "r"(neg128));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(q), "r"(s2), "r"(b2));
+  return y;
 }
 
 struct Work {
@@ -229,11 +247,9 @@ struct Work {
   bool valid;
 };
 
-__device__ __forceinline__ int n_items(const TcArgs& a) {
-  return a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
-}
-
-__device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* goff) {
+// Grouped items run over the non-empty groups only (`act`, `n_act` built in
+// shared memory at kernel start), so CTAs get equal shares of real work.
+__device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* goff, const int32_t* act) {
   Work w;
   const int kc = a.W.k_chunks();
   if (a.mode == kGemmStoreF32) {
@@ -246,7 +262,7 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* g
     w.p0 = 0;
     w.p1 = a.n_tokens;
   } else {
-    w.g = i / a.expert_tiles;
+    w.g = act[i / a.expert_tiles];
     w.rt_local = i % a.expert_tiles;
     w.rt = w.g * a.expert_tiles + w.rt_local;
     w.c0 = 0;
@@ -258,11 +274,6 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* g
   return w;
 }
 
-__device__ unsigned long long* g_trace = nullptr;  // [5][512] clock64 stamps of CTA 0 (diagnostic)
-#define QTRACE(kind, idx)                                                          \
-  do {                                                                             \
-    if (trace && (idx) < 512) trace[(kind) * 512 + (idx)] = clock64(); \
-  } while (0)
 
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
@@ -274,30 +285,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ushift = U == 4 ? 2 : (U == 2 ? 1 : 0);
   const int NS = S / U;           // TMEM/B unit slots (multiple of kDequantGroups)
   const int box = a.box_rows;
+  const int NSB = a.b_stages / U; // activation ring unit slots
   const int d_col0 = S * 32;      // accumulators after the A stages
   const int d_stride = box <= 64 ? 64 : 128;
   const uint32_t b_bytes = uint32_t(box) * 128;
   const uint32_t w_unit = uint32_t(U) * kTileBytes;
   uint8_t* ring_b = base;
-  uint8_t* ring_w = ring_b + size_t(S) * b_bytes;
+  uint8_t* ring_w = ring_b + size_t(a.b_stages) * b_bytes;
   float* xchg = reinterpret_cast<float*>(ring_w + size_t(kWSlots) * w_unit);  // [64][9]
   uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * 9);
   uint64_t* w_full = bars;              // [kWSlots] unit weights landed (tx)
   uint64_t* w_empty = w_full + kWSlots; // [kWSlots] unit weights read (4 dequant warps)
-  uint64_t* b_full = w_empty + kWSlots; // [NS] unit activations landed (tx)
-  uint64_t* a_full = b_full + NS;       // [NS] unit A stages written (4 dequant warps)
+  uint64_t* b_full = w_empty + kWSlots; // [NSB] unit activations landed (tx)
+  uint64_t* b_empty = b_full + NSB;     // [NSB] unit activations consumed (1 dequant lane)
+  uint64_t* a_full = b_empty + NSB;     // [NS] unit A stages written (4 dequant warps)
   uint64_t* empty = a_full + NS;        // [NS] unit consumed by the MMAs (commit)
   uint64_t* acc_full = empty + NS;      // [2]  accumulator complete (commit)
   uint64_t* acc_empty = acc_full + 2;   // [2]  accumulator drained (4 epilogue warps)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(acc_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
   int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
+  int32_t* act = goff + (kMaxGroups + 1);                      // [non-empty groups], then their count
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned long long* const trace = blockIdx.x == 0 ? g_trace : nullptr;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWSlots; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-    for (int i = 0; i < NS; ++i) { mbar_init(&b_full[i], 1); mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < NSB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
+    for (int i = 0; i < NS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -309,25 +323,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (a.mode != kGemmStoreF32)
     for (int g = threadIdx.x; g <= a.groups; g += blockDim.x) goff[g] = a.group_off[g];
+  __syncthreads();
+  if (a.mode != kGemmStoreF32 && warp == 2) {
+    // stable compaction of the non-empty groups (ballot + popc per 32 groups)
+    int n = 0;
+    for (int g0 = 0; g0 < a.groups; g0 += 32) {
+      const int g = g0 + lane;
+      const bool live = g < a.groups && goff[g + 1] > goff[g];
+      const uint32_t m = __ballot_sync(0xffffffffu, live);
+      if (live) act[n + __popc(m & ((1u << lane) - 1u))] = g;
+      n += __popc(m);
+    }
+    if (lane == 0) act[kMaxGroups] = n;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = n_items(a);
+  const int total = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : act[kMaxGroups] * a.expert_tiles;
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
     int ws = 0;
-    uint32_t wph = 0, it = 0;
+    uint32_t wph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff);
+      const Work w = item_at(a, i, goff, act);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
-        for (int c = w.c0; c < w.c1; c += U, it += U) {
+        for (int c = w.c0; c < w.c1; c += U) {
           if (!mbar_wait(&w_empty[ws], wph ^ 1, abort_flag, a.err)) { ok = false; break; }
           if (elect_one()) {
-            QTRACE(0, it);
             mbar_expect_tx(&w_full[ws], w_unit);
             bulk_load(ring_w + size_t(ws) * w_unit, a.W.tile(w.rt, c), w_unit, &w_full[ws]);
           }
@@ -338,34 +364,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 2) {
     // ---------------- activation producer ----------------
-    int st = 0;
-    uint32_t ph = 0;
+    int bs = 0;
+    uint32_t bph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff);
+      const Work w = item_at(a, i, goff, act);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
         for (int c = w.c0; c < w.c1; c += U) {
-          const int slot = st >> ushift;
-          if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          if (!mbar_wait(&b_empty[bs], bph ^ 1, abort_flag, a.err)) { ok = false; break; }
           if (elect_one()) {
-            mbar_expect_tx(&b_full[slot], uint32_t(U) * b_bytes);
-            tma_load_3d(ring_b + size_t(st) * b_bytes, &bmap, 0, a.b_row0 + tb, c, &b_full[slot]);
+            mbar_expect_tx(&b_full[bs], uint32_t(U) * b_bytes);
+            tma_load_3d(ring_b + size_t(bs) * U * b_bytes, &bmap, 0, a.b_row0 + tb, c, &b_full[bs]);
           }
           __syncwarp();
-          st += U;
-          if (st == S) { st = 0; ph ^= 1; }
+          if (++bs == NSB) { bs = 0; bph ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (converged warp, elected lane issues) ----------------
-    int st = 0;
-    uint32_t ph = 0, acc_it = 0, it = 0;
+    int st = 0, bs = 0;
+    uint32_t ph = 0, bph = 0, acc_it = 0;
     const uint32_t idesc = idesc_bf16(box);
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff);
+      const Work w = item_at(a, i, goff, act);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
         const int d = acc_it & 1;
@@ -374,13 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem + d_col0 + d * d_stride;
         for (int c = w.c0; c < w.c1; c += U) {
           const int slot = st >> ushift;
-          if (!mbar_wait(&b_full[slot], ph, abort_flag, a.err)) { ok = false; break; }
+          if (!mbar_wait(&b_full[bs], bph, abort_flag, a.err)) { ok = false; break; }
           if (!mbar_wait(&a_full[slot], ph, abort_flag, a.err)) { ok = false; break; }
           tc_fence_after();
           if (elect_one()) {
-            QTRACE(3, it);
             for (int u = 0; u < U; ++u) {
-              const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(st + u) * b_bytes));
+              const uint64_t bdesc = smem_desc_sw128(smem_u32(ring_b + size_t(bs * U + u) * b_bytes));
 #pragma unroll
               for (int k = 0; k < kTileK / 16; ++k)
                 mma_ts(d_tmem, tmem + (st + u) * 32 + k * 8, bdesc + uint64_t(k * 2), idesc,
@@ -389,9 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&empty[slot]);
           }
           __syncwarp();
-          it += U;
           st += U;
           if (st == S) { st = 0; ph ^= 1; }
+          if (++bs == NSB) { bs = 0; bph ^= 1; }
         }
         if (ok && elect_one()) mma_commit(&acc_full[d]);
         __syncwarp();
@@ -403,56 +426,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
-    int st = 0, ws = 0, turn = 0;
-    uint32_t ph = 0, wph = 0, it = 0;
+    const uint32_t ring_w_s = smem_u32(ring_w);
+    // dequant constants in registers (lop3 and the bf16x2 ops take no immediates)
+    uint32_t k_mask = 0x000F000Fu, k_magic = 0x43004300u, k_neg128 = 0xC300C300u;
+    asm volatile("" : "+r"(k_mask), "+r"(k_magic), "+r"(k_neg128));
+    // This warpgroup takes units n = wg, wg + 3, ... of the CTA's unit
+    // sequence. NS, kWSlots and NSB are multiples of 3, so its TMEM slot,
+    // weight slot and released activation slot (of unit n - NS) each advance
+    // by 3 per unit, and it never walks the other warpgroups' units.
+    int st = wg * U, ws = wg, rel = wg, mine = 0, skip = wg;
+    uint32_t ph = 0, wph = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff);
+      const Work w = item_at(a, i, goff, act);
       if (!w.valid) continue;
+      const int nb = (w.c1 - w.c0) / U;  // units per token block (K ranges are multiples of U)
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
-        for (int c = w.c0; c < w.c1; c += U) {
-          if (turn == wg) {
-            const int slot = st >> ushift;
-            if (!mbar_wait(&w_full[ws], wph, abort_flag, a.err)) { ok = false; break; }
-            if (quad == 0 && lane == 0) QTRACE(1, it);
-            // the MMAs that read these TMEM stages last round must be done
-            if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
-            tc_fence_after();
-            for (int u = 0; u < U; ++u) {
-              const uint8_t* tile = ring_w + size_t(ws) * w_unit + size_t(u) * kTileBytes;
-              const uint4 p0 = reinterpret_cast<const uint4*>(tile + r * 32)[0];
-              const uint4 p1 = reinterpret_cast<const uint4*>(tile + r * 32)[1];
-              const uint32_t sb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r];
-              const uint32_t bb = reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r];
-              __nv_bfloat162 s2, b2;
-              {
-                const uint32_t sv = sb | (sb << 16), bv = bb | (bb << 16);
-                s2 = *reinterpret_cast<const __nv_bfloat162*>(&sv);
-                b2 = *reinterpret_cast<const __nv_bfloat162*>(&bv);
-              }
-              uint32_t v[32];
+        int k = skip;
+        for (; k < nb; k += kDequantGroups) {
+          const int slot = st >> ushift;
+          if (!mbar_wait(&w_full[ws], wph, abort_flag, a.err)) { ok = false; break; }
+          // the MMAs that read these TMEM stages last round must be done...
+          if (!mbar_wait(&empty[slot], ph ^ 1, abort_flag, a.err)) { ok = false; break; }
+          // ...which also ends their reads of unit (n - NS)'s activations
+          if (mine >= NS / kDequantGroups && quad == 0 && lane == 0) mbar_arrive(&b_empty[rel]);
+          tc_fence_after();
+          for (int u = 0; u < U; ++u) {
+            const uint32_t tile = ring_w_s + uint32_t(ws) * w_unit + uint32_t(u) * kTileBytes;
+            const uint4 p0 = lds128(tile + r * 32);
+            const uint4 p1 = lds128(tile + r * 32 + 16);
+            const uint32_t sb = lds_u16(tile + kTilePackedBytes + r * 2);
+            const uint32_t bb = lds_u16(tile + kTilePackedBytes + kTileRows * 2 + r * 2);
+            const uint32_t s2 = __byte_perm(sb, 0, 0x1010), b2 = __byte_perm(bb, 0, 0x1010);
+            uint32_t v[32];
 #define QWEN_DEQ_WORD(WD, W)                                                            \
   _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
-      deq_pair((((W) >> (4 * j)) & 0x000F000Fu) | 0x43004300u, s2, b2);
-              QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
-              QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
+      deq_pair((W) >> (4 * j), k_mask, k_magic, k_neg128, s2, b2);
+            QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
+            QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
 #undef QWEN_DEQ_WORD
-              tmem_st32(tmem + lane_addr + (st + u) * 32, v);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&w_empty[ws]);  // weights read: the producer may refill
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[slot]);
-            if (quad == 0 && lane == 0) QTRACE(2, it);
+            tmem_st32(tmem + lane_addr + (st + u) * 32, v);
           }
-          turn = (turn == kDequantGroups - 1) ? 0 : turn + 1;
-          it += U;
-          st += U;
-          if (st == S) { st = 0; ph ^= 1; }
-          if (++ws == kWSlots) { ws = 0; wph ^= 1; }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&w_empty[ws]);  // weights read: the producer may refill
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[slot]);
+          st += kDequantGroups * U;
+          if (st >= S) { st -= S; ph ^= 1; }
+          ws += kDequantGroups;
+          if (ws >= kWSlots) { ws -= kWSlots; wph ^= 1; }
+          if (mine >= NS / kDequantGroups && (rel += kDequantGroups) >= NSB) rel -= NSB;
+          ++mine;
         }
+        skip = k - nb;
       }
     }
   } else {
@@ -463,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_it = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff);
+      const Work w = item_at(a, i, goff, act);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
         const int d = acc_it & 1;
@@ -522,15 +550,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-const void* g_trace_sym() { return reinterpret_cast<const void*>(&g_trace); }
-void qgemm_tc_set_trace(unsigned long long* buf) {
-  QWEN_CUDA(cudaMemcpyToSymbol(g_trace, &buf, sizeof(buf)));
-}
 
 size_t qgemm_tc_smem(int box_rows, int stages, int unit) {
-  return 1024 + size_t(stages) * size_t(box_rows) * 128 + size_t(kWSlots) * unit * kTileBytes + 64 * 9 * 4 +
-         (2 * size_t(kWSlots) + 3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4;
+  const int b_stages = qgemm_tc_bstages(box_rows);
+  return 1024 + size_t(b_stages) * size_t(box_rows) * 128 + size_t(kWSlots) * unit * kTileBytes + 64 * 9 * 4 +
+         (2 * size_t(kWSlots) + 2 * size_t(b_stages) + 3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4 +
+         (kMaxGroups + 1) * 4;
 }
+
+// Activation ring depth (chunks): 96 KB of box-row tiles, at least the TMEM
+// stages, a multiple of every unit size.
+int qgemm_tc_bstages(int box_rows) { return std::max(qgemm_tc_stages(box_rows), 768 / box_rows); }
 
 // Ring depth (chunks): A stages (32 TMEM columns each) plus two accumulators
 // (64 or 128 columns) fit in 512 columns. The number of unit slots
@@ -555,8 +585,11 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   if (a.mode == kGemmStoreF32 && a.n_tokens <= 0) return;
   if (a.mode != kGemmStoreF32 && a.groups > kMaxGroups) throw std::invalid_argument("too many GEMM groups");
   a.stages = qgemm_tc_stages(a.box_rows);
+  a.b_stages = qgemm_tc_bstages(a.box_rows);
   a.unit = qgemm_tc_unit(a);  // largest of 4, 2, 1 dividing the items and the ring (slots % groups == 0)
   if ((a.stages / a.unit) % kDequantGroups) throw std::logic_error("GEMM unit slots not a multiple of warpgroups");
+  if (a.b_stages % a.unit || a.b_stages < a.stages || (a.b_stages / a.unit) % kDequantGroups)
+    throw std::logic_error("GEMM activation ring geometry");
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages, a.unit);
   static bool configured = false;
   if (!configured) {

@@ -17,7 +17,8 @@ struct TcArgs {
   size_t split_stride = 0;
   int b_row0 = 0;      // first activation row of the B tensor map
   int box_rows = 16;   // N tile: 16, 32, 64 or 128 (the tensor map's box height)
-  int stages = 0;      // shared-memory ring depth (set by the launcher)
+  int stages = 0;      // TMEM A stages in chunks (set by the launcher)
+  int b_stages = 0;    // activation ring depth in chunks (set by the launcher)
   int unit = 1;        // chunks per MMA unit (set by the launcher)
   float* Y = nullptr;
   int ldy = 0;
@@ -45,8 +46,7 @@ void launch_attention_merge(const Dims& d, const float* ws, const float* gate, c
                             int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
 size_t qgemm_tc_smem(int box_rows, int stages, int unit);
-void qgemm_tc_set_trace(unsigned long long* buf);
-const void* g_trace_sym();
 int qgemm_tc_stages(int box_rows);
+int qgemm_tc_bstages(int box_rows);
 
 }  // namespace qwen

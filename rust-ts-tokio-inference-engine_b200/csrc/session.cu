@@ -145,7 +145,6 @@ struct Session {
   DevBuf<int2> attn_items;              // attention work list: (token, KV split) pairs
   int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
-  DevBuf<unsigned long long> trace_buf;
   int sm_count = 148;
   int cur_layer = 0;
   bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
@@ -360,11 +359,6 @@ struct Session {
     hb_out.ensure(size_t(max_rows) * d.H);
     QWEN_CUDA(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device));
     simple_gemm = std::getenv("QWEN_GEMM") && std::string(std::getenv("QWEN_GEMM")) == "simple";
-    if (std::getenv("QWEN_GEMM_TRACE")) {
-      trace_buf.ensure(5 * 512);
-      QWEN_CUDA(cudaMemset(trace_buf.p, 0, 5 * 512 * 8));
-      qgemm_tc_set_trace(trace_buf.p);
-    }
     const int max_split_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1, d.H});
     partial.ensure(size_t(kMaxSplits) * T * max_split_w);
 
@@ -1225,21 +1219,6 @@ int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, s
     }
     s->simple_gemm = prev;
     QWEN_CUDA(cudaEventRecord(s->ev_end, s->stream));
-    if (std::getenv("QWEN_GEMM_TRACE")) {
-      QWEN_CUDA(cudaStreamSynchronize(s->stream));
-      std::vector<unsigned long long> tr(5 * 512);
-      unsigned long long* dp = nullptr;
-      QWEN_CUDA(cudaMemcpyFromSymbol(&dp, g_trace_sym(), sizeof(dp)));
-      if (dp) {
-        QWEN_CUDA(cudaMemcpy(tr.data(), dp, tr.size() * 8, cudaMemcpyDeviceToHost));
-        const unsigned long long t0 = tr[0];
-        for (int i = 0; i < 512; i += (i < 40 ? 1 : 37))
-          if (tr[i])
-            fprintf(stderr, "chunk %3d issue %8lld full_seen %8lld afull %8lld mma %8lld\n", i, (long long)(tr[i] - t0),
-                    tr[512 + i] ? (long long)(tr[512 + i] - t0) : -1, tr[1024 + i] ? (long long)(tr[1024 + i] - t0) : -1,
-                    tr[1536 + i] ? (long long)(tr[1536 + i] - t0) : -1);
-      }
-    }
     std::vector<float> part(stride * splits);
     uint32_t h_err = 0;
     QWEN_CUDA(cudaMemcpyAsync(part.data(), out, part.size() * 4, cudaMemcpyDeviceToHost, s->stream));

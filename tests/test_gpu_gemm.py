@@ -47,7 +47,7 @@ def test_tc_engine_matches_cuda_core_engine(pkg, widths):
                                    (3, H, cfg.vocab)):
                 if which == 3 and layer != layers[0]:
                     continue
-                for T in (1, 5, 16, 64, 130):
+                for T in (1, 5, 16, 30, 64, 130):
                     if which == 3 and T > 64:
                         continue
                     x = bf16_bits(rng.standard_normal((T, k)))
