@@ -249,7 +249,7 @@ def main():
         cfg.value_heads * cfg.value_dim * cfg.key_dim + (cfg.conv - 1) * (
             2 * cfg.key_heads * cfg.key_dim + cfg.value_heads * cfg.value_dim)) * 4
     page_bytes = (cfg.layers // cfg.interval) * 2 * cfg.kv_heads * 16 * cfg.head_dim * 2
-    total_steps = args.warmup + args.steps + 2
+    total_steps = args.warmup + args.steps + 2 + 5  # + capture step + 5 profiled steps
     pages = int(sum((L + total_steps + 15) // 16 + 1 for L in ctx)) + 64
     slots = N_SEQ + 8
     budget = slots * gdn_slot + pages * page_bytes
@@ -269,8 +269,10 @@ def main():
 
     for _ in range(args.warmup):
         one_step()
-    sess.set_profile(True)
-    _, total0, n0, stage0 = sess.timing()
+    # Timed region: whole-step CUDA events only (per-stage events would sit
+    # between kernels and serialise programmatic launches).
+    sess.set_profile(False)
+    _, total0, n0, _ = sess.timing()
     step_ms = []
     launches0 = sess.stats()[16]
     barrier(world)
@@ -284,7 +286,14 @@ def main():
         wall = time.perf_counter() - t0
     barrier(world)
     launches = int(sess.stats()[16] - launches0)
-    _, total1, n1, stage1 = sess.timing()
+    _, total1, n1, _ = sess.timing()
+    # Stage breakdown from a few more steps with per-stage events.
+    prof_steps = 5
+    sess.set_profile(True)
+    _, _, _, stage0 = sess.timing()
+    for _ in range(prof_steps):
+        one_step()
+    _, _, _, stage1 = sess.timing()
     sess.set_profile(False)
     sess.set_capture(True)
     one_step()
@@ -296,7 +305,7 @@ def main():
     tokens_total = N_SEQ * args.steps * world
     value = tokens_total / dev_s
     e2e = tokens_total / wall
-    stage_ms = [(b - a) / args.steps for a, b in zip(stage0, stage1)]
+    stage_ms = [(b - a) / prof_steps for a, b in zip(stage0, stage1)]
     if rank != 0:
         return
     hbm, tflops, peak_kind = measured_peaks()

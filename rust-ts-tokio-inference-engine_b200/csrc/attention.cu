@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
                        const SeqDesc* __restrict__ descs, const int32_t* __restrict__ block_table, int stride,
                        const int2* __restrict__ items, int split_pages, int Hq, int Hkv, int G, int max_splits,
                        float* __restrict__ ws, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int KS = D / 16;     // k-steps of Q K^T
   constexpr int NT = D / 8;      // n-tiles of O
   constexpr int TILE = 16 * D * 2;  // bytes of one 16-row tile
@@ -314,7 +316,7 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
                                      int(smem)));                                                           \
       cfg = true;                                                                                           \
     }                                                                                                       \
-    attn_decode_kernel<DD><<<grid, kAttnWarps * 32, smem, s>>>(kvmap, q, token_seq, token_pos, descs,      \
+    launch_pdl(attn_decode_kernel<DD>, grid, kAttnWarps * 32, smem, s, kvmap, q, token_seq, token_pos, descs,      \
                                                                block_table, bt_stride, items, split_pages,  \
                                                                d.Hq, d.Hkv, G, max_splits, ws, err);        \
     QWEN_CUDA(cudaGetLastError());                                                                          \

@@ -6,6 +6,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #define QWEN_CUDA(call)                                                                    \
   do {                                                                                     \
@@ -105,5 +106,30 @@ enum ErrorBits : uint32_t {
   kErrBounds = 2u,
   kErrTimeout = 4u,
 };
+
+// Programmatic dependent launch. Every step kernel is launched with
+// programmatic stream serialisation: it calls pdl_trigger() on entry so the
+// next kernel may start launching, and pdl_wait() before it touches memory
+// that earlier kernels of the stream write (pdl_wait returns once they have
+// completed and their writes are visible; without a programmatic predecessor
+// it returns at once).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QWEN_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 }  // namespace qwen

@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
                     int hk, int hv, int conv, const float* __restrict__ conv_w, const float* __restrict__ a_log,
                     const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
                     float* __restrict__ gb_out) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int NC = 2 * DK + R * DV;
   __shared__ float qs[DK], ks[DK];
   __shared__ float qk_scale[2];
@@ -116,6 +118,8 @@ __global__ void __launch_bounds__(256)
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
                       __nv_bfloat16* __restrict__ out, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
   constexpr int RPW = DV / 8;   // rows per warp
   using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
@@ -224,10 +228,10 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   bool done = false;
 #define QWEN_GDN(DK_, DV_, R_)                                                                                    \
   if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \
-    gdn_prep_kernel<DK_, DV_, R_><<<dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s>>>(                              \
+    launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
         proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
         ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf);                                                            \
-    gdn_update_kernel<DK_, DV_><<<dim3(n_seq, d.hv), 256, 0, s>>>(descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
+    launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, 0, s, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
                                                                 qk_buf, v_buf, gb_buf, proj, ld_proj, splits,    \
                                                                 split_stride, d.cd, ly.gnorm, d.eps, out, err);  \
     done = true;                                                                                                 \

@@ -42,6 +42,8 @@ __device__ __forceinline__ int block_sum_int(int v, int* red) {
 __global__ void pack_kernel(const SeqDesc* __restrict__ descs, int n_seq,
                             const int32_t* __restrict__ new_pages, int32_t* block_table,
                             int stride, Packed p) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int red[32];
   const int s = blockIdx.x;
   int local = 0;
@@ -77,6 +79,8 @@ __global__ void pack_kernel(const SeqDesc* __restrict__ descs, int n_seq,
 // the sequence's first new page, for every attention layer, K and V.
 __global__ void cow_kernel(KvPool kv, const SeqDesc* __restrict__ descs,
                            const int32_t* __restrict__ new_pages) {
+  pdl_trigger();
+  pdl_wait();
   const SeqDesc d = descs[blockIdx.x];
   if (d.cow_src < 0 || d.n_new <= 0) return;
   const int layer = blockIdx.y;
@@ -95,6 +99,8 @@ __global__ void cow_kernel(KvPool kv, const SeqDesc* __restrict__ descs,
 __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ tokens,
                                   const float* __restrict__ norm_w, float eps, float* x,
                                   __nv_bfloat16* hb) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int t = blockIdx.x, H = embed.k;
   const uint32_t tok = tokens[t];
@@ -128,6 +134,8 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
                                      size_t split_stride, int H, const float* __restrict__ norm_w,
                                      float eps, __nv_bfloat16* __restrict__ hb,
                                      const int32_t* __restrict__ out_token, float* __restrict__ hidden) {
+  pdl_trigger();
+  pdl_wait();
   // Thread i owns column pairs i, i + blockDim, ... (H <= 2 * kPer * blockDim);
   // every load of the row is issued before the first add.
   constexpr int kPer = 4, kSplits = 8;
@@ -231,6 +239,8 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
                                                          const int32_t* __restrict__ token_pos,
                                                          const int64_t* __restrict__ slots, KvPool kv, int layer,
                                                          float* q, float* gate) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int E = D / 32;
   __shared__ float sm[32][D];
   __shared__ double rot[2][D / 2];
@@ -304,6 +314,8 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
 __global__ void attention_merge_kernel(const float* __restrict__ ws, const float* __restrict__ gate,
                                        const int32_t* __restrict__ token_pos, int Hq, int D, int spl,
                                        int max_splits, __nv_bfloat16* out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y;
   const int n = (token_pos[t] + 1 + spl - 1) / spl;
   const float* base = ws + (size_t(t) * Hq + h) * max_splits * (D + 2);
@@ -327,6 +339,8 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int ld, int splits,
                                                     size_t split_stride, int E, int top, int32_t* ids,
                                                     float* weights, float* logits_out) {
+  pdl_trigger();
+  pdl_wait();
   // One CTA per token; thread i holds experts i, i+256, ... (E <= 1024).
   constexpr int kPer = 4, kSplits = 8;
   __shared__ uint64_t wbest[2][8];
@@ -405,6 +419,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __restrict__ ids, int n,
                                                            int n_experts, int32_t* counts, int32_t* offsets,
                                                            int32_t* perm, int32_t* inv) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ int32_t smi[];
   int32_t* cnt = smi;                 // [n_experts]
   int32_t* cursor = cnt + n_experts;  // [n_experts]
@@ -473,6 +489,8 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
                                    const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
                                    int slots, const float* __restrict__ norm_w, float eps,
                                    __nv_bfloat16* __restrict__ hb) {
+  pdl_trigger();
+  pdl_wait();
   // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
   // Thread i owns column pairs i, i + blockDim, ...; each slot's loads are
   // issued in groups of kBatch before the ordered adds.
@@ -531,6 +549,8 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
 // (contiguous per expert, so the GEMM's TMA loads one box per expert).
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int ld, const int32_t* __restrict__ perm,
                                    int div, int H, __nv_bfloat16* dst) {
+  pdl_trigger();
+  pdl_wait();
   const int p = blockIdx.x;
   const int row = perm[p] / div;
   const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(row) * ld);
@@ -541,6 +561,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int ld
 // Greedy selection per row: IEEE total order, lowest index on ties
 // (native/selection.h:3-12); any non-finite logit raises kErrNonFinite.
 __global__ void argmax_kernel(const float* __restrict__ logits, int V, uint32_t* tokens, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint64_t red[32];
   const int r = blockIdx.x;
   const float* lr = logits + size_t(r) * V;
@@ -627,19 +649,19 @@ static inline void count_launch(int n = 1) { g_kernel_launches.fetch_add(uint64_
 
 void launch_pack(const SeqDesc* descs, int n_seq, const int32_t* new_pages, int32_t* block_table,
                  int bt_stride, Packed p, cudaStream_t s) {
-  pack_kernel<<<n_seq, 256, 0, s>>>(descs, n_seq, new_pages, block_table, bt_stride, p);
+  launch_pdl(pack_kernel, n_seq, 256, 0, s, descs, n_seq, new_pages, block_table, bt_stride, p);
   count_launch();
 }
 
 void launch_cow(KvPool kv, const SeqDesc* descs, int n_seq, const int32_t* new_pages, cudaStream_t s) {
   if (kv.layers == 0) return;
-  cow_kernel<<<dim3(n_seq, kv.layers), 256, 0, s>>>(kv, descs, new_pages);
+  launch_pdl(cow_kernel, dim3(n_seq, kv.layers), 256, 0, s, kv, descs, new_pages);
   count_launch();
 }
 
 void launch_embed_norm(const QMat& embed, const uint32_t* tokens, int T, const float* norm_w,
                        float eps, float* x, __nv_bfloat16* hb, cudaStream_t s) {
-  embed_norm_kernel<<<T, 256, 0, s>>>(embed, tokens, norm_w, eps, x, hb);
+  launch_pdl(embed_norm_kernel, T, 256, 0, s, embed, tokens, norm_w, eps, x, hb);
   count_launch();
 }
 
@@ -650,7 +672,7 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
   if (n <= 0) return;
   if (H > 8 * 1024 || H % 2) throw std::invalid_argument("hidden width must be even and at most 8192");
   if (splits > 8) throw std::invalid_argument("residual split-K above 8");
-  residual_norm_kernel<<<n, row_threads(H), 0, s>>>(x, partial, splits, split_stride, H, norm_w, eps, hb, out_token,
+  launch_pdl(residual_norm_kernel, n, row_threads(H), 0, s, x, partial, splits, split_stride, H, norm_w, eps, hb, out_token,
                                                     hidden_f32);
   count_launch();
 }
@@ -665,7 +687,7 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
   const int threads = 32 * std::min(32, d.Hq + 2 * d.Hkv);
 #define QWEN_PREP(DD)                                                                                         \
   if (d.D == DD) {                                                                                          \
-    attn_prep_kernel<DD><<<T, threads, 0, s>>>(proj, ld_proj, splits, split_stride, d.Hq, d.Hkv, d.rope,     \
+    launch_pdl(attn_prep_kernel<DD>, T, threads, 0, s, proj, ld_proj, splits, split_stride, d.Hq, d.Hkv, d.rope,     \
                                                double(d.theta), d.eps, ly.q_norm, ly.k_norm, token_pos,      \
                                                slot_mapping, kv, kv_layer, q, gate);                         \
     count_launch();                                                                                         \
@@ -681,7 +703,7 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
                             int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s) {
   if (T <= 0) return;
-  attention_merge_kernel<<<dim3(T, d.Hq), 128, 0, s>>>(ws, gate, token_pos, d.Hq, d.D, split_pages * kPageTokens,
+  launch_pdl(attention_merge_kernel, dim3(T, d.Hq), 128, 0, s, ws, gate, token_pos, d.Hq, d.D, split_pages * kPageTokens,
                                                        max_splits, out);
   count_launch();
 }
@@ -691,7 +713,7 @@ void launch_route(const float* logits, int ld, int splits, size_t split_stride, 
   if (E > 1024) throw std::invalid_argument("more than 1024 experts");
   if (splits > 8) throw std::invalid_argument("router split-K above 8");
   if (T <= 0) return;
-  route_kernel<<<T, 256, 0, s>>>(logits, ld, splits, split_stride, E, top, ids, weights, logits_out);
+  launch_pdl(route_kernel, T, 256, 0, s, logits, ld, splits, split_stride, E, top, ids, weights, logits_out);
   count_launch();
 }
 
@@ -705,7 +727,7 @@ void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t
                                    200 * 1024));
     configured = true;
   }
-  expert_sort_kernel<<<1, 1024, smem, s>>>(ids, n_assign, n_experts, counts, offsets, perm, inv);
+  launch_pdl(expert_sort_kernel, 1, 1024, smem, s, ids, n_assign, n_experts, counts, offsets, perm, inv);
   count_launch();
 }
 
@@ -715,7 +737,7 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
   if (slots > 64 || H > 8 * 1024 || H % 2) throw std::invalid_argument("combine geometry");
-  moe_combine_kernel<<<T, std::max(64, row_threads(H)), 0, s>>>(x, y_sorted, inv, weights, H, slots, norm_w, eps,
+  launch_pdl(moe_combine_kernel, T, std::max(64, row_threads(H)), 0, s, x, y_sorted, inv, weights, H, slots, norm_w, eps,
                                                                 hb);
   count_launch();
 }
@@ -723,14 +745,14 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
 void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
                         __nv_bfloat16* dst, cudaStream_t s) {
   if (n <= 0) return;
-  gather_rows_kernel<<<n, 128, 0, s>>>(src, ld, perm, div, H, dst);
+  launch_pdl(gather_rows_kernel, n, 128, 0, s, src, ld, perm, div, H, dst);
   count_launch();
 }
 
 void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err,
                    cudaStream_t s) {
   if (rows <= 0) return;
-  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, tokens, err);
+  launch_pdl(argmax_kernel, rows, 1024, 0, s, logits, V, tokens, err);
   count_launch();
 }
 

@@ -308,6 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   int32_t* act = goff + (kMaxGroups + 1);                      // [non-empty groups], then their count
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  // Dependencies on earlier kernels: the activations (warp 2), the outputs
+  // (epilogue) and, grouped, the group offsets read below. In dense mode the
+  // weight producer and the dequant/MMA warps start on the constant weights
+  // while the previous kernel finishes.
+  if (a.mode != kGemmStoreF32 || warp == 2 || warp >= kEpiWarp0) pdl_wait();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWSlots; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
     for (int i = 0; i < NSB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
@@ -599,7 +605,7 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
   const int grid = std::max(1, std::min(items, sm_count));
   if (smem > 227 * 1024) throw std::invalid_argument("tcgen05 GEMM shared memory above 227 KB");
-  qgemm_tc_kernel<<<grid, kThreads, smem, s>>>(bmap, a);
+  launch_pdl(qgemm_tc_kernel, grid, kThreads, smem, s, bmap, a);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
