@@ -36,7 +36,6 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
                     float* __restrict__ gb_out) {
   pdl_trigger();
   pdl_wait();
-  constexpr int NC = 2 * DK + R * DV;
   __shared__ float qs[DK], ks[DK];
   __shared__ float qk_scale[2];
   const int seq = blockIdx.x, kh = blockIdx.y;
@@ -222,7 +221,8 @@ __global__ void __launch_bounds__(256)
 
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
                 const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool, int gdn_index,
-                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, cudaStream_t s) {
+                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int /*sm_count*/,
+                cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
   bool done = false;

@@ -311,22 +311,52 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
 }
 
 // Merge split partials, apply the output gate sigmoid(gate), write bf16.
+// The split weights exp(m_s - M) / sum_s l_s exp(m_s - M) are computed once
+// per (token, head) into shared memory (dynamic: max_splits floats).
 __global__ void attention_merge_kernel(const float* __restrict__ ws, const float* __restrict__ gate,
                                        const int32_t* __restrict__ token_pos, int Hq, int D, int spl,
                                        int max_splits, __nv_bfloat16* out) {
   pdl_trigger();
   pdl_wait();
+  extern __shared__ float wsplit[];
+  __shared__ float red[32];
+  __shared__ float s_max, s_den;
   const int t = blockIdx.x, h = blockIdx.y;
   const int n = (token_pos[t] + 1 + spl - 1) / spl;
   const float* base = ws + (size_t(t) * Hq + h) * max_splits * (D + 2);
-  float M = -FLT_MAX;
-  for (int s = 0; s < n; ++s) M = fmaxf(M, base[s * (D + 2)]);
+  float m = -FLT_MAX;
+  for (int s = threadIdx.x; s < n; s += blockDim.x) m = fmaxf(m, base[s * (D + 2)]);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -FLT_MAX;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) M = fmaxf(M, red[w]);
+    s_max = M;
+  }
+  __syncthreads();
+  const float M = s_max;
   float den = 0.f;
-  for (int s = 0; s < n; ++s) den += base[s * (D + 2) + 1] * __expf(base[s * (D + 2)] - M);
+  for (int s = threadIdx.x; s < n; s += blockDim.x) {
+    const float e = __expf(base[s * (D + 2)] - M);
+    wsplit[s] = e;
+    den += base[s * (D + 2) + 1] * e;
+  }
+  den = warp_sum(den);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = den;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[w];
+    s_den = tot;
+  }
+  __syncthreads();
+  const float inv = 1.f / s_den;
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
     float num = 0.f;
-    for (int s = 0; s < n; ++s) num += base[s * (D + 2) + 2 + i] * __expf(base[s * (D + 2)] - M);
-    const float y = num / den * sigmoidf_(gate[(size_t(t) * Hq + h) * D + i]);
+    for (int s = 0; s < n; ++s) num += base[s * (D + 2) + 2 + i] * wsplit[s];
+    const float y = num * inv * sigmoidf_(gate[(size_t(t) * Hq + h) * D + i]);
     out[size_t(t) * Hq * D + h * D + i] = __float2bfloat16_rn(y);
   }
 }
@@ -560,37 +590,68 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int ld
 
 // Greedy selection per row: IEEE total order, lowest index on ties
 // (native/selection.h:3-12); any non-finite logit raises kErrNonFinite.
-__global__ void argmax_kernel(const float* __restrict__ logits, int V, uint32_t* tokens, uint32_t* err) {
+// Grid (rows, kArgmaxSplit): each CTA scans a slice of the row with float4
+// loads and four independent running maxima; the last CTA of a row (counted
+// in done[row], which it resets) reduces the slice maxima. The packed key
+// (total order << 32 | ~index) makes the result independent of the order.
+constexpr int kArgmaxSplit = 8;
+__global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int V, uint32_t* tokens,
+                                                     uint32_t* err, uint64_t* part, uint32_t* done) {
   pdl_trigger();
   pdl_wait();
-  __shared__ uint64_t red[32];
-  const int r = blockIdx.x;
+  __shared__ uint64_t red[16];
+  __shared__ bool last;
+  const int r = blockIdx.x, sp = blockIdx.y;
   const float* lr = logits + size_t(r) * V;
-  uint64_t best = 0;
+  const int per = ((V + kArgmaxSplit - 1) / kArgmaxSplit + 3) & ~3;
+  const int i0 = sp * per, i1 = min(V, i0 + per);
+  uint64_t best[4] = {0, 0, 0, 0};
   bool finite = true;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float f = lr[i];
+  auto take = [&](int k, float f, int i) {
     finite &= isfinite(f);
-    const uint64_t k = (uint64_t(total_key(f)) << 32) | uint32_t(0xFFFFFFFFu - i);
-    best = k > best ? k : best;
+    const uint64_t key = (uint64_t(total_key(f)) << 32) | uint32_t(0xFFFFFFFFu - i);
+    best[k] = key > best[k] ? key : best[k];
+  };
+  if ((V & 3) == 0) {
+    for (int i = i0 + 4 * threadIdx.x; i < i1; i += 4 * blockDim.x) {  // i1 - i0 is a multiple of 4
+      const float4 f = *reinterpret_cast<const float4*>(lr + i);
+      take(0, f.x, i);
+      take(1, f.y, i + 1);
+      take(2, f.z, i + 2);
+      take(3, f.w, i + 3);
+    }
+  } else {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) take(0, lr[i], i);
   }
+  uint64_t b = best[0];
+#pragma unroll
+  for (int k = 1; k < 4; ++k) b = best[k] > b ? best[k] : b;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-    best = other > best ? other : best;
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, b, o);
+    b = other > b ? other : b;
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) red[warp] = best;
+  if (lane == 0) red[warp] = b;
   if (!finite) atomicOr(err, kErrNonFinite);
   __syncthreads();
-  if (warp == 0) {
-    best = lane < int(blockDim.x >> 5) ? red[lane] : 0;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
+  if (threadIdx.x == 0) {
+    uint64_t m = 0;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) m = red[w] > m ? red[w] : m;
+    part[size_t(r) * kArgmaxSplit + sp] = m;
+    __threadfence();
+    last = atomicAdd(&done[r], 1u) == kArgmaxSplit - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    uint64_t m = 0;
+    for (int k = 0; k < kArgmaxSplit; ++k) {
+      const uint64_t v = *reinterpret_cast<volatile uint64_t*>(&part[size_t(r) * kArgmaxSplit + k]);
+      m = v > m ? v : m;
     }
-    if (lane == 0) tokens[r] = 0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu);
+    tokens[r] = 0xFFFFFFFFu - uint32_t(m & 0xFFFFFFFFu);
+    done[r] = 0;
   }
 }
 
@@ -703,7 +764,8 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
                             int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s) {
   if (T <= 0) return;
-  launch_pdl(attention_merge_kernel, dim3(T, d.Hq), 128, 0, s, ws, gate, token_pos, d.Hq, d.D, split_pages * kPageTokens,
+  launch_pdl(attention_merge_kernel, dim3(T, d.Hq), 128, size_t(max_splits) * sizeof(float), s, ws, gate, token_pos,
+             d.Hq, d.D, split_pages * kPageTokens,
                                                        max_splits, out);
   count_launch();
 }
@@ -749,10 +811,10 @@ void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, i
   count_launch();
 }
 
-void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err,
-                   cudaStream_t s) {
+void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err, uint64_t* part,
+                   uint32_t* done, cudaStream_t s) {
   if (rows <= 0) return;
-  launch_pdl(argmax_kernel, rows, 1024, 0, s, logits, V, tokens, err);
+  launch_pdl(argmax_kernel, dim3(rows, kArgmaxSplit), 512, 0, s, logits, V, tokens, err, part, done);
   count_launch();
 }
 

@@ -91,7 +91,7 @@ void launch_qgemm(const GemmArgs& a, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                 size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
                 int gdn_index, __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
-                cudaStream_t s);
+                int sm_count, cudaStream_t s);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);
@@ -103,8 +103,8 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
                         float eps, __nv_bfloat16* hb, const int32_t* out_token, int rows,
                         float* hidden_f32, cudaStream_t s);
-void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err,
-                   cudaStream_t s);
+void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err, uint64_t* part,
+                   uint32_t* done, cudaStream_t s);
 void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,
                         GdnPool pool, int slot, const Dims& d, uint64_t seed, cudaStream_t s);
 void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,

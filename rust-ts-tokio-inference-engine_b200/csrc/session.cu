@@ -143,6 +143,8 @@ struct Session {
   DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
   DevBuf<float> gdn_qk, gdn_v, gdn_gb;  // DeltaNet prepared q/k, v, (decay, beta) per token
   DevBuf<int2> attn_items;              // attention work list: (token, KV split) pairs
+  DevBuf<uint64_t> argmax_part;         // per-row slice maxima of the split argmax
+  DevBuf<uint32_t> argmax_done;         // per-row slice counters (kept at zero between launches)
   int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
   int sm_count = 148;
@@ -334,6 +336,9 @@ struct Session {
     out_token.ensure(T);
     tokens.ensure(T);
     sampled.ensure(max_rows);
+    argmax_part.ensure(size_t(max_rows) * 8);
+    argmax_done.ensure(max_rows);
+    QWEN_CUDA(cudaMemset(argmax_done.p, 0, size_t(max_rows) * 4));
     err.ensure(1);
     x.ensure(size_t(T) * d.H);
     const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
@@ -665,7 +670,7 @@ struct Session {
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
         launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, gdn, ly.type_index,
-                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, s);
+                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, s);
         stage(5);  // RecurrentOutput
       } else {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
@@ -704,7 +709,7 @@ struct Session {
     logits.ensure(size_t(R) * d.V);
     dense(m.lm_head, hb_out.p, max_rows, R, logits.p, d.V, size_t(R) * d.V, 1, s);
     stage(18);  // StateValidation (finite check + greedy selection)
-    launch_argmax(logits.p, R, d.V, sampled.p, err.p, s);
+    launch_argmax(logits.p, R, d.V, sampled.p, err.p, argmax_part.p, argmax_done.p, s);
     launches += 1;
   }
 
