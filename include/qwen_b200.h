@@ -204,16 +204,21 @@ int rs_qwen_device_step_ragged(void* session, size_t n_seq, const StateId* paren
                                size_t logits_count, char* error, size_t capacity);
 
 /* Speculative verify + accept over a ragged batch, on the device.
- * Sequence s: parents[s] holds target logits' argmax seed[s] (the greedy token
- * after the parent, already emitted), and drafts[s*width .. +ndraft[s]] are
- * MTP proposals. The call runs the target over [seed, drafts...] for every
- * sequence in one ragged step, computes the accepted length with the
- * reference's plan() rule (src/serving/native_speculative.rs:74-128: accept
- * while draft[i] == argmax(row i) and not EOS), and compacts KV pages and
- * DeltaNet state on the device to the version after the emitted tokens
- * (replay semantics of native_mtp_decode.rs:238-272 without a replay).
- * Outputs per sequence: accepted[s], emitted tokens (width+1 per sequence,
- * n_emitted[s] valid), outs[s] = the compacted version. */
+ * Sequence s: parents[s] is a published version at position p; seeds[s] is
+ * the greedy token after it (already emitted, not yet fed) and
+ * drafts[s*width .. +ndraft[s]] (ndraft[s] <= width <= 8) are MTP proposals.
+ * The call feeds [seed, drafts...] to the target in one ragged step (greedy
+ * row r_j after fed token j), then applies the reference's plan() rule
+ * (src/serving/native_speculative.rs:74-128): emit r_0, r_1, ... while
+ * draft j == r_j and r_j is not an EOS; the first mismatch or EOS is emitted
+ * and ends the plan; after all drafts match, the bonus r_k is emitted if the
+ * context has room. accepted[s] = matched drafts (a matched EOS counts),
+ * emitted[s*(width+1) ..] / n_emitted[s] = the emitted tokens, and outs[s] =
+ * the version after [seed, d_0 .. d_{accepted-1}] (position p + 1 + accepted):
+ * its DeltaNet state was written per token during the step and its KV pages
+ * are the step's, truncated (compaction on the device; no replay). With
+ * RS_QWEN_RAGGED_HIDDEN the version keeps the post-norm hidden rows of the
+ * accepted tokens. Parents stay published. */
 int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId* parents,
                                      const uint32_t* seeds, const uint32_t* drafts,
                                      const uint32_t* ndraft, size_t width, const uint32_t* eos,

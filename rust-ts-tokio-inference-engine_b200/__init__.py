@@ -279,6 +279,27 @@ class DeviceSession:
     def release(self, sid: StateId):
         _call("rs_qwen_device_release", self.h, C.byref(sid))
 
+    def verify_accept(self, parents, seeds, drafts, eos=(), flags=0, width=None):
+        """Speculative verify + accept (rs_qwen_device_mtp_verify_accept).
+        drafts: list of per-sequence draft lists. Returns (outs, accepted, emitted lists)."""
+        n = len(parents)
+        width = max([len(x) for x in drafts] + [0]) if width is None else width
+        par = (StateId * n)(*parents)
+        seed = np.ascontiguousarray(seeds, np.uint32)
+        nd = np.array([len(x) for x in drafts], np.uint32)
+        dr = np.zeros((n, max(width, 1)), np.uint32)
+        for i, x in enumerate(drafts):
+            dr[i, :len(x)] = x
+        eo = np.ascontiguousarray(eos, np.uint32)
+        outs = (StateId * n)()
+        acc = np.zeros(n, np.uint32)
+        em = np.zeros((n, width + 1), np.uint32)
+        ne = np.zeros(n, np.uint32)
+        _call("rs_qwen_device_mtp_verify_accept", self.h, n, par, _ptr(seed, C.c_uint32), _ptr(dr, C.c_uint32),
+              _ptr(nd, C.c_uint32), width, _ptr(eo, C.c_uint32) if len(eo) else None, len(eo), flags, outs,
+              _ptr(acc, C.c_uint32), _ptr(em, C.c_uint32), _ptr(ne, C.c_uint32))
+        return list(outs), [int(a) for a in acc], [list(map(int, em[i, :ne[i]])) for i in range(n)]
+
     def snapshot(self, sid: StateId):
         n = state_count(self.cfg)
         out = np.zeros(n, np.float32)

@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
                     const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                     int hk, int hv, int conv, const float* __restrict__ conv_w, const float* __restrict__ a_log,
                     const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
-                    float* __restrict__ gb_out) {
+                    float* __restrict__ gb_out, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
   __shared__ float qs[DK], ks[DK];
@@ -75,6 +75,12 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
 #pragma unroll
     for (int j = 0; j < 7; ++j)
       if (j < conv - 1) taps[j] = j + 1 < conv - 1 ? taps[j + 1] : cur;
+    if (d.cand >= 0) {  // verify step: the history after token i is candidate i's conv state
+      float* cc = pool.conv + (size_t(cand_slots[d.cand + i]) * pool.n_gdn + li) * cl;
+#pragma unroll
+      for (int j = 0; j < 7; ++j)
+        if (j < conv - 1) cc[size_t(j) * cd + gc] = taps[j];
+    }
     const float act = siluf_(acc);
     if (c < DK) qs[c] = act;
     else if (c < 2 * DK) ks[c - DK] = act;
@@ -105,9 +111,11 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
     }
     __syncthreads();
   }
+  if (d.cand < 0) {
 #pragma unroll
-  for (int j = 0; j < 7; ++j)
-    if (j < conv - 1) dst_conv[size_t(j) * cd + gc] = taps[j];
+    for (int j = 0; j < 7; ++j)
+      if (j < conv - 1) dst_conv[size_t(j) * cd + gc] = taps[j];
+  }
 }
 
 template <int DK, int DV>
@@ -116,7 +124,7 @@ __global__ void __launch_bounds__(256)
                       int hk, int hv, const float* __restrict__ qk, const float* __restrict__ vv,
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
-                      __nv_bfloat16* __restrict__ out, uint32_t* err) {
+                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
@@ -183,6 +191,17 @@ __global__ void __launch_bounds__(256)
       rd = warp_sum(rd);
       if (lane == 0) os[r] = rd;
     }
+    if (d.cand >= 0) {  // verify step: the state after this token is candidate `it`'s state
+      float* cs = pool.state + (size_t(cand_slots[d.cand + it]) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
+#pragma unroll
+      for (int i = 0; i < RPW; ++i) {
+        Vec v;
+        float* f = reinterpret_cast<float*>(&v);
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) f[j] = S[i][j];
+        *reinterpret_cast<Vec*>(cs + size_t(warp * RPW + i) * DK + lane * CPL) = v;
+      }
+    }
     __syncthreads();
     // gated RMSNorm over dv (native/qwen_model.inc:203-204)
     float o = threadIdx.x < DV ? os[threadIdx.x] : 0.f;
@@ -212,7 +231,7 @@ __global__ void __launch_bounds__(256)
       f[j] = S[i][j];
       finite &= isfinite(S[i][j]);
     }
-    *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = v;
+    if (d.cand < 0) *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = v;
   }
   if (!finite) atomicOr(err, kErrNonFinite);
 }
@@ -222,7 +241,7 @@ __global__ void __launch_bounds__(256)
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
                 const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool, int gdn_index,
                 __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int /*sm_count*/,
-                cudaStream_t s) {
+                const int32_t* cand_slots, cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
   bool done = false;
@@ -230,10 +249,11 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \
     launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
         proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
-        ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf);                                                            \
+        ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf, cand_slots);                                                \
     launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, 0, s, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
                                                                 qk_buf, v_buf, gb_buf, proj, ld_proj, splits,    \
-                                                                split_stride, d.cd, ly.gnorm, d.eps, out, err);  \
+                                                                split_stride, d.cd, ly.gnorm, d.eps, out, err,   \
+                                                                cand_slots);                                     \
     done = true;                                                                                                 \
   }
   QWEN_GDN(128, 128, 2)

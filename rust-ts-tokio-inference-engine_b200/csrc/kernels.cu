@@ -655,6 +655,78 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
   }
 }
 
+// Speculative accept, one thread per sequence (the plan() rule of
+// src/serving/native_speculative.rs:100-127). A verify step fed
+// [seed, d_0 .. d_{k-1}] from the parent and sampled rows r_0 .. r_k (r_j =
+// greedy token after fed token j). Emitted tokens are r_0, r_1, ... while
+// d_i == r_i and r_i is not EOS; the first mismatch (or an EOS) is emitted and
+// ends the plan; after k matches the bonus r_k is emitted if the context still
+// has room (remaining = ctx - position - 1). accepted = matched drafts (an EOS
+// that matched counts), so the new state is the state after token
+// `accepted` of the fed sequence.
+__global__ void accept_kernel(const SeqDesc* __restrict__ descs, int n, const int32_t* __restrict__ cu_seqlens,
+                              const uint32_t* __restrict__ tokens, const uint32_t* __restrict__ sampled,
+                              const uint32_t* __restrict__ eos, int n_eos, int ctx, int32_t* acc_out,
+                              uint32_t* emitted, int emit_stride, uint32_t* n_emitted) {
+  pdl_trigger();
+  pdl_wait();
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n) return;
+  const SeqDesc d = descs[s];
+  const int k = d.count - 1, t0 = cu_seqlens[s];
+  const int remaining = ctx - d.position - 1;
+  auto is_eos = [&](uint32_t t) {
+    for (int e = 0; e < n_eos; ++e)
+      if (eos[e] == t) return true;
+    return false;
+  };
+  uint32_t* em = emitted + size_t(s) * emit_stride;
+  int ne = 0, acc = 0;
+  bool stopped = false;
+  for (int i = 0; i < k; ++i) {
+    const uint32_t target = sampled[d.out_row0 + i];
+    em[ne++] = target;
+    const bool term = is_eos(target);
+    const uint32_t draft = tokens[t0 + 1 + i];
+    if (draft != target || term) {
+      acc += draft == target;
+      stopped = true;
+      break;
+    }
+    ++acc;
+  }
+  if (!stopped && ne < remaining) em[ne++] = sampled[d.out_row0 + k];
+  acc_out[s] = acc;
+  n_emitted[s] = uint32_t(ne);
+}
+
+// Verify compaction: the state after token `accepted` (candidate slot
+// cand_slots[cand + accepted]) becomes the sequence's version. Its DeltaNet
+// state and conv history were written there by the step; here its block-table
+// row (the pages of positions < position + accepted + 1) is copied from the
+// full-length candidate's row and, when kept, its hidden rows are written.
+__global__ void verify_compact_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cand_slots,
+                                      const int32_t* __restrict__ acc, int32_t* block_table, int stride,
+                                      const float* __restrict__ hidden_stage, const int32_t* __restrict__ cu_seqlens,
+                                      float* hidden_pool, int chunk, int H) {
+  pdl_trigger();
+  pdl_wait();
+  const int s = blockIdx.x;
+  const SeqDesc d = descs[s];
+  const int a = acc[s];
+  const int chosen = cand_slots[d.cand + a];
+  if (chosen != d.child) {
+    const int n_keep = (d.position + a + 1 + kPageTokens - 1) / kPageTokens;
+    for (int j = threadIdx.x; j < n_keep; j += blockDim.x)
+      block_table[size_t(chosen) * stride + j] = block_table[size_t(d.child) * stride + j];
+  }
+  if (d.hidden) {
+    const float* src = hidden_stage + size_t(cu_seqlens[s]) * H;
+    float* dst = hidden_pool + size_t(chosen) * chunk * H;
+    for (int i = threadIdx.x; i < (a + 1) * H; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
 // Seeded synthetic prefix state: KV bf16 N(0,1) for positions < position,
 // DeltaNet S fp32 N(0, 0.02), conv history fp32 N(0, 1). Values depend on
 // (seed, layer, element), never on the page or slot they land in.
@@ -808,6 +880,24 @@ void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, i
                         __nv_bfloat16* dst, cudaStream_t s) {
   if (n <= 0) return;
   launch_pdl(gather_rows_kernel, n, 128, 0, s, src, ld, perm, div, H, dst);
+  count_launch();
+}
+
+void launch_accept(const SeqDesc* descs, int n, const int32_t* cu_seqlens, const uint32_t* tokens,
+                   const uint32_t* sampled, const uint32_t* eos, int n_eos, int ctx, int32_t* acc, uint32_t* emitted,
+                   int emit_stride, uint32_t* n_emitted, cudaStream_t s) {
+  if (n <= 0) return;
+  launch_pdl(accept_kernel, (n + 127) / 128, 128, 0, s, descs, n, cu_seqlens, tokens, sampled, eos, n_eos, ctx, acc,
+             emitted, emit_stride, n_emitted);
+  count_launch();
+}
+
+void launch_verify_compact(const SeqDesc* descs, int n, const int32_t* cand_slots, const int32_t* acc,
+                           int32_t* block_table, int stride, const float* hidden_stage, const int32_t* cu_seqlens,
+                           float* hidden_pool, int chunk, int H, cudaStream_t s) {
+  if (n <= 0) return;
+  launch_pdl(verify_compact_kernel, n, 256, 0, s, descs, cand_slots, acc, block_table, stride, hidden_stage,
+             cu_seqlens, hidden_pool, chunk, H);
   count_launch();
 }
 

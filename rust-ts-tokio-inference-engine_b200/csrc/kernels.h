@@ -21,6 +21,8 @@ struct SeqDesc {
   int32_t cow_src;    // page copied into the first new page (copy-on-write), -1 none
   int32_t cow_len;    // tokens copied by the copy-on-write
   int32_t hidden;     // keep post-norm hidden rows in the child slot
+  int32_t cand;       // verify steps: offset of this sequence's per-token state slots in the
+                      // candidate list (slot of the state after token j = cand_slots[cand + j]), -1 none
 };
 
 // Device-built packing results.
@@ -91,7 +93,7 @@ void launch_qgemm(const GemmArgs& a, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                 size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
                 int gdn_index, __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
-                int sm_count, cudaStream_t s);
+                int sm_count, const int32_t* cand_slots, cudaStream_t s);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);
@@ -103,6 +105,12 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
                         float eps, __nv_bfloat16* hb, const int32_t* out_token, int rows,
                         float* hidden_f32, cudaStream_t s);
+void launch_accept(const SeqDesc* descs, int n, const int32_t* cu_seqlens, const uint32_t* tokens,
+                   const uint32_t* sampled, const uint32_t* eos, int n_eos, int ctx, int32_t* acc, uint32_t* emitted,
+                   int emit_stride, uint32_t* n_emitted, cudaStream_t s);
+void launch_verify_compact(const SeqDesc* descs, int n, const int32_t* cand_slots, const int32_t* acc,
+                           int32_t* block_table, int stride, const float* hidden_stage, const int32_t* cu_seqlens,
+                           float* hidden_pool, int chunk, int H, cudaStream_t s);
 void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err, uint64_t* part,
                    uint32_t* done, cudaStream_t s);
 void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,

@@ -109,6 +109,8 @@ struct Version {
 
 constexpr size_t kStatsCount = 17 + 19 * 3;
 constexpr int kMaxSplits = 8;
+constexpr int kMaxDraft = 8;  // drafts per verified sequence (native_speculative.rs: at most 8)
+constexpr int kMaxEos = 64;
 
 struct Session {
   WeightStore* store = nullptr;
@@ -145,6 +147,9 @@ struct Session {
   DevBuf<int2> attn_items;              // attention work list: (token, KV split) pairs
   DevBuf<uint64_t> argmax_part;         // per-row slice maxima of the split argmax
   DevBuf<uint32_t> argmax_done;         // per-row slice counters (kept at zero between launches)
+  // speculative verify: per-token candidate state slots, EOS list, accept results
+  DevBuf<int32_t> cand_dev, acc_dev;
+  DevBuf<uint32_t> eos_dev, emitted_dev, nemit_dev;
   int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
   int sm_count = 148;
@@ -339,6 +344,11 @@ struct Session {
     argmax_part.ensure(size_t(max_rows) * 8);
     argmax_done.ensure(max_rows);
     QWEN_CUDA(cudaMemset(argmax_done.p, 0, size_t(max_rows) * 4));
+    cand_dev.ensure(T);
+    acc_dev.ensure(max_seqs);
+    eos_dev.ensure(kMaxEos);
+    emitted_dev.ensure(size_t(max_seqs) * (kMaxDraft + 1));
+    nemit_dev.ensure(max_seqs);
     err.ensure(1);
     x.ensure(size_t(T) * d.H);
     const int proj_w = std::max({d.gdn_in_rows, d.attn_in_rows, d.E + 1});
@@ -401,17 +411,40 @@ struct Session {
     uint32_t position, count;
     const uint32_t* tokens;
   };
+  // Speculative verify (rs_qwen_device_mtp_verify_accept): each sequence's
+  // tokens are [seed, drafts...]; results per sequence.
+  struct VerifyIn {
+    const uint32_t* eos;
+    size_t n_eos;
+    uint32_t* accepted;
+    uint32_t* emitted;  // [n][emit_stride]
+    size_t emit_stride;
+    uint32_t* n_emitted;
+  };
 
   // Runs one ragged step. Outputs: outs[s], then per output row a sampled
   // token and/or fp32 logits. Throws on any error after rolling back.
   void step(const std::vector<SeqIn>& seqs, uint32_t flags, StateId* outs, uint32_t* sampled_out,
-            float* logits_out) {
+            float* logits_out, const VerifyIn* vin = nullptr) {
     set_device();
     const uint64_t t_start = now_ns();
     ++calls;
     const int n = int(seqs.size());
     if (n <= 0) throw std::invalid_argument("ragged step needs at least one sequence");
     if (n > max_seqs) throw std::invalid_argument("too many sequences in one step");
+    if (vin) {
+      if (flags & (RS_QWEN_RAGGED_CONSUME | RS_QWEN_RAGGED_LOGITS))
+        throw std::invalid_argument("verify steps keep their parents and return no logits");
+      if (vin->n_eos > size_t(kMaxEos)) throw std::invalid_argument("too many EOS tokens");
+      flags |= RS_QWEN_RAGGED_ALL_ROWS;
+      size_t cand_total = 0;
+      for (const auto& s : seqs) {
+        if (!s.parent) throw std::invalid_argument("verify needs a parent version per sequence");
+        if (s.count < 1 || s.count > uint32_t(kMaxDraft + 1)) throw std::invalid_argument("draft count above 8");
+        cand_total += s.count;
+      }
+      if (table->residents() + cand_total > slots) throw std::runtime_error("combined resident budget exhausted");
+    }
     const bool consume = flags & RS_QWEN_RAGGED_CONSUME;
     const bool all_rows = flags & RS_QWEN_RAGGED_ALL_ROWS;
     const bool keep_hidden = flags & RS_QWEN_RAGGED_HIDDEN;
@@ -471,6 +504,8 @@ struct Session {
     std::vector<StateId> reserved;
     std::vector<int32_t> deferred_free;
     std::vector<int> tok_off(n + 1, 0);
+    std::vector<std::vector<StateId>> cands(vin ? n : 0);  // verify: per token's candidate version
+    std::vector<int32_t> cand_host;
     // On failure every page reference taken for a child is dropped (shared
     // pages were either ref'd or inherited from a consumed parent), and
     // consumed parents' dropped pages are released too.
@@ -538,6 +573,20 @@ struct Session {
         sd.hidden = keep_hidden ? 1 : 0;
         const uint64_t charge = version_bytes(cp.size(), keep_hidden ? cnt : 0);
         StateId id;
+        sd.cand = -1;
+        if (vin) {
+          // one candidate version per fed token, charged for its own length
+          sd.cand = int32_t(cand_host.size());
+          for (int j = 0; j < cnt; ++j) {
+            const size_t pj = d.n_attn > 0 ? size_t(pos + j + 1 + kPageTokens - 1) / kPageTokens : 0;
+            const StateId cj = table->reserve(s.position + j + 1, version_bytes(pj, keep_hidden ? j + 1 : 0));
+            reserved.push_back(cj);
+            cands[i].push_back(cj);
+            cand_host.push_back(int32_t(cj.slot));
+          }
+          sd.child = cand_host.back();
+          continue;
+        }
         if (consume && s.parent) {
           // consume: the parent's pages move to the child; a dropped COW page is freed after the step
           std::vector<int32_t> parent_pages = par[i]->pages;
@@ -569,6 +618,12 @@ struct Session {
       if (!npages.empty())
         QWEN_CUDA(cudaMemcpyAsync(new_pages.p, hp, npages.size() * 4, cudaMemcpyHostToDevice, stream));
       QWEN_CUDA(cudaMemcpyAsync(tokens.p, ht, size_t(T) * 4, cudaMemcpyHostToDevice, stream));
+      if (vin) {
+        QWEN_CUDA(cudaMemcpyAsync(cand_dev.p, cand_host.data(), cand_host.size() * 4, cudaMemcpyHostToDevice,
+                                  stream));
+        if (vin->n_eos)
+          QWEN_CUDA(cudaMemcpyAsync(eos_dev.p, vin->eos, vin->n_eos * 4, cudaMemcpyHostToDevice, stream));
+      }
       QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, stream));
       if (!items.empty()) {
         attn_items.ensure(items.size());
@@ -588,9 +643,22 @@ struct Session {
         last_R = R;
       }
       forward(n, T, R, max_len, keep_hidden, logits_out != nullptr);
+      std::vector<int32_t> acc_h(vin ? n : 0);
+      std::vector<uint32_t> emit_h(vin ? size_t(n) * (kMaxDraft + 1) : 0), nemit_h(vin ? n : 0);
+      if (vin) {
+        launch_accept(descs.p, n, cu_seqlens.p, tokens.p, sampled.p, eos_dev.p, int(vin->n_eos), d.ctx, acc_dev.p,
+                      emitted_dev.p, kMaxDraft + 1, nemit_dev.p, stream);
+        launch_verify_compact(descs.p, n, cand_dev.p, acc_dev.p, block_table.p, bt_stride, hidden_stage.p,
+                              cu_seqlens.p, hidden_pool.p, d.chunk, d.H, stream);
+      }
       stage_close();
       QWEN_CUDA(cudaEventRecord(ev_end, stream));
-      if (keep_hidden)
+      if (vin) {
+        QWEN_CUDA(cudaMemcpyAsync(acc_h.data(), acc_dev.p, size_t(n) * 4, cudaMemcpyDeviceToHost, stream));
+        QWEN_CUDA(cudaMemcpyAsync(emit_h.data(), emitted_dev.p, emit_h.size() * 4, cudaMemcpyDeviceToHost, stream));
+        QWEN_CUDA(cudaMemcpyAsync(nemit_h.data(), nemit_dev.p, size_t(n) * 4, cudaMemcpyDeviceToHost, stream));
+      }
+      if (keep_hidden && !vin)
         for (int i = 0; i < n; ++i)
           QWEN_CUDA(cudaMemcpyAsync(hidden_pool.p + size_t(hd[i].child) * d.chunk * d.H,
                                     hidden_stage.p + size_t(tok_off[i]) * d.H, size_t(seqs[i].count) * d.H * 4,
@@ -619,6 +687,35 @@ struct Session {
       }
       if (h_err & kErrNonFinite) throw std::runtime_error("nonfinite device state");
       if (h_err) throw std::runtime_error("device step error flag " + std::to_string(h_err));
+      if (vin) {
+        // publish the candidate after `accepted` drafts; roll the others back
+        for (int i = 0; i < n; ++i) {
+          const int a = acc_h[i], pos = int(seqs[i].position);
+          if (a < 0 || a >= int(seqs[i].count) || nemit_h[i] > uint32_t(kMaxDraft + 1))
+            throw std::runtime_error("verify accept result out of range");
+          Version v;
+          v.pages = child_pages[i];
+          const int len = pos + a + 1;
+          const size_t keep = d.n_attn > 0 ? size_t(len + kPageTokens - 1) / kPageTokens : 0;
+          std::vector<int32_t> dropped(v.pages.begin() + keep, v.pages.end());
+          v.pages.resize(keep);
+          if (keep) page_filled[v.pages.back()] = uint8_t(len - int(keep - 1) * kPageTokens);
+          v.hidden_rows = keep_hidden ? uint32_t(a + 1) : 0;
+          table->publish(cands[i][a], std::move(v));
+          for (int j = 0; j < int(cands[i].size()); ++j)
+            if (j != a) table->rollback(cands[i][j]);
+          unref_pages(dropped);
+          outs[i] = cands[i][a];
+          vin->accepted[i] = uint32_t(a);
+          vin->n_emitted[i] = nemit_h[i];
+          for (size_t e = 0; e < vin->emit_stride; ++e)
+            vin->emitted[i * vin->emit_stride + e] = e < nemit_h[i] ? emit_h[size_t(i) * (kMaxDraft + 1) + e] : 0u;
+        }
+        steps += uint64_t(n);
+        ++completed;
+        wall_ns += now_ns() - t_start;
+        return;
+      }
     } catch (...) {
       cudaStreamSynchronize(stream);
       fail_cleanup();
@@ -670,7 +767,7 @@ struct Session {
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
         launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, gdn, ly.type_index,
-                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, s);
+                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, cand_dev.p, s);
         stage(5);  // RecurrentOutput
       } else {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
@@ -1183,12 +1280,31 @@ int rs_qwen_device_mtp_snapshot(void* session, const StateId*, float*, size_t, c
     throw std::runtime_error("MTP head not available in this build");
   });
 }
-int rs_qwen_device_mtp_verify_accept(void* session, size_t, const StateId*, const uint32_t*, const uint32_t*,
-                                     const uint32_t*, size_t, const uint32_t*, size_t, uint32_t, StateId*,
-                                     uint32_t*, uint32_t*, uint32_t*, char* error, size_t capacity) {
+int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId* parents, const uint32_t* seeds,
+                                     const uint32_t* drafts, const uint32_t* ndraft, size_t width,
+                                     const uint32_t* eos, size_t n_eos, uint32_t flags, StateId* outs,
+                                     uint32_t* accepted, uint32_t* emitted, uint32_t* n_emitted, char* error,
+                                     size_t capacity) {
   return checked(error, capacity, [&] {
-    (void)S(session);
-    throw std::runtime_error("MTP verify not available in this build");
+    Session* s = S(session);
+    if (!n_seq || !parents || !seeds || !ndraft || !outs || !accepted || !emitted || !n_emitted ||
+        (width && !drafts) || (n_eos && !eos))
+      throw std::invalid_argument("verify descriptor");
+    if (width > size_t(kMaxDraft)) throw std::invalid_argument("draft width above 8");
+    if (flags & ~RS_QWEN_RAGGED_HIDDEN) throw std::invalid_argument("verify flags: only RS_QWEN_RAGGED_HIDDEN");
+    std::vector<uint32_t> fed;
+    std::vector<size_t> off(n_seq);
+    for (size_t i = 0; i < n_seq; ++i) {
+      if (ndraft[i] > width) throw std::invalid_argument("draft count above the width");
+      off[i] = fed.size();
+      fed.push_back(seeds[i]);
+      for (uint32_t j = 0; j < ndraft[i]; ++j) fed.push_back(drafts[i * width + j]);
+    }
+    std::vector<Session::SeqIn> seqs(n_seq);
+    for (size_t i = 0; i < n_seq; ++i)
+      seqs[i] = {&parents[i], uint32_t(parents[i].position), 1 + ndraft[i], fed.data() + off[i]};
+    Session::VerifyIn vin{eos, n_eos, accepted, emitted, width + 1, n_emitted};
+    s->step(seqs, flags, outs, nullptr, nullptr, &vin);
   });
 }
 

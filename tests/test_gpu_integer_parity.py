@@ -9,7 +9,7 @@ from conftest import has_cuda
 
 pytestmark = pytest.mark.gpu
 
-SEQ_DESC_INTS = 12
+SEQ_DESC_INTS = 13  # SeqDesc: position, count, parent, child, n_shared, new_off, n_new, out_row0, n_out, cow_src, cow_len, hidden, cand
 
 
 @pytest.fixture(scope="module")
