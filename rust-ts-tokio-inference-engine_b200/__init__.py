@@ -321,6 +321,31 @@ class DeviceSession:
         _call("rs_qwen_device_drain", self.h, C.byref(n))
         return n.value
 
+    def mtp_attach(self, store):
+        _call("rs_qwen_device_mtp_attach", self.h, store.h)
+
+    def mtp_step(self, previous, source, tokens, row: int = 0, draft_source: int = 0):
+        """One MTP draft step (rs_qwen_device_mtp_step); returns (draft version, last-row logits)."""
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        out = StateId()
+        logits = np.zeros(self.cfg.vocab, np.float32)
+        _call("rs_qwen_device_mtp_step", self.h, None if previous is None else C.byref(previous), C.byref(source),
+              draft_source, row, _ptr(tok, C.c_uint32), len(tok), C.byref(out), _ptr(logits, C.c_float),
+              logits.size, 0)
+        return out, logits
+
+    def mtp_release(self, sid: StateId):
+        _call("rs_qwen_device_mtp_release", self.h, C.byref(sid))
+
+    def mtp_snapshot(self, sid: StateId, rows: int):
+        """(K [kv, context, d], V [kv, context, d], hidden [rows, hidden]) of a draft version."""
+        c = self.cfg
+        per = c.kv_heads * c.context * c.head_dim
+        out = np.zeros(2 * per + rows * c.hidden, np.float32)
+        _call("rs_qwen_device_mtp_snapshot", self.h, C.byref(sid), _ptr(out, C.c_float), out.size)
+        kv = out[:2 * per].reshape(2, c.kv_heads, c.context, c.head_dim)
+        return kv[0], kv[1], out[2 * per:].reshape(rows, c.hidden)
+
     def synthetic_state(self, position: int, seed: int) -> StateId:
         out = StateId()
         _call("rs_qwen_device_synthetic_state", self.h, position, seed, C.byref(out))

@@ -655,6 +655,45 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
   }
 }
 
+// MTP draft input (native/qwen_mtp.inc:157-161): per token t,
+// cat[t] = [bf16(rms(embed(token_t)) * w_e), bf16(rms(hidden_t) * w_h)]
+// (the embedding dequantised from the 4-bit table as in embed_norm_kernel).
+__global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens, const float* __restrict__ hidden,
+                                 const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
+                                 __nv_bfloat16* __restrict__ cat) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[32];
+  extern __shared__ float erow[];  // [H]
+  const int t = blockIdx.x, H = embed.k;
+  const uint32_t tok = tokens[t];
+  float se = 0.f, sh = 0.f;
+  for (int w = threadIdx.x; w < H / 8; w += blockDim.x) {
+    const int c0 = w * 8;
+    const uint8_t* tile = embed.tile(int(tok / kTileRows), c0 / kTileK);
+    const int r = tok % kTileRows;
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + r * 32 + (c0 % kTileK) / 2);
+    const float sc = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+    const float bi = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = fmaf(sc, float(nibble(word, j)), bi);
+      erow[c0 + j] = v;
+      se += v * v;
+    }
+  }
+  const float* hr = hidden + size_t(t) * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) sh += hr[c] * hr[c];
+  const float tot_e = block_sum(se, red);
+  const float tot_h = block_sum(sh, red);
+  const float ie = rsqrtf(tot_e / H + eps), ih = rsqrtf(tot_h / H + eps);
+  __nv_bfloat16* out = cat + size_t(t) * 2 * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    out[c] = __float2bfloat16_rn(erow[c] * ie * w_e[c]);
+    out[H + c] = __float2bfloat16_rn(hr[c] * ih * w_h[c]);
+  }
+}
+
 // Speculative accept, one thread per sequence (the plan() rule of
 // src/serving/native_speculative.rs:100-127). A verify step fed
 // [seed, d_0 .. d_{k-1}] from the parent and sampled rows r_0 .. r_k (r_j =
@@ -880,6 +919,13 @@ void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, i
                         __nv_bfloat16* dst, cudaStream_t s) {
   if (n <= 0) return;
   launch_pdl(gather_rows_kernel, n, 128, 0, s, src, ld, perm, div, H, dst);
+  count_launch();
+}
+
+void launch_mtp_input(const QMat& embed, const uint32_t* tokens, int T, const float* hidden, const float* w_e,
+                      const float* w_h, float eps, __nv_bfloat16* cat, cudaStream_t s) {
+  if (T <= 0) return;
+  launch_pdl(mtp_input_kernel, T, 256, size_t(embed.k) * sizeof(float), s, embed, tokens, hidden, w_e, w_h, eps, cat);
   count_launch();
 }
 

@@ -105,6 +105,8 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
                         float eps, __nv_bfloat16* hb, const int32_t* out_token, int rows,
                         float* hidden_f32, cudaStream_t s);
+void launch_mtp_input(const QMat& embed, const uint32_t* tokens, int T, const float* hidden, const float* w_e,
+                      const float* w_h, float eps, __nv_bfloat16* cat, cudaStream_t s);
 void launch_accept(const SeqDesc* descs, int n, const int32_t* cu_seqlens, const uint32_t* tokens,
                    const uint32_t* sampled, const uint32_t* eos, int n_eos, int ctx, int32_t* acc, uint32_t* emitted,
                    int emit_stride, uint32_t* n_emitted, cudaStream_t s);

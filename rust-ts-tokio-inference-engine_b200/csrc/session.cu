@@ -107,6 +107,14 @@ struct Version {
   uint32_t hidden_rows = 0;    // post-norm hidden rows kept (hidden_* calls)
 };
 
+// MTP draft version (native/qwen_mtp.inc): KV of the MTP attention layer for
+// [0, position) in the draft page pool, and the MTP head's post-norm hidden
+// rows of the step that made it.
+struct DraftVersion {
+  std::vector<int32_t> pages;
+  uint32_t hidden_rows = 0;
+};
+
 constexpr size_t kStatsCount = 17 + 19 * 3;
 constexpr int kMaxSplits = 8;
 constexpr int kMaxDraft = 8;  // drafts per verified sequence (native_speculative.rs: at most 8)
@@ -150,6 +158,21 @@ struct Session {
   // speculative verify: per-token candidate state slots, EOS list, accept results
   DevBuf<int32_t> cand_dev, acc_dev;
   DevBuf<uint32_t> eos_dev, emitted_dev, nemit_dev;
+  // MTP draft head: its own version table (sharing the slot and byte budget),
+  // a one-layer KV page pool with block-table rows per draft slot, and the
+  // draft hidden rows (at most kMaxDraft per version)
+  bool mtp_on = false;
+  std::unique_ptr<StateTable<DraftVersion>> drafts;
+  KvPool mkv;
+  DevBuf<__nv_bfloat16> mkv_mem, mcat;
+  CUtensorMap mkv_map;
+  DevBuf<int32_t> mbt;
+  DevBuf<float> mhidden;
+  std::vector<int32_t> mfree, mref;
+  std::vector<uint8_t> mfilled;
+  size_t mpage_bytes = 0;
+  size_t draft_residents() const { return drafts ? drafts->residents() : 0; }
+  uint64_t draft_bytes() const { return drafts ? drafts->bytes() : 0; }
   int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
   DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
   int sm_count = 148;
@@ -443,7 +466,8 @@ struct Session {
         if (s.count < 1 || s.count > uint32_t(kMaxDraft + 1)) throw std::invalid_argument("draft count above 8");
         cand_total += s.count;
       }
-      if (table->residents() + cand_total > slots) throw std::runtime_error("combined resident budget exhausted");
+      if (table->residents() + draft_residents() + cand_total > slots)
+        throw std::runtime_error("combined resident budget exhausted");
     }
     const bool consume = flags & RS_QWEN_RAGGED_CONSUME;
     const bool all_rows = flags & RS_QWEN_RAGGED_ALL_ROWS;
@@ -494,7 +518,8 @@ struct Session {
           if (seqs[j].parent && seqs[j].parent->slot == seqs[i].parent->slot)
             throw std::invalid_argument("consumed parent used twice");
     }
-    if (!consume && table->residents() + size_t(n) > slots) throw std::runtime_error("combined resident budget exhausted");
+    if (!consume && table->residents() + draft_residents() + size_t(n) > slots)
+      throw std::runtime_error("combined resident budget exhausted");
 
     // page planning (host), descriptors
     staging.ensure(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64 + items.size() * 8);
@@ -808,6 +833,220 @@ struct Session {
     stage(18);  // StateValidation (finite check + greedy selection)
     launch_argmax(logits.p, R, d.V, sampled.p, err.p, argmax_part.p, argmax_done.p, s);
     launches += 1;
+  }
+
+  // ------------------------------------------------------------ MTP draft head
+  // rs_qwen_device_mtp_attach (native/qwen_mtp.inc:2-6): must precede any admission.
+  void mtp_attach(WeightStore* w) {
+    set_device();
+    if (!w || !w->ready || !w->model.has_mtp) throw std::invalid_argument("MTP weights missing (language_model.mtp.*)");
+    if (w != store) throw std::invalid_argument("the MTP head must live in the session's weight store");
+    if (mtp_on) throw std::invalid_argument("MTP already attached");
+    if (table->residents()) throw std::invalid_argument("MTP attach must precede admission");
+    mpage_bytes = size_t(2) * d.Hkv * kPageTokens * d.D * 2;
+    // as many pages as the target pool (one attention layer each), at least a
+    // full context for every slot when the target has no attention layers
+    size_t pages = d.n_attn > 0 ? size_t(kv.n_pages) : slots * size_t(bt_stride);
+    size_t free_b = 0, total_b = 0;
+    QWEN_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const size_t headroom = size_t(2) << 30;
+    pages = std::min({pages, free_b > headroom ? (free_b - headroom) / mpage_bytes : size_t(0),
+                      size_t(INT32_MAX / kPageTokens)});
+    if (pages == 0) throw std::runtime_error("no device memory left for MTP KV pages");
+    mkv_mem.ensure(pages * (mpage_bytes / 2));
+    mkv.base = mkv_mem.p;
+    mkv.n_pages = int(pages);
+    mkv.layers = 1;
+    mkv.Hkv = d.Hkv;
+    mkv.D = d.D;
+    mkv_map = make_kv_map(mkv, 0);
+    mbt.ensure(slots * size_t(bt_stride));
+    QWEN_CUDA(cudaMemset(mbt.p, 0, slots * size_t(bt_stride) * 4));
+    mhidden.ensure(slots * size_t(kMaxDraft) * d.H);
+    mcat.ensure(size_t(kMaxDraft) * 2 * d.H);
+    mref.assign(pages, 0);
+    mfilled.assign(pages, 0);
+    mfree.resize(pages);
+    for (size_t i = 0; i < pages; ++i) mfree[i] = int32_t(pages - 1 - i);
+    drafts = std::make_unique<StateTable<DraftVersion>>(allocate_owner(), slots, limit);
+    mtp_on = true;
+  }
+
+  void mtp_unref(const std::vector<int32_t>& pages) {
+    for (int32_t p : pages)
+      if (--mref[p] == 0) {
+        mfilled[p] = 0;
+        mfree.push_back(p);
+      }
+  }
+
+  // rs_qwen_device_mtp_step (native/qwen_mtp.inc:8-56 and 133-181): `count`
+  // draft tokens at positions [p, p + count), p = previous ? previous.position
+  // : 0, each paired with a hidden row of `source` (a target version's kept
+  // rows, or with draft_source the previous draft's last row). Writes the
+  // vocabulary logits of the last token.
+  void mtp_step(const StateId* previous, const StateId* source, int draft_source, size_t row,
+                const uint32_t* toks, size_t count, StateId* output, float* logits_out) {
+    set_device();
+    if (!mtp_on) throw std::invalid_argument("MTP unavailable: attach a head first");
+    if (!source || !toks || !output || !logits_out || draft_source < 0 || draft_source > 1 || !count ||
+        count > size_t(kMaxDraft))
+      throw std::invalid_argument("MTP descriptor");
+    const size_t position = previous ? previous->position : 0;
+    if (position > size_t(d.ctx) || count > size_t(d.ctx) - position) throw std::invalid_argument("MTP context capacity");
+    for (size_t i = 0; i < count; ++i)
+      if (toks[i] >= uint32_t(d.V)) throw std::invalid_argument("MTP token vocabulary");
+    const DraftVersion* old = previous ? &drafts->get(*previous) : nullptr;
+    const float* hidden_src = nullptr;
+    if (draft_source) {
+      const auto& src = drafts->get(*source);
+      if (!previous || source->owner != previous->owner || source->slot != previous->slot ||
+          source->generation != previous->generation || source->position != previous->position ||
+          source->bytes != previous->bytes || count != 1 || row + 1 != src.hidden_rows)
+        throw std::invalid_argument("MTP autoregressive parent identity");
+      hidden_src = mhidden.p + (size_t(source->slot) * kMaxDraft + row) * d.H;
+    } else {
+      const auto& src = table->get(*source);
+      const size_t rows = src.hidden_rows;
+      if (!rows || row > rows || count > rows - row) throw std::invalid_argument("MTP hidden row capacity");
+      if (source->position < rows || source->position - rows + row != position)
+        throw std::invalid_argument("MTP target hidden alignment");
+      hidden_src = hidden_pool.p + (size_t(source->slot) * d.chunk + row) * d.H;
+    }
+    const int pos = int(position), cnt = int(count);
+    const int n_prefix = (pos + kPageTokens - 1) / kPageTokens;
+    const int n_total = (pos + cnt + kPageTokens - 1) / kPageTokens;
+    if (old && int(old->pages.size()) != n_prefix) throw std::runtime_error("MTP parent page list inconsistent");
+    if (n_total > bt_stride) throw std::invalid_argument("context exceeds block table");
+    const uint64_t charge = uint64_t(n_total) * mpage_bytes + uint64_t(count) * d.H * 4;
+    if (table->residents() + draft_residents() >= slots || charge > limit - table->bytes() - draft_bytes())
+      throw std::runtime_error("combined resident budget exhausted");
+    // page planning (the target's rules on the draft pool)
+    SeqDesc sd;
+    std::memset(&sd, 0, sizeof(sd));
+    sd.position = pos;
+    sd.count = cnt;
+    sd.parent = previous ? int32_t(previous->slot) : -1;
+    sd.cow_src = -1;
+    sd.cand = -1;
+    int n_shared = n_prefix;
+    if (pos % kPageTokens) {
+      const int32_t lp = old->pages[n_prefix - 1];
+      if (mfilled[lp] > pos % kPageTokens) {
+        n_shared = n_prefix - 1;
+        sd.cow_src = lp;
+        sd.cow_len = pos % kPageTokens;
+      } else {
+        mfilled[lp] = uint8_t(std::min(kPageTokens, pos + cnt - (n_prefix - 1) * kPageTokens));
+      }
+    }
+    const int n_new = n_total - n_shared;
+    if (n_new > int(mfree.size())) throw std::runtime_error("MTP KV page pool exhausted");
+    std::vector<int32_t> cp(old ? old->pages.begin() : cp.end(), old ? old->pages.begin() + n_shared : cp.end());
+    for (int32_t p : cp) ++mref[p];
+    std::vector<int32_t> fresh;
+    for (int j = 0; j < n_new; ++j) {
+      const int32_t p = mfree.back();
+      mfree.pop_back();
+      mref[p] = 1;
+      mfilled[p] = uint8_t(std::min(kPageTokens, pos + cnt - (n_shared + j) * kPageTokens));
+      fresh.push_back(p);
+      cp.push_back(p);
+    }
+    sd.n_shared = n_shared;
+    sd.new_off = 0;
+    sd.n_new = n_new;
+    sd.out_row0 = 0;
+    sd.n_out = 1;
+    StateId id{};
+    bool reserved = false;
+    try {
+      id = drafts->reserve(position + count, charge);
+      reserved = true;
+      sd.child = int32_t(id.slot);
+      // attention work list (16-page splits)
+      std::vector<int2> items;
+      for (int j = 0; j < cnt; ++j)
+        for (int k = 0; k * 16 < (pos + j + kPageTokens) / kPageTokens; ++k) items.push_back(make_int2(j, k));
+      const int splits = std::max(1, (pos + cnt + 16 * kPageTokens - 1) / (16 * kPageTokens));
+      attn_ws.ensure(size_t(cnt) * d.Hq * splits * (d.D + 2));
+      attn_items.ensure(items.size());
+      cudaStream_t s = stream;
+      QWEN_CUDA(cudaMemcpyAsync(descs.p, &sd, sizeof(sd), cudaMemcpyHostToDevice, s));
+      if (n_new) QWEN_CUDA(cudaMemcpyAsync(new_pages.p, fresh.data(), size_t(n_new) * 4, cudaMemcpyHostToDevice, s));
+      QWEN_CUDA(cudaMemcpyAsync(tokens.p, toks, count * 4, cudaMemcpyHostToDevice, s));
+      QWEN_CUDA(cudaMemcpyAsync(attn_items.p, items.data(), items.size() * 8, cudaMemcpyHostToDevice, s));
+      QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, s));
+      mtp_forward(cnt, hidden_src, int(items.size()), splits, sd.cow_src >= 0);
+      QWEN_CUDA(cudaMemcpyAsync(mhidden.p + size_t(id.slot) * kMaxDraft * d.H, hidden_stage.p, count * d.H * 4,
+                                cudaMemcpyDeviceToDevice, s));
+      uint32_t h_err = 0;
+      QWEN_CUDA(cudaMemcpyAsync(logits_out, logits.p, size_t(d.V) * 4, cudaMemcpyDeviceToHost, s));
+      QWEN_CUDA(cudaMemcpyAsync(&h_err, err.p, 4, cudaMemcpyDeviceToHost, s));
+      QWEN_CUDA(cudaStreamSynchronize(s));
+      if (h_err & kErrNonFinite) throw std::runtime_error("nonfinite MTP result");
+      if (h_err) throw std::runtime_error("MTP device error flag " + std::to_string(h_err));
+    } catch (...) {
+      cudaStreamSynchronize(stream);
+      mtp_unref(cp);
+      if (reserved) drafts->rollback(id);
+      throw;
+    }
+    DraftVersion v;
+    v.pages = std::move(cp);
+    v.hidden_rows = uint32_t(count);
+    drafts->publish(id, std::move(v));
+    *output = id;
+    ++calls;
+  }
+
+  // The MTP head over T tokens (native/qwen_mtp.inc:157-171): fc of the
+  // normalised [embedding, target hidden], one gated-attention layer on the
+  // draft pool, the MoE, the MTP norm; the target's lm_head on the last row.
+  void mtp_forward(int T, const float* hidden_src, int n_items, int splits, bool cow) {
+    cudaStream_t s = stream;
+    const ModelDev& m = store->model;
+    const LayerDev& ly = m.mtp_layer;
+    Packed pk{cu_seqlens.p, token_seq.p, token_pos.p, slot_mapping.p, out_token.p};
+    launch_pack(descs.p, 1, new_pages.p, mbt.p, bt_stride, pk, s);
+    if (cow) launch_cow(mkv, descs.p, 1, new_pages.p, s);
+    launch_mtp_input(m.embed, tokens.p, T, hidden_src, m.mtp_norm_emb, m.mtp_norm_hidden, d.eps, mcat.p, s);
+    QWEN_CUDA(cudaMemsetAsync(x.p, 0, size_t(T) * d.H * 4, s));
+    const size_t hstride = size_t(T) * d.H;
+    const int fs = dense(m.mtp_fc, mcat.p, kMaxDraft, T, partial.p, d.H, hstride, kMaxSplits, s);
+    launch_residual_norm(x.p, partial.p, fs, hstride, T, d.H, ly.in_norm, d.eps, hb.p, nullptr, 0, nullptr, s);
+    const int aw = d.attn_in_rows;
+    const size_t astride = size_t(T) * aw;
+    const int ps = dense(ly.in_proj, hb.p, max_tokens, T, partial.p, aw, astride, kMaxSplits, s);
+    launch_attn_prep(d, ly, partial.p, aw, ps, astride, token_pos.p, slot_mapping.p, T, mkv, 0, q.p, gate.p, s);
+    launch_attn_decode(mkv_map, d, q.p, token_seq.p, token_pos.p, descs.p, mbt.p, bt_stride, attn_items.p, n_items,
+                       16, attn_ws.p, splits, err.p, s);
+    launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, 16, splits, hb2.p, s);
+    const int os = dense(ly.out_proj, hb2.p, max_tokens, T, partial.p, d.H, hstride, kMaxSplits, s);
+    launch_residual_norm(x.p, partial.p, os, hstride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0, nullptr, s);
+    const int A = T * (d.top + 1);
+    cur_layer = 0;
+    moe(ly, T, A, s);
+    if (capture_routing) {  // the MTP layer's routing, reported as layer 0
+      capture.ensure(size_t(std::max(1, d.L)) * A);
+      QWEN_CUDA(cudaMemcpyAsync(capture.p, ids.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
+      captured_tokens = T;
+    }
+    launch_moe_combine(x.p, moe_y.p, inv.p, weights.p, T, d.H, d.top + 1, nullptr, d.eps, hb.p, nullptr, 0, nullptr,
+                       s);
+    launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.mtp_norm, d.eps, hb.p, nullptr, 0, hidden_stage.p, s);
+    launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.mtp_norm, d.eps, hb_out.p, out_token.p, 1, nullptr, s);
+    logits.ensure(size_t(d.V));
+    dense(m.lm_head, hb_out.p, max_rows, 1, logits.p, d.V, size_t(d.V), 1, s);
+    launch_argmax(logits.p, 1, d.V, sampled.p, err.p, argmax_part.p, argmax_done.p, s);  // finite check
+  }
+
+  void mtp_release(const StateId& id) {
+    set_device();
+    if (!mtp_on) throw std::invalid_argument("MTP unavailable");
+    std::vector<int32_t> pages = drafts->get(id).pages;
+    drafts->release(id);
+    mtp_unref(pages);
   }
 
   void moe(const LayerDev& ly, int T, int A, cudaStream_t s) {
@@ -1169,6 +1408,15 @@ int rs_qwen_device_drain(void* session, uint64_t* invalidated, char* error, size
     std::fill(s->page_ref.begin(), s->page_ref.end(), 0);
     std::fill(s->page_filled.begin(), s->page_filled.end(), 0);
     if (s->table->residents() || s->table->bytes()) throw std::runtime_error("device drain residual");
+    if (s->mtp_on) {  // draft versions too (native/qwen_device.inc:65 drains both tables)
+      *invalidated += s->drafts->residents();
+      s->drafts->clear();
+      const size_t mp = s->mref.size();
+      s->mfree.resize(mp);
+      for (size_t i = 0; i < mp; ++i) s->mfree[i] = int32_t(mp - 1 - i);
+      std::fill(s->mref.begin(), s->mref.end(), 0);
+      std::fill(s->mfilled.begin(), s->mfilled.end(), 0);
+    }
   });
 }
 
@@ -1255,29 +1503,53 @@ int rs_qwen_device_debug_capture(void* session, int what, void* out, size_t coun
 }
 
 int rs_qwen_device_mtp_attach(void* session, void* weights, char* error, size_t capacity) {
+  return checked(error, capacity, [&] { S(session)->mtp_attach(static_cast<WeightStore*>(weights)); });
+}
+int rs_qwen_device_mtp_step(void* session, const StateId* previous, const StateId* source, int draft_source,
+                            size_t row, const uint32_t* tokens, size_t count, StateId* output, float* logits,
+                            size_t logits_count, int diagnostics, char* error, size_t capacity) {
   return checked(error, capacity, [&] {
-    (void)S(session);
-    (void)weights;
-    throw std::runtime_error("MTP head not available in this build");
+    Session* s = S(session);
+    if (diagnostics < 0 || diagnostics > 1) throw std::invalid_argument("MTP descriptor");
+    if (diagnostics) throw std::invalid_argument("MTP diagnostics are an MLX-baseline feature not offered here");
+    if (logits_count != size_t(s->d.V)) throw std::invalid_argument("MTP unavailable or vocabulary capacity");
+    s->mtp_step(previous, source, draft_source, row, tokens, count, output, logits);
   });
 }
-int rs_qwen_device_mtp_step(void* session, const StateId*, const StateId*, int, size_t, const uint32_t*, size_t,
-                            StateId*, float*, size_t, int, char* error, size_t capacity) {
+int rs_qwen_device_mtp_release(void* session, const StateId* id, char* error, size_t capacity) {
   return checked(error, capacity, [&] {
-    (void)S(session);
-    throw std::runtime_error("MTP head not available in this build");
+    if (!id) throw std::invalid_argument("MTP release descriptor");
+    S(session)->mtp_release(*id);
   });
 }
-int rs_qwen_device_mtp_release(void* session, const StateId*, char* error, size_t capacity) {
+int rs_qwen_device_mtp_snapshot(void* session, const StateId* id, float* output, size_t count, char* error,
+                                size_t capacity) {
   return checked(error, capacity, [&] {
-    (void)S(session);
-    throw std::runtime_error("MTP head not available in this build");
-  });
-}
-int rs_qwen_device_mtp_snapshot(void* session, const StateId*, float*, size_t, char* error, size_t capacity) {
-  return checked(error, capacity, [&] {
-    (void)S(session);
-    throw std::runtime_error("MTP head not available in this build");
+    Session* s = S(session);
+    if (!id || !output) throw std::invalid_argument("MTP snapshot capacity");
+    if (!s->mtp_on) throw std::invalid_argument("MTP unavailable");
+    s->set_device();
+    const Dims& d = s->d;
+    const auto& v = s->drafts->get(*id);
+    const size_t per = size_t(d.Hkv) * d.ctx * d.D;
+    if (count != 2 * per + size_t(v.hidden_rows) * d.H) throw std::invalid_argument("MTP snapshot capacity");
+    std::fill(output, output + 2 * per, 0.f);
+    std::vector<__nv_bfloat16> page(size_t(2) * d.Hkv * kPageTokens * d.D);
+    for (size_t pi = 0; pi < v.pages.size(); ++pi) {
+      QWEN_CUDA(cudaMemcpy(page.data(), s->mkv.page(0, v.pages[pi]), page.size() * 2, cudaMemcpyDeviceToHost));
+      for (int kvsel = 0; kvsel < 2; ++kvsel)
+        for (int g = 0; g < d.Hkv; ++g)
+          for (int o = 0; o < kPageTokens; ++o) {
+            const size_t p = pi * kPageTokens + o;
+            if (p >= id->position) continue;
+            const __nv_bfloat16* src = page.data() + ((size_t(kvsel) * d.Hkv + g) * kPageTokens + o) * d.D;
+            float* dst = output + kvsel * per + (size_t(g) * d.ctx + p) * d.D;
+            for (int i = 0; i < d.D; ++i) dst[i] = __bfloat162float(src[i]);
+          }
+    }
+    QWEN_CUDA(cudaMemcpy(output + 2 * per, s->mhidden.p + size_t(id->slot) * kMaxDraft * d.H,
+                         size_t(v.hidden_rows) * d.H * 4, cudaMemcpyDeviceToHost));
+    s->exports += count * 4;
   });
 }
 int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId* parents, const uint32_t* seeds,
