@@ -145,17 +145,27 @@ def dist_setup(n_gpus):
     if world > 1:
         import datetime
 
+        import torch
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        # NCCL between GPU ranks (one process per GPU), gloo when there is no GPU;
+        # a short timeout so a rank that never arrives ends the others with an error
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     return rank, world, local
 
 
 def max_over_ranks(value, world):
+    """The largest value over all ranks (timings are max over ranks)."""
     if world == 1:
         return value
     import torch
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64)
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -341,4 +351,9 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    try:
+        main()
+    finally:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
