@@ -1,6 +1,6 @@
 // Paged GQA attention for decode and chunked prefill (flash-decoding).
 //
-// CTA = (work item, kv head g), 4 warps. A work item is one (query token t,
+// CTA = (work item, kv head g), kAttnWarps warps. A work item is one (query token t,
 // KV split) pair from a host-built list holding only the splits that token
 // attends, so no CTA is launched for keys beyond a token's position; a split
 // covers `split_pages` consecutive 16-token pages (chosen per step). The
@@ -9,7 +9,7 @@
 // 16x64 box per 64 head dims, K and V), computes S = Q K^T and O += P V with
 // mma.sync (bf16 operands, fp32 accumulators; the G query heads of kv head g are
 // the 16 MMA rows) and keeps an online softmax per head row in registers.
-// The four warps' (max, sum, O) are merged in shared memory and written as the
+// The warps' (max, sum, O) are merged in shared memory and written as the
 // split's partial; attention_merge_kernel combines splits and applies the
 // output gate. Keys at positions >= pos(t)+1 are masked (causal, bottom-right).
 #include <cuda.h>
@@ -25,7 +25,7 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 2;  // two warps per CTA: three CTAs fit an SM (shared memory, registers)
 constexpr int kKvStages = 2;
 constexpr long long kAttnWaitCycles = 2000000000ll;
 
@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   uint8_t* qs = base;                                      // Q tile [16][D] bf16, swizzled
   uint8_t* kv = qs + TILE;                                 // [warps][stages][K tile, V tile]
   float* red = reinterpret_cast<float*>(kv + kAttnWarps * kKvStages * 2 * TILE);  // [warps][16][2]
-  float* obuf = red + kAttnWarps * 16 * 2;                 // [16][D] merge buffer
-  uint64_t* bars = reinterpret_cast<uint64_t*>(obuf + 16 * D);  // [warps][stages]
+  float* obuf = reinterpret_cast<float*>(kv);               // [16][D] merge buffer, on the drained ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + kAttnWarps * 16 * 2);  // [warps][stages]
 
   const int2 item = items[blockIdx.x];
   const int t = item.x, split = item.y, g = blockIdx.y;
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
       tma_load_2d(kt + TILE + b * 16 * 128, &kvmap, b * 64, yv, &mybars[stage]);
     }
   };
-  const int my_pages = (p1 - p0 - warp + kAttnWarps - 1) / kAttnWarps;  // pages warp, warp+4, ...
+  const int my_pages = (p1 - p0 - warp + kAttnWarps - 1) / kAttnWarps;  // pages warp, warp + kAttnWarps, ...
   if (lane == 0)
     for (int i = 0; i < kKvStages && i < my_pages; ++i) issue(warp + i * kAttnWarps, i);
 
@@ -179,9 +179,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;  // rows lane/4 and lane/4+8
   bool ok = true;
+  int stalled = 0;
   for (int i = 0; i < my_pages; ++i) {
     const int stage = i % kKvStages;
-    if (!mbar_wait_bounded(&mybars[stage], (i / kKvStages) & 1, err)) { ok = false; break; }
+    if (!mbar_wait_bounded(&mybars[stage], (i / kKvStages) & 1, err)) { ok = false; stalled = i; break; }
     const uint32_t kt = smem_u32(mykv + stage * 2 * TILE), vt = kt + TILE;
     // S = Q K^T over 16 keys (two n-tiles of 8)
     float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -241,8 +242,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     __syncwarp();
     if (lane == 0 && i + kKvStages < my_pages) issue(warp + (i + kKvStages) * kAttnWarps, stage);
   }
-  (void)ok;
-  // merge the warps: row maxima and sums
+  if (!ok && lane == 0) {
+    // timed out: wait (bounded) for this warp's page loads still in flight before
+    // the ring is reused and the CTA leaves
+    for (int j = stalled; j < min(my_pages, stalled + kKvStages); ++j)
+      mbar_wait_bounded(&mybars[j % kKvStages], (j / kKvStages) & 1, err);
+  }
+  // merge the warps: row maxima and sums (the ring is drained: every page a
+  // warp loaded it also consumed, so the ring now holds the merge buffer)
+  __syncthreads();
   const int r0 = lane >> 2;
   if ((lane & 3) == 0) {
     red[(warp * 16 + r0) * 2 + 0] = m0;
@@ -292,8 +300,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 
 size_t attn_decode_smem(int D) {
   const size_t tile = 16 * size_t(D) * 2;
-  return 1024 + tile + kAttnWarps * kKvStages * 2 * tile + kAttnWarps * 16 * 2 * 4 + 16 * size_t(D) * 4 +
-         kAttnWarps * kKvStages * 8;
+  return 1024 + tile + kAttnWarps * kKvStages * 2 * tile + kAttnWarps * 16 * 2 * 4 + kAttnWarps * kKvStages * 8;
 }
 
 CUtensorMap make_kv_map(const KvPool& kv, int layer);
