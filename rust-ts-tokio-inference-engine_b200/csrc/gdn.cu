@@ -36,13 +36,15 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
                     float* __restrict__ gb_out, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float qs[DK], ks[DK];
-  __shared__ float qk_scale[2];
+  // q / k sums of squares: one partial per warp (4 warps each for dk = 128),
+  // double-buffered by token parity so one barrier per token suffices
+  constexpr int QW = DK / 32;  // warps holding q (and as many holding k)
+  __shared__ float red[2][2 * QW];
   const int seq = blockIdx.x, kh = blockIdx.y;
   const SeqDesc d = descs[seq];
   const int t0 = cu_seqlens[seq];
   const int kd = hk * DK, vd = hv * DV, cd = 2 * kd + vd;
-  const int c = threadIdx.x, lane = threadIdx.x & 31;
+  const int c = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gc = c < DK ? kh * DK + c : (c < 2 * DK ? kd + kh * DK + (c - DK) : 2 * kd + kh * R * DV + (c - 2 * DK));
   const size_t cl = size_t(conv - 1) * cd;
   const float* src_conv = d.parent >= 0 ? pool.conv + (size_t(d.parent) * pool.n_gdn + li) * cl : nullptr;
@@ -82,9 +84,23 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
         if (j < conv - 1) cc[size_t(j) * cd + gc] = taps[j];
     }
     const float act = siluf_(acc);
-    if (c < DK) qs[c] = act;
-    else if (c < 2 * DK) ks[c - DK] = act;
-    else v_out[size_t(t) * vd + kh * R * DV + (c - 2 * DK)] = act;
+    if (c >= 2 * DK) {
+      v_out[size_t(t) * vd + kh * R * DV + (c - 2 * DK)] = act;
+    } else {
+      // q / k: inverse RMS over the head (warp partials, fixed order), folded
+      // with the 1/dk and 1/sqrt(dk) scales; only these 2*dk threads meet
+      float ss = warp_sum(act * act);
+      if (lane == 0) red[i & 1][warp] = ss;
+      asm volatile("bar.sync 1, %0;" ::"r"(2 * DK) : "memory");
+      const int g0 = c < DK ? 0 : QW;
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < QW; ++w) tot += red[i & 1][g0 + w];
+      const float rinv = rsqrtf(tot / DK + 1e-6f);
+      float* dst = qk_out + ((size_t(t) * hk + kh) * 2) * DK;
+      if (c < DK) dst[c] = act * (rinv / DK);
+      else dst[DK + (c - DK)] = act * (rinv * rsqrtf(float(DK)));
+    }
     if (c < R) {
       const int h = kh * R + c;
       const float av = P(pr, cd + vd + h) + dt_bias[h];
@@ -92,24 +108,6 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
       gb_out[(size_t(t) * hv + h) * 2 + 0] = expf(-expf(a_log[h]) * sp);
       gb_out[(size_t(t) * hv + h) * 2 + 1] = sigmoidf_(P(pr, cd + vd + hv + h));
     }
-    __syncthreads();
-    if (c < 64) {  // warps 0/1: q / k inverse RMS, folded with the 1/dk and 1/sqrt(dk) scales
-      const float* v = c < 32 ? qs : ks;
-      float ss = 0.f;
-      for (int j = lane; j < DK; j += 32) ss += v[j] * v[j];
-      ss = warp_sum(ss);
-      if (lane == 0) {
-        const float rinv = rsqrtf(ss / DK + 1e-6f);
-        qk_scale[c >> 5] = c < 32 ? rinv / DK : rinv * rsqrtf(float(DK));
-      }
-    }
-    __syncthreads();
-    if (c < 2 * DK) {
-      float* dst = qk_out + ((size_t(t) * hk + kh) * 2) * DK;
-      if (c < DK) dst[c] = qs[c] * qk_scale[0];
-      else dst[DK + (c - DK)] = ks[c - DK] * qk_scale[1];
-    }
-    __syncthreads();
   }
   if (d.cand < 0) {
 #pragma unroll
