@@ -226,6 +226,22 @@ int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId*
                                      uint32_t* accepted, uint32_t* emitted,
                                      uint32_t* n_emitted, char* error, size_t capacity);
 
+/* NEW: expert parallelism (the survey's multi-GPU mode b; no reference
+ * counterpart). Rank 0 calls rs_qwen_ep_unique_id (128 bytes, NCCL unique id)
+ * and shares it; every rank then calls rs_qwen_device_ep_init on its own
+ * session (one GPU per process) with the same world size, its rank and the
+ * same cap_tokens. From then on the target model's MoE layers compute only the
+ * rank's block of routed experts [rank*E/world, (rank+1)*E/world) for the
+ * rows of every rank, exchanged with NCCL send/recv over NVLink in
+ * fixed-size stages of cap_tokens*top rows per peer; the shared expert and
+ * everything else stay local, and logits equal the single-GPU ones bit for
+ * bit. All ranks must step in lockstep (the same sequence of target steps,
+ * each with at most cap_tokens tokens, and T >= 1); the MTP head stays local.
+ * E must be a multiple of world. */
+int rs_qwen_ep_unique_id(uint8_t* out, size_t out_bytes, char* error, size_t capacity);
+int rs_qwen_device_ep_init(void* session, int world, int rank, const uint8_t* id, size_t id_bytes,
+                           size_t cap_tokens, char* error, size_t capacity);
+
 /* NEW (no reference counterpart; stands in for a long prefill when measuring
  * decode at long contexts): create a published version at `position` whose
  * KV pages for [0, position) hold seeded bf16 N(0, 1) values, whose DeltaNet

@@ -95,6 +95,8 @@ SIGNATURES = {
     "rs_qwen_device_synthetic_state": (C.c_int, [_P, _SZ, C.c_uint64, _SIDP, _ERR, _SZ]),
     "rs_qwen_device_set_capture": (C.c_int, [_P, C.c_int, _ERR, _SZ]),
     "rs_qwen_device_set_profile": (C.c_int, [_P, C.c_int, _ERR, _SZ]),
+    "rs_qwen_ep_unique_id": (C.c_int, [C.c_void_p, _SZ, _ERR, _SZ]),
+    "rs_qwen_device_ep_init": (C.c_int, [_P, C.c_int, C.c_int, C.c_void_p, _SZ, _SZ, _ERR, _SZ]),
     "rs_qwen_device_timing": (C.c_int, [_P, C.POINTER(C.c_double), _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_routing": (C.c_int, [_P, _I32P, _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_capture": (C.c_int, [_P, C.c_int, C.c_void_p, _SZ, C.POINTER(_SZ), _ERR, _SZ]),
@@ -172,6 +174,13 @@ def layer_program(cfg: RsQwenConfig):
 
 def state_count(cfg: RsQwenConfig) -> int:
     return load().rs_qwen_state_count(C.byref(cfg))
+
+
+def ep_unique_id() -> bytes:
+    """NCCL unique id (128 bytes) for rs_qwen_device_ep_init, made by rank 0."""
+    buf = (C.c_uint8 * 128)()
+    _call("rs_qwen_ep_unique_id", buf, 128)
+    return bytes(buf)
 
 
 class WeightStore:
@@ -353,6 +362,11 @@ class DeviceSession:
 
     def set_capture(self, routing: bool):
         _call("rs_qwen_device_set_capture", self.h, int(routing))
+
+    def ep_init(self, world: int, rank: int, uid: bytes, cap_tokens: int):
+        """Join the expert-parallel group (see rs_qwen_device_ep_init)."""
+        buf = (C.c_uint8 * len(uid)).from_buffer_copy(uid)
+        _call("rs_qwen_device_ep_init", self.h, world, rank, buf, len(uid), cap_tokens)
 
     def set_profile(self, on: bool):
         _call("rs_qwen_device_set_profile", self.h, int(on))

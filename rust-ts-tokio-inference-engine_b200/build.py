@@ -52,7 +52,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if force or jobs or not LIB.exists():
         tmp = LIB.with_suffix(".so.tmp")
         subprocess.run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs),
-                        "-o", str(tmp), "-lcudart"], check=True)
+                        "-o", str(tmp), "-lcudart", "-lnccl"], check=True)
         tmp.replace(LIB)
     return LIB
 

@@ -18,6 +18,8 @@
 #include <map>
 #include <tuple>
 
+#include <nccl.h>
+
 #include "kernels.h"
 #include "noalloc.h"
 #include "qgemm_tc.h"
@@ -272,7 +274,26 @@ struct Session {
   uint64_t exports = 0, uploads = 0, steps = 0, calls = 0, completed = 0, graph_ns = 0,
            wait_ns = 0, export_ns = 0, wall_ns = 0, groups = 0, launches = 0;
 
+  // Expert parallelism (survey multi-GPU mode b): routed experts split over
+  // `world` ranks, rank r owning [r*E/world, (r+1)*E/world); rows travel in
+  // fixed-size NCCL stages of `cap` = cap_tokens * top rows per peer, so a step
+  // needs no host synchronisation. All ranks must step in lockstep (the same
+  // number of target steps, each with at most cap_tokens tokens).
+  struct EpState {
+    bool on = false;
+    int world = 1, rank = 0, per_rank = 0, cap_tokens = 0, cap = 0, hdr_ints = 0, max_rows = 0;
+    size_t stage_bytes = 0;
+    ncclComm_t comm = nullptr;
+    DevBuf<uint8_t> send, recv;
+    DevBuf<float> rsend, rrecv, yloc;
+    DevBuf<__nv_bfloat16> xloc, actloc;
+    DevBuf<int32_t> goff, seg, origin, n_rows;
+    DevBuf<uint64_t> srcs, rsrcs;  // device tables of the stage pointers per source rank
+  } ep;
+  bool in_mtp = false;  // the MTP head's MoE computes every expert locally
+
   ~Session() {
+    if (ep.comm) ncclCommDestroy(ep.comm);
     for (auto e : ev_pool) cudaEventDestroy(e);
     if (ev_begin) cudaEventDestroy(ev_begin);
     if (ev_end) cudaEventDestroy(ev_end);
@@ -1026,7 +1047,14 @@ struct Session {
     launch_residual_norm(x.p, partial.p, os, hstride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0, nullptr, s);
     const int A = T * (d.top + 1);
     cur_layer = 0;
-    moe(ly, T, A, s);
+    in_mtp = true;
+    try {
+      moe(ly, T, A, s);
+    } catch (...) {
+      in_mtp = false;
+      throw;
+    }
+    in_mtp = false;
     if (capture_routing) {  // the MTP layer's routing, reported as layer 0
       capture.ensure(size_t(std::max(1, d.L)) * A);
       QWEN_CUDA(cudaMemcpyAsync(capture.p, ids.p, size_t(A) * 4, cudaMemcpyDeviceToDevice, s));
@@ -1049,6 +1077,99 @@ struct Session {
     mtp_unref(pages);
   }
 
+  void ep_init(int world, int rank, const ncclUniqueId& uid, int cap_tokens) {
+    if (ep.on) throw std::invalid_argument("expert parallelism already initialised");
+    if (world < 1 || rank < 0 || rank >= world || d.E % world) throw std::invalid_argument("expert-parallel geometry");
+    if (cap_tokens < 1 || cap_tokens > max_tokens) throw std::invalid_argument("expert-parallel token capacity");
+    set_device();
+    ep.world = world;
+    ep.rank = rank;
+    ep.per_rank = d.E / world;
+    ep.cap_tokens = cap_tokens;
+    ep.cap = cap_tokens * d.top;
+    ep.hdr_ints = (ep.per_rank + 3) & ~3;
+    ep.stage_bytes = size_t(ep.hdr_ints) * 4 + size_t(ep.cap) * d.H * 2;
+    ep.max_rows = world * ep.cap + cap_tokens;  // routed rows from every source + this rank's shared rows
+    ep.send.ensure(size_t(world) * ep.stage_bytes);
+    ep.recv.ensure(size_t(world) * ep.stage_bytes);
+    ep.rsend.ensure(size_t(world) * ep.cap * d.H);
+    ep.rrecv.ensure(size_t(world) * ep.cap * d.H);
+    ep.xloc.ensure(size_t(ep.max_rows) * d.H);
+    ep.actloc.ensure(size_t(ep.max_rows) * d.I);
+    ep.yloc.ensure(size_t(ep.max_rows) * d.H);
+    ep.goff.ensure(d.E + 2);
+    ep.seg.ensure(size_t(2) * world * ep.per_rank);
+    ep.origin.ensure(ep.max_rows);
+    ep.n_rows.ensure(1);
+    std::vector<uint64_t> srcs(world), rsrcs(world);
+    for (int p = 0; p < world; ++p) {
+      srcs[p] = reinterpret_cast<uint64_t>((p == rank ? ep.send.p : ep.recv.p) + size_t(p) * ep.stage_bytes);
+      rsrcs[p] = reinterpret_cast<uint64_t>((p == rank ? ep.rsend.p : ep.rrecv.p) + size_t(p) * ep.cap * d.H);
+    }
+    ep.srcs.ensure(world);
+    ep.rsrcs.ensure(world);
+    QWEN_CUDA(cudaMemcpy(ep.srcs.p, srcs.data(), size_t(world) * 8, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.rsrcs.p, rsrcs.data(), size_t(world) * 8, cudaMemcpyHostToDevice));
+    const ncclResult_t r = ncclCommInitRank(&ep.comm, world, uid, rank);
+    if (r != ncclSuccess) throw std::runtime_error(std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    ep.on = true;
+  }
+
+  // One grouped exchange of equal-size buffers with every other rank.
+  void ep_exchange(const void* send, void* recv, size_t bytes, cudaStream_t s) {
+    ncclResult_t r = ncclGroupStart();
+    for (int p = 0; p < ep.world && r == ncclSuccess; ++p) {
+      if (p == ep.rank) continue;
+      r = ncclSend(static_cast<const uint8_t*>(send) + size_t(p) * bytes, bytes, ncclUint8, p, ep.comm, s);
+      if (r == ncclSuccess) r = ncclRecv(static_cast<uint8_t*>(recv) + size_t(p) * bytes, bytes, ncclUint8, p, ep.comm, s);
+    }
+    const ncclResult_t r2 = ncclGroupEnd();
+    if (r != ncclSuccess || r2 != ncclSuccess)
+      throw std::runtime_error(std::string("expert-parallel exchange: ") + ncclGetErrorString(r != ncclSuccess ? r : r2));
+  }
+
+  // The MoE block with the routed experts split over the ranks (see EpState).
+  void moe_ep(const LayerDev& ly, int T, int A, cudaStream_t s) {
+    if (T > ep.cap_tokens) throw std::logic_error("expert-parallel step above its token capacity");
+    const int world = ep.world;
+    launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
+    launch_ep_pack(xperm.p, counts.p, offsets.p, ep.send.p, ep.stage_bytes, world, ep.per_rank, ep.hdr_ints, ep.cap,
+                   d.H, s);
+    ep_exchange(ep.send.p, ep.recv.p, ep.stage_bytes, s);
+    launch_ep_plan_gather(reinterpret_cast<const uint8_t* const*>(ep.srcs.p), world, ep.rank, ep.per_rank, ep.hdr_ints,
+                          d.E, counts.p, offsets.p, xperm.p, ep.goff.p, ep.seg.p, ep.n_rows.p, ep.xloc.p, ep.origin.p,
+                          ep.cap, d.H, ep.max_rows, err.p, sm_count, s);
+    const int per_expert = (world * T * d.top + T + d.E) / (d.E + 1);
+    const int box = box_for(std::max(1, 2 * per_expert));
+    TcArgs gu;
+    gu.W = ly.expert_gu;
+    gu.mode = kGemmGateUp;
+    gu.expert_tiles = 2 * d.I / kTileRows;
+    gu.groups = d.E + 1;
+    gu.group_off = ep.goff.p;
+    gu.box_rows = box;
+    gu.Yb = ep.actloc.p;
+    gu.ldyb = d.I;
+    gu.err = err.p;
+    launch_tc(ep.xloc.p, ep.max_rows, gu, s);
+    stage(12);  // MoeDown
+    TcArgs dn;
+    dn.W = ly.expert_dn;
+    dn.mode = kGemmDown;
+    dn.expert_tiles = d.H / kTileRows;
+    dn.groups = d.E + 1;
+    dn.group_off = ep.goff.p;
+    dn.box_rows = box;
+    dn.Y = ep.yloc.p;
+    dn.ldy = d.H;
+    dn.err = err.p;
+    launch_tc(ep.actloc.p, ep.max_rows, dn, s);
+    launch_ep_return(ep.yloc.p, ep.origin.p, ep.n_rows.p, ep.rsend.p, moe_y.p, ep.cap, d.H, ep.max_rows, sm_count, s);
+    ep_exchange(ep.rsend.p, ep.rrecv.p, size_t(ep.cap) * d.H * 4, s);
+    launch_ep_return_unpack(reinterpret_cast<const float* const*>(ep.rsrcs.p), offsets.p, moe_y.p, world, ep.per_rank,
+                            d.H, A, sm_count, s);
+  }
+
   void moe(const LayerDev& ly, int T, int A, cudaStream_t s) {
     stage(10);  // MoeRouting
     const int rw = d.E + 1;
@@ -1058,6 +1179,10 @@ struct Session {
                  capture_routing ? cap_logits.p + size_t(cur_layer) * T * (d.E + 1) : nullptr, s);
     launch_expert_sort(ids.p, A, d.E + 1, counts.p, offsets.p, perm.p, inv.p, s);
     stage(11);  // MoeUpGate
+    if (ep.on && !in_mtp && !simple_gemm) {
+      moe_ep(ly, T, A, s);
+      return;
+    }
     if (simple_gemm) {
       GemmArgs gu;
       gu.W = ly.expert_gu;
@@ -1654,6 +1779,27 @@ int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_d
   return project_noalloc(W, which == 3 ? 1 : kMaxSplits, static_cast<const __nv_bfloat16*>(x_device), int(T),
                          y_device, s->sm_count, stream ? static_cast<cudaStream_t>(stream) : s->stream, error,
                          capacity);
+}
+
+int rs_qwen_ep_unique_id(uint8_t* out, size_t out_bytes, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!out || out_bytes != sizeof(ncclUniqueId)) throw std::invalid_argument("expert-parallel id capacity");
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) throw std::runtime_error(std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
+  });
+}
+
+int rs_qwen_device_ep_init(void* session, int world, int rank, const uint8_t* id, size_t id_bytes, size_t cap_tokens,
+                           char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!id || id_bytes != sizeof(ncclUniqueId) || cap_tokens > size_t(1) << 30)
+      throw std::invalid_argument("expert-parallel init arguments");
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    S(session)->ep_init(world, rank, uid, int(cap_tokens));
+  });
 }
 
 int rs_qwen_device_set_profile(void* session, int profile, char* error, size_t capacity) {

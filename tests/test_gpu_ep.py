@@ -1,0 +1,111 @@
+"""Expert parallelism (rs_qwen_ep_unique_id / rs_qwen_device_ep_init): the
+target model's MoE layers with the routed experts split over ranks, rows
+exchanged with NCCL send/recv. A token's expert rows get the same arithmetic
+as on one GPU, so the expert-parallel logits must equal the single-GPU
+logits bit for bit.
+
+- world = 1 (one GPU): the whole pack / plan / gather / return path runs with
+  the self stage only;
+- world = 2 (two GPUs, skipped otherwise): one process per GPU, each rank
+  stepping its own sequences in lockstep, against a plain session of the same
+  rank.
+"""
+import multiprocessing as mp
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import has_cuda
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _steps(pkg, cfg, sess, seed, n_seq):
+    """A mixed prefill + decode step then a decode step on synthetic states;
+    returns the sampled tokens and last-row logits of both steps."""
+    rng = np.random.default_rng(seed)
+    positions = [int(p) for p in rng.integers(5, 300, size=n_seq)]
+    counts = [3] + [1] * (n_seq - 1)
+    parents = [sess.synthetic_state(p, seed * 100 + i) for i, p in enumerate(positions)]
+    toks = rng.integers(0, cfg.vocab, size=sum(counts)).astype(np.uint32)
+    flags = pkg.RAGGED_SAMPLED | pkg.RAGGED_LOGITS
+    outs, s1, l1 = sess.step_ragged(parents, positions, counts, toks, flags=flags)
+    pos2 = [p + c for p, c in zip(positions, counts)]
+    outs2, s2, l2 = sess.step_ragged(outs, pos2, [1] * n_seq, s1.astype(np.uint32), flags=flags)
+    for o in parents + list(outs) + list(outs2):
+        sess.release(o)
+    return s1, l1, s2, l2
+
+
+def _compare(pkg, cfg, store, world, rank, uid, seed, n_seq):
+    plain = pkg.DeviceSession(store, cfg, slots=4 * n_seq, budget_bytes=2 << 30)
+    ep = pkg.DeviceSession(store, cfg, slots=4 * n_seq, budget_bytes=2 << 30)
+    ep.ep_init(world, rank, uid, n_seq + 2)
+    try:
+        a = _steps(pkg, cfg, plain, seed, n_seq)
+        b = _steps(pkg, cfg, ep, seed, n_seq)
+    finally:
+        ep.close()
+        plain.close()
+    return all(np.array_equal(x, y) for x, y in zip(a, b))
+
+
+@pytest.mark.parametrize("widths", ["cfg0", "cfg1"])
+def test_expert_parallel_world1_equals_plain(pkg, widths):
+    if not has_cuda():
+        pytest.skip("no CUDA device")
+    cfg = pkg.config0() if widths == "cfg0" else pkg.config1(layers=4, context=1024)
+    store = pkg.WeightStore().synthetic(cfg, 77)
+    try:
+        assert _compare(pkg, cfg, store, 1, 0, pkg.ep_unique_id(), 5, 6)
+    finally:
+        store.close()
+
+
+def _rank_main(rank, world, q_id, q_out):
+    os.environ["CUDA_VISIBLE_DEVICES"] = str(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    sys.path.insert(0, str(ROOT))
+    import importlib
+    pkg = importlib.import_module("rust-ts-tokio-inference-engine_b200")
+    try:
+        if rank == 0:
+            uid = pkg.ep_unique_id()
+            for _ in range(world - 1):
+                q_id.put(uid)
+        else:
+            uid = q_id.get(timeout=120)
+        cfg = pkg.config1(layers=4, context=1024)
+        store = pkg.WeightStore().synthetic(cfg, 77)
+        ok = _compare(pkg, cfg, store, world, rank, uid, 11 + rank, 5)
+        store.close()
+        q_out.put((rank, bool(ok), ""))
+    except Exception as e:  # reported to the parent; never left hanging
+        q_out.put((rank, False, repr(e)))
+
+
+def test_expert_parallel_two_gpus_equals_plain():
+    import torch
+    if not has_cuda() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q_id, q_out = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, q_id, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            r, ok, msg = q_out.get(timeout=600)
+            results[r] = (ok, msg)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert results == {0: (True, ""), 1: (True, "")}, results
