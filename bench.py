@@ -99,8 +99,11 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def stage_bytes(cfg, ctx, routing):
-    """Algorithmic HBM bytes per step for each operator stage (device-layout bytes)."""
+def stage_bytes(cfg, ctx, routing, expert_range=None):
+    """Algorithmic HBM bytes per step for each operator stage (device-layout bytes).
+    With expert_range = (lo, hi) (expert parallelism) the MoE terms count the
+    experts of that block hit by `routing` (every rank's tokens) and the rows
+    routed to them."""
     H, E, I = cfg.hidden, cfg.experts, cfg.intermediate
     n_attn = cfg.layers // cfg.interval
     n_gdn = cfg.layers - n_attn
@@ -120,13 +123,18 @@ def stage_bytes(cfg, ctx, routing):
     out["AttentionReduction"] = n_attn * (float(np.sum(ctx + 1)) * kv_per_tok + B * attn_in * 4)
     out["AttentionOutput"] = n_attn * (H * cfg.q_heads * cfg.head_dim * w + B * H * 4)
     out["MoeRouting"] = cfg.layers * ((E + 1) * H * w + B * H * 2)
-    if routing is not None:
+    rows = cfg.layers * B * (cfg.top + 1)
+    if expert_range is not None:
+        lo, hi = expert_range
+        distinct = [len(np.unique(r[(r >= lo) & (r < hi)])) for r in routing]
+        rows = float(sum(np.count_nonzero((r >= lo) & (r < hi)) for r in routing)) + cfg.layers * B
+    elif routing is not None:
         distinct = [len(np.unique(routing[layer])) for layer in range(routing.shape[0])]
     else:
         distinct = [E * (1 - (1 - cfg.top / E) ** B)] * cfg.layers
     ue = np.array(distinct, np.float64) + 1  # + shared expert
-    out["MoeUpGate"] = float(np.sum(ue * 2 * I * H * w)) + cfg.layers * B * (cfg.top + 1) * (H * 2 + I * 2)
-    out["MoeDown"] = float(np.sum(ue * H * I * w)) + cfg.layers * B * (cfg.top + 1) * (I * 2 + H * 4)
+    out["MoeUpGate"] = float(np.sum(ue * 2 * I * H * w)) + rows * (H * 2 + I * 2)
+    out["MoeDown"] = float(np.sum(ue * H * I * w)) + rows * (I * 2 + H * 4)
     out["FinalProjection"] = cfg.vocab * H * w + B * cfg.vocab * 4
     return out, float(np.mean(ue))
 
@@ -228,12 +236,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--ep", action="store_true",
+                    help="expert parallelism: routed experts split over the ranks, rows stored straight into the "
+                         "owner's window over NVLink")
+    ap.add_argument("--ep-nccl", action="store_true", help="expert parallelism with NCCL send/recv stages instead")
     args = ap.parse_args()
     rank, world, local = dist_setup(args.gpus)
     cfg_kw = dict(layers=args.layers)
     config = {"workload": "configs[1]: 64 ragged decode seqs, contexts logU[128,32768], 48L Qwen3-Next-80B-A3B "
                           "shapes, 4-bit g64", "seqs_per_gpu": N_SEQ, "page_tokens": 16,
-              "parallelism": f"replicas{args.gpus}", "l2": "inputs larger than L2 (44.8 GB weights per step)"}
+              "parallelism": (f"ep{args.gpus}-nccl" if args.ep_nccl else f"ep{args.gpus}") if args.ep or args.ep_nccl
+              else f"replicas{args.gpus}",
+              "l2": "inputs larger than L2 (44.8 GB weights per step)"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -264,6 +278,21 @@ def main():
     slots = N_SEQ + 8
     budget = slots * gdn_slot + pages * page_bytes
     sess = pkg.DeviceSession(store, cfg, slots=slots, budget_bytes=budget)
+    args.ep = args.ep or args.ep_nccl
+    if args.ep:  # every rank joins before its first step; all ranks then step in lockstep
+        import torch.distributed as dist
+        if args.ep_nccl:
+            obj = [pkg.ep_unique_id() if rank == 0 else None]
+            if world > 1:
+                dist.broadcast_object_list(obj, src=0)
+            sess.ep_init(world, rank, obj[0], N_SEQ)
+        else:
+            handle = sess.ep_window(world, rank, N_SEQ)
+            handles = [handle]
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, handle)
+            sess.ep_connect(handles)
     parents = [sess.synthetic_state(int(L), 1000 + s) for s, L in enumerate(ctx)]
     pos = ctx.astype(np.uint32).copy()
     rng = np.random.default_rng(SEED)
@@ -309,6 +338,16 @@ def main():
     one_step()
     routing = sess.debug_routing(N_SEQ)
     sess.set_capture(False)
+    expert_range = None
+    if args.ep:  # this rank's expert block is hit by every rank's tokens
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.from_numpy(np.ascontiguousarray(routing)).to("cuda")
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            routing = np.concatenate([x.cpu().numpy() for x in parts], axis=1)
+        per = cfg.experts // world
+        expert_range = (rank * per, (rank + 1) * per)
     dev_s = (total1 - total0) / 1e3
     dev_s = max_over_ranks(dev_s, world)
     wall = max_over_ranks(wall, world)
@@ -316,10 +355,11 @@ def main():
     value = tokens_total / dev_s
     e2e = tokens_total / wall
     stage_ms = [(b - a) / prof_steps for a, b in zip(stage0, stage1)]
+    barrier(world)  # every rank has finished its steps (expert-parallel windows stay valid until here)
     if rank != 0:
         return
     hbm, tflops, peak_kind = measured_peaks()
-    bytes_per, mean_ue = stage_bytes(cfg, ctx, routing)
+    bytes_per, mean_ue = stage_bytes(cfg, ctx, routing, expert_range)
     dom = max(bytes_per, key=lambda k: stage_ms[STAGES.index(k)])
     dom_ms = stage_ms[STAGES.index(dom)]
     achieved = bytes_per[dom] / (dom_ms / 1e3) / 1e9

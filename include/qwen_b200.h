@@ -241,6 +241,19 @@ int rs_qwen_device_mtp_verify_accept(void* session, size_t n_seq, const StateId*
 int rs_qwen_ep_unique_id(uint8_t* out, size_t out_bytes, char* error, size_t capacity);
 int rs_qwen_device_ep_init(void* session, int world, int rank, const uint8_t* id, size_t id_bytes,
                            size_t cap_tokens, char* error, size_t capacity);
+/* The same mode over direct NVLink stores instead of NCCL (one process per
+ * GPU, all GPUs visible to every process): rs_qwen_device_ep_window allocates
+ * this rank's window (the stages other ranks write to it and their epoch
+ * flags) and returns its 64-byte CUDA IPC handle; once every rank has one,
+ * rs_qwen_device_ep_connect(handles of ranks 0..world-1) maps the peers'
+ * windows. The pack and return kernels then store only the valid rows into
+ * the owner's window and raise a flag (bounded waits on the reader side);
+ * same lockstep rules. Every rank must have finished its steps before any
+ * session is destroyed. */
+int rs_qwen_device_ep_window(void* session, int world, int rank, size_t cap_tokens, uint8_t* handle,
+                             size_t handle_bytes, char* error, size_t capacity);
+int rs_qwen_device_ep_connect(void* session, const uint8_t* handles, size_t handles_bytes, char* error,
+                              size_t capacity);
 
 /* NEW (no reference counterpart; stands in for a long prefill when measuring
  * decode at long contexts): create a published version at `position` whose

@@ -97,6 +97,8 @@ SIGNATURES = {
     "rs_qwen_device_set_profile": (C.c_int, [_P, C.c_int, _ERR, _SZ]),
     "rs_qwen_ep_unique_id": (C.c_int, [C.c_void_p, _SZ, _ERR, _SZ]),
     "rs_qwen_device_ep_init": (C.c_int, [_P, C.c_int, C.c_int, C.c_void_p, _SZ, _SZ, _ERR, _SZ]),
+    "rs_qwen_device_ep_window": (C.c_int, [_P, C.c_int, C.c_int, _SZ, C.c_void_p, _SZ, _ERR, _SZ]),
+    "rs_qwen_device_ep_connect": (C.c_int, [_P, C.c_void_p, _SZ, _ERR, _SZ]),
     "rs_qwen_device_timing": (C.c_int, [_P, C.POINTER(C.c_double), _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_routing": (C.c_int, [_P, _I32P, _SZ, _ERR, _SZ]),
     "rs_qwen_device_debug_capture": (C.c_int, [_P, C.c_int, C.c_void_p, _SZ, C.POINTER(_SZ), _ERR, _SZ]),
@@ -367,6 +369,19 @@ class DeviceSession:
         """Join the expert-parallel group (see rs_qwen_device_ep_init)."""
         buf = (C.c_uint8 * len(uid)).from_buffer_copy(uid)
         _call("rs_qwen_device_ep_init", self.h, world, rank, buf, len(uid), cap_tokens)
+
+    def ep_window(self, world: int, rank: int, cap_tokens: int) -> bytes:
+        """Expert parallelism over direct NVLink stores, step 1: allocate this
+        rank's window; returns its CUDA IPC handle (64 bytes) for the peers."""
+        buf = (C.c_uint8 * 64)()
+        _call("rs_qwen_device_ep_window", self.h, world, rank, cap_tokens, buf, 64)
+        return bytes(buf)
+
+    def ep_connect(self, handles):
+        """Step 2: every rank's window handle, in rank order."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _call("rs_qwen_device_ep_connect", self.h, buf, len(blob))
 
     def set_profile(self, on: bool):
         _call("rs_qwen_device_set_profile", self.h, int(on))

@@ -8,7 +8,10 @@
 //   ep_pack          per peer p: a stage = [counts of p's experts][rows], the
 //                    rows being the sorted gathered activations of the
 //                    assignments p owns (contiguous in the sort);
-//   NCCL send/recv   fixed-size stages (cap rows each), one grouped exchange;
+//   transport        either direct NVLink stores of the valid rows into the
+//                    owner's window (CUDA IPC mapping) followed by an epoch
+//                    flag (release at system scope, set by the last CTA), or
+//                    NCCL send/recv of fixed-size stages (cap rows each);
 //   ep_plan          per local expert: rows from every source, in source
 //                    order (then the source's sort order), and the shared
 //                    expert's local rows last -> group offsets over E + 1
@@ -16,7 +19,7 @@
 //   ep_gather        those rows into one bf16 matrix, with each row's origin;
 //   grouped GEMMs    (unchanged) over the local rows;
 //   ep_return_pack   each result row into its source's return stage (fp32);
-//   NCCL send/recv   the return stages;
+//   transport        the same way back (flags / NCCL);
 //   ep_return_unpack every local assignment's result row back to its sorted
 //                    position, so the mixture runs unchanged.
 // A token's expert rows see the same arithmetic as on one GPU (the GEMM's
@@ -33,14 +36,60 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+constexpr long long kEpWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+// Threads 0..world-1 wait (bounded) until flags[t] has reached `epoch`; on
+// expiry kTimeout is raised and the CTA goes on (its results are then void).
+__device__ __forceinline__ void ep_wait_flags(const uint32_t* flags, int world, uint32_t epoch, uint32_t* err) {
+  if (flags && threadIdx.x < world) {
+    const long long t0 = clock64();
+    while (int32_t(ld_acquire_sys(flags + threadIdx.x) - epoch) < 0) {
+      if (clock64() - t0 > kEpWaitCycles) {
+        atomicOr(err, kErrTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+// After every CTA of the grid has written its rows: the last one (device
+// counter, which it resets) publishes `epoch` to every peer's flag.
+__device__ __forceinline__ void ep_signal_last(uint32_t* const* flag_dst, int world, uint32_t epoch, uint32_t* done) {
+  if (!flag_dst) return;
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // this CTA's stores (local and remote) before its arrival
+    last = atomicAdd(done, 1u) == gridDim.x * gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    *done = 0;
+  }
+  if (threadIdx.x < world) st_release_sys(flag_dst[threadIdx.x], epoch);
+}
+
 // Stage layout: [hdr_ints int32 counts (padded to 16 B)] [cap rows x H bf16]
 __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ xperm, const int32_t* __restrict__ counts,
-                               const int32_t* __restrict__ offsets, uint8_t* __restrict__ send, size_t stage_bytes,
-                               int per_rank, int hdr_ints, int cap, int H) {
+                               const int32_t* __restrict__ offsets, uint8_t* const* __restrict__ dst,
+                               int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
+                               uint32_t* done) {
   pdl_trigger();
   pdl_wait();
   const int p = blockIdx.y;
-  uint8_t* st = send + size_t(p) * stage_bytes;
+  uint8_t* st = dst[p];
   const int e0 = p * per_rank;
   if (blockIdx.x == 0)
     for (int j = threadIdx.x; j < hdr_ints; j += blockDim.x)
@@ -54,6 +103,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ xperm, const in
     reinterpret_cast<uint4*>(rows + size_t(row) * H)[c] =
         reinterpret_cast<const uint4*>(xperm + size_t(r0 + row) * H)[c];
   }
+  ep_signal_last(flag_dst, gridDim.y, epoch, done);
 }
 
 // Exclusive scan of v[0..n) by one warp (each lane a consecutive run of
@@ -83,9 +133,11 @@ __device__ int warp_exclusive_scan(const int32_t* v, int32_t* out, int n, int la
 // expert's rows; a source sending more than `cap` rows raises kErrBounds.
 __global__ void ep_plan_kernel(const uint8_t* const* __restrict__ srcs, int world, int rank, int per_rank, int E,
                                const int32_t* __restrict__ counts, int32_t* __restrict__ goff,
-                               int32_t* __restrict__ seg, int32_t* __restrict__ n_rows, uint32_t* err, int cap) {
+                               int32_t* __restrict__ seg, int32_t* __restrict__ n_rows, uint32_t* err, int cap,
+                               const uint32_t* wait_flags, uint32_t epoch) {
   pdl_trigger();
   pdl_wait();
+  ep_wait_flags(wait_flags, world, epoch, err);
   extern __shared__ int32_t sm[];
   const int n = world * per_rank;
   int32_t* cnt_pe = sm;           // [world][per_rank]  (stage order)
@@ -173,25 +225,29 @@ __global__ void ep_gather_kernel(const uint8_t* const* __restrict__ srcs, int wo
 // Result rows back: routed rows into their source's return stage (fp32,
 // cap rows per source), shared rows straight into the sorted result matrix.
 __global__ void ep_return_pack_kernel(const float* __restrict__ yloc, const int32_t* __restrict__ origin,
-                                      const int32_t* __restrict__ n_rows, float* __restrict__ rsend,
-                                      float* __restrict__ y_sorted, int cap, int H) {
+                                      const int32_t* __restrict__ n_rows, float* const* __restrict__ rdst,
+                                      float* __restrict__ y_sorted, int cap, int H, int world,
+                                      uint32_t* const* flag_dst, uint32_t epoch, uint32_t* done) {
   pdl_trigger();
   pdl_wait();
   const int n = *n_rows;
   const int h4 = H / 4;
   for (int row = blockIdx.x; row < n; row += gridDim.x) {
-    const int o = origin[row];
-    float* dst = o >= 0 ? rsend + size_t(o) * H : y_sorted + size_t(-1 - o) * H;  // o = p * cap + stage row
+    const int o = origin[row];  // p * cap + stage row, or -1 - sorted position (shared expert)
+    float* dst = o >= 0 ? rdst[o / cap] + size_t(o % cap) * H : y_sorted + size_t(-1 - o) * H;
     const float4* src = reinterpret_cast<const float4*>(yloc + size_t(row) * H);
     for (int c = threadIdx.x; c < h4; c += blockDim.x) reinterpret_cast<float4*>(dst)[c] = src[c];
   }
+  ep_signal_last(flag_dst, world, epoch, done);
 }
 
 // Every local routed assignment's result from its owner's return stage.
 __global__ void ep_return_unpack_kernel(const float* const* __restrict__ rsrcs, const int32_t* __restrict__ offsets,
-                                        float* __restrict__ y_sorted, int world, int per_rank, int H) {
+                                        float* __restrict__ y_sorted, int world, int per_rank, int H,
+                                        const uint32_t* wait_flags, uint32_t epoch, uint32_t* err) {
   pdl_trigger();
   pdl_wait();
+  ep_wait_flags(wait_flags, world, epoch, err);
   const int n_routed = offsets[world * per_rank];
   const int h4 = H / 4;
   for (int q = blockIdx.x; q < n_routed; q += gridDim.x) {
@@ -205,10 +261,11 @@ __global__ void ep_return_unpack_kernel(const float* const* __restrict__ rsrcs, 
 
 }  // namespace
 
-void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* send,
-                    size_t stage_bytes, int world, int per_rank, int hdr_ints, int cap, int H, cudaStream_t s) {
-  launch_pdl(ep_pack_kernel, dim3(64, world), 256, 0, s, xperm, counts, offsets, send, stage_bytes, per_rank, hdr_ints,
-             cap, H);
+void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* const* dst,
+                    int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
+                    uint32_t* done, cudaStream_t s) {
+  launch_pdl(ep_pack_kernel, dim3(64, world), 256, 0, s, xperm, counts, offsets, dst, per_rank, hdr_ints, cap, H,
+             flag_dst, epoch, done);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
@@ -216,28 +273,32 @@ void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
                            const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xperm, int32_t* goff,
                            int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
-                           int max_rows, uint32_t* err, int sm_count, cudaStream_t s) {
+                           int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
+                           cudaStream_t s) {
   const size_t n = size_t(world) * per_rank;
   if (4 * n * 4 > 48 * 1024) throw std::invalid_argument("expert-parallel plan: too many (expert, rank) segments");
-  launch_pdl(ep_plan_kernel, 1, 256, 4 * n * 4, s, srcs, world, rank, per_rank, E, counts, goff, seg, n_rows, err, cap);
+  launch_pdl(ep_plan_kernel, 1, 256, 4 * n * 4, s, srcs, world, rank, per_rank, E, counts, goff, seg, n_rows, err, cap,
+             wait_flags, epoch);
   launch_pdl(ep_gather_kernel, std::max(1, std::min(max_rows, 4 * sm_count)), 256, 2 * n * 4, s, srcs, world, per_rank,
              hdr_ints, E, goff, seg, offsets, xperm, xloc, origin, cap, H, rank);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(2, std::memory_order_relaxed);
 }
 
-void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n_rows, float* rsend, float* y_sorted,
-                      int cap, int H, int max_rows, int sm_count, cudaStream_t s) {
+void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n_rows, float* const* rdst,
+                      float* y_sorted, int cap, int H, int world, int max_rows, uint32_t* const* flag_dst,
+                      uint32_t epoch, uint32_t* done, int sm_count, cudaStream_t s) {
   launch_pdl(ep_return_pack_kernel, std::max(1, std::min(max_rows, 4 * sm_count)), 256, 0, s, yloc, origin, n_rows,
-             rsend, y_sorted, cap, H);
+             rdst, y_sorted, cap, H, world, flag_dst, epoch, done);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 void launch_ep_return_unpack(const float* const* rsrcs, const int32_t* offsets, float* y_sorted, int world,
-                             int per_rank, int H, int max_rows, int sm_count, cudaStream_t s) {
+                             int per_rank, int H, int max_rows, const uint32_t* wait_flags, uint32_t epoch,
+                             uint32_t* err, int sm_count, cudaStream_t s) {
   launch_pdl(ep_return_unpack_kernel, std::max(1, std::min(max_rows, 4 * sm_count)), 256, 0, s, rsrcs, offsets,
-             y_sorted, world, per_rank, H);
+             y_sorted, world, per_rank, H, wait_flags, epoch, err);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }

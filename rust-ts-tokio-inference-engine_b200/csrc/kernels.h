@@ -117,17 +117,23 @@ void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint3
                    uint32_t* done, cudaStream_t s);
 void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,
                         GdnPool pool, int slot, const Dims& d, uint64_t seed, cudaStream_t s);
-// Expert parallelism (ep.cu): stage packing, local row plan / gather, result return.
-void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* send,
-                    size_t stage_bytes, int world, int per_rank, int hdr_ints, int cap, int H, cudaStream_t s);
+// Expert parallelism (ep.cu): stage packing, local row plan / gather, result
+// return. Per-peer destination tables; flag tables / wait flags non-null for
+// the direct NVLink transport (null with NCCL).
+void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* const* dst,
+                    int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
+                    uint32_t* done, cudaStream_t s);
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
                            const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xperm, int32_t* goff,
                            int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
-                           int max_rows, uint32_t* err, int sm_count, cudaStream_t s);
-void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n_rows, float* rsend, float* y_sorted,
-                      int cap, int H, int max_rows, int sm_count, cudaStream_t s);
+                           int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
+                           cudaStream_t s);
+void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n_rows, float* const* rdst,
+                      float* y_sorted, int cap, int H, int world, int max_rows, uint32_t* const* flag_dst,
+                      uint32_t epoch, uint32_t* done, int sm_count, cudaStream_t s);
 void launch_ep_return_unpack(const float* const* rsrcs, const int32_t* offsets, float* y_sorted, int world,
-                             int per_rank, int H, int max_rows, int sm_count, cudaStream_t s);
+                             int per_rank, int H, int max_rows, const uint32_t* wait_flags, uint32_t epoch,
+                             uint32_t* err, int sm_count, cudaStream_t s);
 void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
                         __nv_bfloat16* dst, cudaStream_t s);
 

@@ -279,21 +279,36 @@ struct Session {
   // fixed-size NCCL stages of `cap` = cap_tokens * top rows per peer, so a step
   // needs no host synchronisation. All ranks must step in lockstep (the same
   // number of target steps, each with at most cap_tokens tokens).
+  // Two transports: direct NVLink stores into every rank's window (a CUDA IPC
+  // mapped allocation holding the stages addressed to that rank and epoch
+  // flags; `p2p`), or NCCL send/recv of fixed-size stages.
   struct EpState {
-    bool on = false;
+    bool on = false, p2p = false;
     int world = 1, rank = 0, per_rank = 0, cap_tokens = 0, cap = 0, hdr_ints = 0, max_rows = 0;
-    size_t stage_bytes = 0;
+    size_t stage_bytes = 0, disp_bytes = 0, ret_bytes = 0, win_bytes = 0;
+    uint32_t epoch = 0;
     ncclComm_t comm = nullptr;
-    DevBuf<uint8_t> send, recv;
+    uint8_t* window = nullptr;            // p2p: [world][stage] dispatch | [world][cap*H] f32 return | flags
+    std::vector<void*> peer_windows;      // p2p: opened peer mappings (nullptr for this rank)
+    DevBuf<uint8_t> send, recv;           // nccl: per-peer stages
     DevBuf<float> rsend, rrecv, yloc;
     DevBuf<__nv_bfloat16> xloc, actloc;
     DevBuf<int32_t> goff, seg, origin, n_rows;
-    DevBuf<uint64_t> srcs, rsrcs;  // device tables of the stage pointers per source rank
+    DevBuf<uint32_t> done;                // last-CTA counters (pack, return)
+    // device pointer tables, world entries each: where this rank writes for
+    // peer p (dispatch / return), flags it raises at p, where it reads
+    // source p's stages (dispatch / return)
+    DevBuf<uint64_t> disp_dst, ret_dst, disp_flag, ret_flag, srcs, rsrcs;
+    const uint32_t* wait_disp = nullptr;  // p2p: this rank's flag arrays
+    const uint32_t* wait_ret = nullptr;
   } ep;
   bool in_mtp = false;  // the MTP head's MoE computes every expert locally
 
   ~Session() {
     if (ep.comm) ncclCommDestroy(ep.comm);
+    for (void* w : ep.peer_windows)
+      if (w) cudaIpcCloseMemHandle(w);
+    if (ep.window) cudaFree(ep.window);
     for (auto e : ev_pool) cudaEventDestroy(e);
     if (ev_begin) cudaEventDestroy(ev_begin);
     if (ev_end) cudaEventDestroy(ev_end);
@@ -1077,8 +1092,8 @@ struct Session {
     mtp_unref(pages);
   }
 
-  void ep_init(int world, int rank, const ncclUniqueId& uid, int cap_tokens) {
-    if (ep.on) throw std::invalid_argument("expert parallelism already initialised");
+  void ep_alloc(int world, int rank, int cap_tokens) {
+    if (ep.on || ep.world > 1 || ep.window || ep.comm) throw std::invalid_argument("expert parallelism already initialised");
     if (world < 1 || rank < 0 || rank >= world || d.E % world) throw std::invalid_argument("expert-parallel geometry");
     if (cap_tokens < 1 || cap_tokens > max_tokens) throw std::invalid_argument("expert-parallel token capacity");
     set_device();
@@ -1090,10 +1105,6 @@ struct Session {
     ep.hdr_ints = (ep.per_rank + 3) & ~3;
     ep.stage_bytes = size_t(ep.hdr_ints) * 4 + size_t(ep.cap) * d.H * 2;
     ep.max_rows = world * ep.cap + cap_tokens;  // routed rows from every source + this rank's shared rows
-    ep.send.ensure(size_t(world) * ep.stage_bytes);
-    ep.recv.ensure(size_t(world) * ep.stage_bytes);
-    ep.rsend.ensure(size_t(world) * ep.cap * d.H);
-    ep.rrecv.ensure(size_t(world) * ep.cap * d.H);
     ep.xloc.ensure(size_t(ep.max_rows) * d.H);
     ep.actloc.ensure(size_t(ep.max_rows) * d.I);
     ep.yloc.ensure(size_t(ep.max_rows) * d.H);
@@ -1101,17 +1112,84 @@ struct Session {
     ep.seg.ensure(size_t(2) * world * ep.per_rank);
     ep.origin.ensure(ep.max_rows);
     ep.n_rows.ensure(1);
-    std::vector<uint64_t> srcs(world), rsrcs(world);
+    ep.done.ensure(2);
+    QWEN_CUDA(cudaMemset(ep.done.p, 0, 8));
+    for (auto* t : {&ep.disp_dst, &ep.ret_dst, &ep.disp_flag, &ep.ret_flag, &ep.srcs, &ep.rsrcs}) t->ensure(world);
+  }
+  void ep_tables(const std::vector<uint64_t>& disp_dst, const std::vector<uint64_t>& ret_dst,
+                 const std::vector<uint64_t>& disp_flag, const std::vector<uint64_t>& ret_flag,
+                 const std::vector<uint64_t>& srcs, const std::vector<uint64_t>& rsrcs) {
+    const size_t b = size_t(ep.world) * 8;
+    QWEN_CUDA(cudaMemcpy(ep.disp_dst.p, disp_dst.data(), b, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.ret_dst.p, ret_dst.data(), b, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.disp_flag.p, disp_flag.data(), b, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.ret_flag.p, ret_flag.data(), b, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.srcs.p, srcs.data(), b, cudaMemcpyHostToDevice));
+    QWEN_CUDA(cudaMemcpy(ep.rsrcs.p, rsrcs.data(), b, cudaMemcpyHostToDevice));
+  }
+
+  // NCCL transport.
+  void ep_init(int world, int rank, const ncclUniqueId& uid, int cap_tokens) {
+    ep_alloc(world, rank, cap_tokens);
+    ep.send.ensure(size_t(world) * ep.stage_bytes);
+    ep.recv.ensure(size_t(world) * ep.stage_bytes);
+    ep.rsend.ensure(size_t(world) * ep.cap * d.H);
+    ep.rrecv.ensure(size_t(world) * ep.cap * d.H);
+    std::vector<uint64_t> dd(world), rd(world), z(world, 0), sr(world), rs(world);
     for (int p = 0; p < world; ++p) {
-      srcs[p] = reinterpret_cast<uint64_t>((p == rank ? ep.send.p : ep.recv.p) + size_t(p) * ep.stage_bytes);
-      rsrcs[p] = reinterpret_cast<uint64_t>((p == rank ? ep.rsend.p : ep.rrecv.p) + size_t(p) * ep.cap * d.H);
+      dd[p] = reinterpret_cast<uint64_t>(ep.send.p + size_t(p) * ep.stage_bytes);
+      rd[p] = reinterpret_cast<uint64_t>(ep.rsend.p + size_t(p) * ep.cap * d.H);
+      sr[p] = reinterpret_cast<uint64_t>((p == rank ? ep.send.p : ep.recv.p) + size_t(p) * ep.stage_bytes);
+      rs[p] = reinterpret_cast<uint64_t>((p == rank ? ep.rsend.p : ep.rrecv.p) + size_t(p) * ep.cap * d.H);
     }
-    ep.srcs.ensure(world);
-    ep.rsrcs.ensure(world);
-    QWEN_CUDA(cudaMemcpy(ep.srcs.p, srcs.data(), size_t(world) * 8, cudaMemcpyHostToDevice));
-    QWEN_CUDA(cudaMemcpy(ep.rsrcs.p, rsrcs.data(), size_t(world) * 8, cudaMemcpyHostToDevice));
+    ep_tables(dd, rd, z, z, sr, rs);
     const ncclResult_t r = ncclCommInitRank(&ep.comm, world, uid, rank);
     if (r != ncclSuccess) throw std::runtime_error(std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    ep.on = true;
+  }
+
+  // Direct NVLink transport, step 1: this rank's window (stages addressed to
+  // it and its flags), exported as a CUDA IPC handle.
+  void ep_window(int world, int rank, int cap_tokens, cudaIpcMemHandle_t* handle) {
+    ep_alloc(world, rank, cap_tokens);
+    ep.disp_bytes = size_t(world) * ep.stage_bytes;
+    ep.ret_bytes = size_t(world) * ep.cap * d.H * 4;
+    ep.win_bytes = ep.disp_bytes + ep.ret_bytes + 256;
+    QWEN_CUDA(cudaMalloc(&ep.window, ep.win_bytes));
+    QWEN_CUDA(cudaMemset(ep.window + ep.disp_bytes + ep.ret_bytes, 0, 256));  // epoch flags start at 0
+    QWEN_CUDA(cudaIpcGetMemHandle(handle, ep.window));
+  }
+  // Step 2: open every peer's window and build the tables.
+  void ep_connect(const cudaIpcMemHandle_t* handles) {
+    if (!ep.window || ep.on) throw std::invalid_argument("expert-parallel window missing or already connected");
+    set_device();
+    const int world = ep.world, me = ep.rank;
+    ep.peer_windows.assign(world, nullptr);
+    std::vector<uint8_t*> win(world);
+    for (int p = 0; p < world; ++p) {
+      if (p == me) {
+        win[p] = ep.window;
+        continue;
+      }
+      void* ptr = nullptr;
+      QWEN_CUDA(cudaIpcOpenMemHandle(&ptr, handles[p], cudaIpcMemLazyEnablePeerAccess));
+      ep.peer_windows[p] = ptr;
+      win[p] = static_cast<uint8_t*>(ptr);
+    }
+    const size_t flags_off = ep.disp_bytes + ep.ret_bytes;
+    std::vector<uint64_t> dd(world), rd(world), df(world), rf(world), sr(world), rs(world);
+    for (int p = 0; p < world; ++p) {
+      dd[p] = reinterpret_cast<uint64_t>(win[p] + size_t(me) * ep.stage_bytes);
+      rd[p] = reinterpret_cast<uint64_t>(win[p] + ep.disp_bytes + size_t(me) * ep.cap * d.H * 4);
+      df[p] = reinterpret_cast<uint64_t>(win[p] + flags_off + size_t(me) * 4);
+      rf[p] = reinterpret_cast<uint64_t>(win[p] + flags_off + size_t(world + me) * 4);
+      sr[p] = reinterpret_cast<uint64_t>(ep.window + size_t(p) * ep.stage_bytes);
+      rs[p] = reinterpret_cast<uint64_t>(ep.window + ep.disp_bytes + size_t(p) * ep.cap * d.H * 4);
+    }
+    ep_tables(dd, rd, df, rf, sr, rs);
+    ep.wait_disp = reinterpret_cast<const uint32_t*>(ep.window + flags_off);
+    ep.wait_ret = ep.wait_disp + world;
+    ep.p2p = true;
     ep.on = true;
   }
 
@@ -1132,13 +1210,20 @@ struct Session {
   void moe_ep(const LayerDev& ly, int T, int A, cudaStream_t s) {
     if (T > ep.cap_tokens) throw std::logic_error("expert-parallel step above its token capacity");
     const int world = ep.world;
+    const uint32_t epoch = ++ep.epoch;  // the same on every rank (lockstep)
+    uint32_t* const* dflag = ep.p2p ? reinterpret_cast<uint32_t* const*>(ep.disp_flag.p) : nullptr;
+    uint32_t* const* rflag = ep.p2p ? reinterpret_cast<uint32_t* const*>(ep.ret_flag.p) : nullptr;
     launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
-    launch_ep_pack(xperm.p, counts.p, offsets.p, ep.send.p, ep.stage_bytes, world, ep.per_rank, ep.hdr_ints, ep.cap,
-                   d.H, s);
-    ep_exchange(ep.send.p, ep.recv.p, ep.stage_bytes, s);
+    launch_ep_pack(xperm.p, counts.p, offsets.p, reinterpret_cast<uint8_t* const*>(ep.disp_dst.p), world, ep.per_rank,
+                   ep.hdr_ints, ep.cap, d.H, dflag, epoch, ep.done.p, s);
+    if (!ep.p2p) {
+      stage(15);  // MoeMerge: the expert-parallel exchanges
+      ep_exchange(ep.send.p, ep.recv.p, ep.stage_bytes, s);
+      stage(11);  // MoeUpGate
+    }
     launch_ep_plan_gather(reinterpret_cast<const uint8_t* const*>(ep.srcs.p), world, ep.rank, ep.per_rank, ep.hdr_ints,
                           d.E, counts.p, offsets.p, xperm.p, ep.goff.p, ep.seg.p, ep.n_rows.p, ep.xloc.p, ep.origin.p,
-                          ep.cap, d.H, ep.max_rows, err.p, sm_count, s);
+                          ep.cap, d.H, ep.max_rows, err.p, ep.p2p ? ep.wait_disp : nullptr, epoch, sm_count, s);
     const int per_expert = (world * T * d.top + T + d.E) / (d.E + 1);
     const int box = box_for(std::max(1, 2 * per_expert));
     TcArgs gu;
@@ -1164,10 +1249,15 @@ struct Session {
     dn.ldy = d.H;
     dn.err = err.p;
     launch_tc(ep.actloc.p, ep.max_rows, dn, s);
-    launch_ep_return(ep.yloc.p, ep.origin.p, ep.n_rows.p, ep.rsend.p, moe_y.p, ep.cap, d.H, ep.max_rows, sm_count, s);
-    ep_exchange(ep.rsend.p, ep.rrecv.p, size_t(ep.cap) * d.H * 4, s);
+    launch_ep_return(ep.yloc.p, ep.origin.p, ep.n_rows.p, reinterpret_cast<float* const*>(ep.ret_dst.p), moe_y.p,
+                     ep.cap, d.H, world, ep.max_rows, rflag, epoch, ep.done.p + 1, sm_count, s);
+    if (!ep.p2p) {
+      stage(15);  // MoeMerge
+      ep_exchange(ep.rsend.p, ep.rrecv.p, size_t(ep.cap) * d.H * 4, s);
+      stage(12);  // MoeDown
+    }
     launch_ep_return_unpack(reinterpret_cast<const float* const*>(ep.rsrcs.p), offsets.p, moe_y.p, world, ep.per_rank,
-                            d.H, A, sm_count, s);
+                            d.H, A, ep.p2p ? ep.wait_ret : nullptr, epoch, err.p, sm_count, s);
   }
 
   void moe(const LayerDev& ly, int T, int A, cudaStream_t s) {
@@ -1799,6 +1889,29 @@ int rs_qwen_device_ep_init(void* session, int world, int rank, const uint8_t* id
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     S(session)->ep_init(world, rank, uid, int(cap_tokens));
+  });
+}
+
+int rs_qwen_device_ep_window(void* session, int world, int rank, size_t cap_tokens, uint8_t* handle,
+                             size_t handle_bytes, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!handle || handle_bytes != sizeof(cudaIpcMemHandle_t) || cap_tokens > size_t(1) << 30)
+      throw std::invalid_argument("expert-parallel window arguments");
+    cudaIpcMemHandle_t h;
+    S(session)->ep_window(world, rank, int(cap_tokens), &h);
+    std::memcpy(handle, &h, sizeof(h));
+  });
+}
+
+int rs_qwen_device_ep_connect(void* session, const uint8_t* handles, size_t handles_bytes, char* error,
+                              size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!handles || handles_bytes != size_t(s->ep.world) * sizeof(cudaIpcMemHandle_t))
+      throw std::invalid_argument("expert-parallel handles");
+    std::vector<cudaIpcMemHandle_t> hs(s->ep.world);
+    std::memcpy(hs.data(), handles, handles_bytes);
+    s->ep_connect(hs.data());
   });
 }
 

@@ -42,60 +42,85 @@ def _steps(pkg, cfg, sess, seed, n_seq):
     return s1, l1, s2, l2
 
 
-def _compare(pkg, cfg, store, world, rank, uid, seed, n_seq):
+def _compare(pkg, cfg, store, world, rank, uid, seed, n_seq, exchange=None):
+    """uid: NCCL transport; exchange(handle) -> all handles: direct NVLink stores
+    (every rank then finishes its steps before any window is freed)."""
     plain = pkg.DeviceSession(store, cfg, slots=4 * n_seq, budget_bytes=2 << 30)
     ep = pkg.DeviceSession(store, cfg, slots=4 * n_seq, budget_bytes=2 << 30)
-    ep.ep_init(world, rank, uid, n_seq + 2)
+    if exchange is None:
+        ep.ep_init(world, rank, uid, n_seq + 2)
+    else:
+        ep.ep_connect(exchange(ep.ep_window(world, rank, n_seq + 2)))
     try:
         a = _steps(pkg, cfg, plain, seed, n_seq)
         b = _steps(pkg, cfg, ep, seed, n_seq)
+        if exchange is not None:
+            exchange(b"done")
     finally:
         ep.close()
         plain.close()
     return all(np.array_equal(x, y) for x, y in zip(a, b))
 
 
+@pytest.mark.parametrize("transport", ["nccl", "nvlink"])
 @pytest.mark.parametrize("widths", ["cfg0", "cfg1"])
-def test_expert_parallel_world1_equals_plain(pkg, widths):
+def test_expert_parallel_world1_equals_plain(pkg, widths, transport):
     if not has_cuda():
         pytest.skip("no CUDA device")
     cfg = pkg.config0() if widths == "cfg0" else pkg.config1(layers=4, context=1024)
     store = pkg.WeightStore().synthetic(cfg, 77)
     try:
-        assert _compare(pkg, cfg, store, 1, 0, pkg.ep_unique_id(), 5, 6)
+        if transport == "nccl":
+            assert _compare(pkg, cfg, store, 1, 0, pkg.ep_unique_id(), 5, 6)
+        else:
+            assert _compare(pkg, cfg, store, 1, 0, None, 5, 6, exchange=lambda h: [h] if h != b"done" else None)
     finally:
         store.close()
 
 
-def _rank_main(rank, world, q_id, q_out):
-    os.environ["CUDA_VISIBLE_DEVICES"] = str(rank)
+def _rank_main(rank, world, transport, qs, q_out):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     sys.path.insert(0, str(ROOT))
     import importlib
+    import torch
+    torch.cuda.set_device(rank)  # every GPU stays visible (peer windows)
     pkg = importlib.import_module("rust-ts-tokio-inference-engine_b200")
     try:
-        if rank == 0:
-            uid = pkg.ep_unique_id()
-            for _ in range(world - 1):
-                q_id.put(uid)
-        else:
-            uid = q_id.get(timeout=120)
+        def exchange(h):  # every rank's handle, in rank order
+            for p in range(world):
+                if p != rank:
+                    qs[p].put((rank, h))
+            got = {rank: h}
+            while len(got) < world:
+                r, hp = qs[rank].get(timeout=120)
+                got[r] = hp
+            return [got[p] for p in range(world)]
+        uid = None
+        if transport == "nccl":
+            if rank == 0:
+                uid = pkg.ep_unique_id()
+                for p in range(1, world):
+                    qs[p].put((0, uid))
+            else:
+                uid = qs[rank].get(timeout=120)[1]
         cfg = pkg.config1(layers=4, context=1024)
         store = pkg.WeightStore().synthetic(cfg, 77)
-        ok = _compare(pkg, cfg, store, world, rank, uid, 11 + rank, 5)
-        store.close()
+        ok = _compare(pkg, cfg, store, world, rank, uid, 11 + rank, 5,
+                      exchange=exchange if transport == "nvlink" else None)
         q_out.put((rank, bool(ok), ""))
+        store.close()
     except Exception as e:  # reported to the parent; never left hanging
         q_out.put((rank, False, repr(e)))
 
 
-def test_expert_parallel_two_gpus_equals_plain():
+@pytest.mark.parametrize("transport", ["nccl", "nvlink"])
+def test_expert_parallel_two_gpus_equals_plain(transport):
     import torch
     if not has_cuda() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
-    q_id, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, q_id, q_out)) for r in range(2)]
+    qs, q_out = [ctx.Queue() for _ in range(2)], ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, transport, qs, q_out)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
