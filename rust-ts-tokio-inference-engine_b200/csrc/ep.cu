@@ -82,7 +82,10 @@ __device__ __forceinline__ void ep_signal_last(uint32_t* const* flag_dst, int wo
 }
 
 // Stage layout: [hdr_ints int32 counts (padded to 16 B)] [cap rows x H bf16]
-__global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ xperm, const int32_t* __restrict__ counts,
+// Rows come straight from the MoE input: sorted position q is row perm[q] / div
+// of `src` (stride ld), so no gathered copy is made first.
+__global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ src, int ld, const int32_t* __restrict__ perm,
+                               int div, const int32_t* __restrict__ counts,
                                const int32_t* __restrict__ offsets, uint8_t* const* __restrict__ dst,
                                int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                                uint32_t* done) {
@@ -101,7 +104,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ xperm, const in
     if (idx / h8 >= cap) break;  // cannot happen: n <= cap is checked by the planner of the step
     const int row = idx / h8, c = idx - row * h8;
     reinterpret_cast<uint4*>(rows + size_t(row) * H)[c] =
-        reinterpret_cast<const uint4*>(xperm + size_t(r0 + row) * H)[c];
+        reinterpret_cast<const uint4*>(src + size_t(perm[r0 + row] / div) * ld)[c];
   }
   ep_signal_last(flag_dst, gridDim.y, epoch, done);
 }
@@ -185,7 +188,8 @@ __global__ void ep_plan_kernel(const uint8_t* const* __restrict__ srcs, int worl
 // stage row for routed rows, -1 - sorted position for shared rows.
 __global__ void ep_gather_kernel(const uint8_t* const* __restrict__ srcs, int world, int per_rank, int hdr_ints,
                                  int E, const int32_t* __restrict__ goff, const int32_t* __restrict__ seg,
-                                 const int32_t* __restrict__ offsets, const __nv_bfloat16* __restrict__ xperm,
+                                 const int32_t* __restrict__ offsets, const __nv_bfloat16* __restrict__ xsrc, int ld,
+                                 const int32_t* __restrict__ perm, int div,
                                  __nv_bfloat16* __restrict__ xloc, int32_t* __restrict__ origin, int cap, int H,
                                  int rank) {
   pdl_trigger();
@@ -214,7 +218,7 @@ __global__ void ep_gather_kernel(const uint8_t* const* __restrict__ srcs, int wo
       if (threadIdx.x == 0) origin[row] = p * cap + srow;
     } else {
       const int q = offsets[E] + (row - n_routed);
-      src = reinterpret_cast<const uint4*>(xperm + size_t(q) * H);
+      src = reinterpret_cast<const uint4*>(xsrc + size_t(perm[q] / div) * ld);
       if (threadIdx.x == 0) origin[row] = -1 - q;
     }
     uint4* dst = reinterpret_cast<uint4*>(xloc + size_t(row) * H);
@@ -261,17 +265,20 @@ __global__ void ep_return_unpack_kernel(const float* const* __restrict__ rsrcs, 
 
 }  // namespace
 
-void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* const* dst,
+void launch_ep_pack(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, const int32_t* counts,
+                    const int32_t* offsets, uint8_t* const* dst,
                     int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                     uint32_t* done, cudaStream_t s) {
-  launch_pdl(ep_pack_kernel, dim3(64, world), 256, 0, s, xperm, counts, offsets, dst, per_rank, hdr_ints, cap, H,
+  launch_pdl(ep_pack_kernel, dim3(64, world), 256, 0, s, src, ld, perm, div, counts, offsets, dst, per_rank, hdr_ints,
+             cap, H,
              flag_dst, epoch, done);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
-                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xperm, int32_t* goff,
+                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xsrc, int ld,
+                           const int32_t* perm, int div, int32_t* goff,
                            int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
                            int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
                            cudaStream_t s) {
@@ -280,7 +287,7 @@ void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int 
   launch_pdl(ep_plan_kernel, 1, 256, 4 * n * 4, s, srcs, world, rank, per_rank, E, counts, goff, seg, n_rows, err, cap,
              wait_flags, epoch);
   launch_pdl(ep_gather_kernel, std::max(1, std::min(max_rows, 4 * sm_count)), 256, 2 * n * 4, s, srcs, world, per_rank,
-             hdr_ints, E, goff, seg, offsets, xperm, xloc, origin, cap, H, rank);
+             hdr_ints, E, goff, seg, offsets, xsrc, ld, perm, div, xloc, origin, cap, H, rank);
   QWEN_CUDA(cudaGetLastError());
   g_kernel_launches.fetch_add(2, std::memory_order_relaxed);
 }

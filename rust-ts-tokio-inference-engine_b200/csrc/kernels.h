@@ -120,11 +120,13 @@ void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int positi
 // Expert parallelism (ep.cu): stage packing, local row plan / gather, result
 // return. Per-peer destination tables; flag tables / wait flags non-null for
 // the direct NVLink transport (null with NCCL).
-void launch_ep_pack(const __nv_bfloat16* xperm, const int32_t* counts, const int32_t* offsets, uint8_t* const* dst,
+void launch_ep_pack(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, const int32_t* counts,
+                    const int32_t* offsets, uint8_t* const* dst,
                     int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                     uint32_t* done, cudaStream_t s);
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
-                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xperm, int32_t* goff,
+                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xsrc, int ld,
+                           const int32_t* perm, int div, int32_t* goff,
                            int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
                            int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
                            cudaStream_t s);

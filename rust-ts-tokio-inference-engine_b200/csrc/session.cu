@@ -1213,16 +1213,16 @@ struct Session {
     const uint32_t epoch = ++ep.epoch;  // the same on every rank (lockstep)
     uint32_t* const* dflag = ep.p2p ? reinterpret_cast<uint32_t* const*>(ep.disp_flag.p) : nullptr;
     uint32_t* const* rflag = ep.p2p ? reinterpret_cast<uint32_t* const*>(ep.ret_flag.p) : nullptr;
-    launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
-    launch_ep_pack(xperm.p, counts.p, offsets.p, reinterpret_cast<uint8_t* const*>(ep.disp_dst.p), world, ep.per_rank,
-                   ep.hdr_ints, ep.cap, d.H, dflag, epoch, ep.done.p, s);
+    launch_ep_pack(hb.p, d.H, perm.p, d.top + 1, counts.p, offsets.p, reinterpret_cast<uint8_t* const*>(ep.disp_dst.p),
+                   world, ep.per_rank, ep.hdr_ints, ep.cap, d.H, dflag, epoch, ep.done.p, s);
     if (!ep.p2p) {
       stage(15);  // MoeMerge: the expert-parallel exchanges
       ep_exchange(ep.send.p, ep.recv.p, ep.stage_bytes, s);
       stage(11);  // MoeUpGate
     }
     launch_ep_plan_gather(reinterpret_cast<const uint8_t* const*>(ep.srcs.p), world, ep.rank, ep.per_rank, ep.hdr_ints,
-                          d.E, counts.p, offsets.p, xperm.p, ep.goff.p, ep.seg.p, ep.n_rows.p, ep.xloc.p, ep.origin.p,
+                          d.E, counts.p, offsets.p, hb.p, d.H, perm.p, d.top + 1, ep.goff.p, ep.seg.p, ep.n_rows.p,
+                          ep.xloc.p, ep.origin.p,
                           ep.cap, d.H, ep.max_rows, err.p, ep.p2p ? ep.wait_disp : nullptr, epoch, sm_count, s);
     const int per_expert = (world * T * d.top + T + d.E) / (d.E + 1);
     const int box = box_for(std::max(1, 2 * per_expert));
