@@ -48,7 +48,9 @@ def contexts(n, seed):
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks + throttle reasons sampled during the timed region.
+    Sampling starts before the warm-up (nvidia-smi takes a while to print its
+    first line); summary() keeps the samples read between begin() and end()."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -56,8 +58,9 @@ class ClockSampler:
 
     def __init__(self, gpu_index: int):
         self.gpu, self.rows, self.proc = gpu_index, [], None
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -70,9 +73,14 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            self.rows.append((time.perf_counter(), [x.strip() for x in line.split(",")]))
 
-    def __exit__(self, *exc):
+    def begin(self):
+        self.t0 = time.perf_counter()
+
+    def end(self):
+        self.t1 = time.perf_counter()
+        time.sleep(0.15)  # the sample covering the last timed step
         if self.proc:
             self.proc.terminate()
             try:
@@ -81,14 +89,16 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
+        lo, hi = self.t0 or 0.0, (self.t1 or float("inf")) + 0.15
+        rows = [r for t, r in self.rows if lo <= t <= hi]
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        reasons = sorted({names[i] for r in rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows)}
 
 
 def measured_peaks():
@@ -306,6 +316,7 @@ def main():
         outs, s, _ = sess.step_ragged(parents, pos, ones, tokens, flags=flags, sampled_out=sampled)
         parents, tokens, pos = outs, s.copy(), pos + 1
 
+    clocks = ClockSampler(local).start()
     for _ in range(args.warmup):
         one_step()
     # Timed region: whole-step CUDA events only (per-stage events would sit
@@ -316,13 +327,14 @@ def main():
     launches0 = sess.stats()[16]
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            one_step()
-            step_ms.append(sess.timing()[0])
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - t0
+    clocks.begin()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+        step_ms.append(sess.timing()[0])
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clocks.end()
     barrier(world)
     launches = int(sess.stats()[16] - launches0)
     _, total1, n1, _ = sess.timing()
