@@ -69,15 +69,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// Bounded wait that ignores the abort flag: at teardown after an abort it lets
-// this warp's own copies or MMAs in flight complete before the CTA exits.
-__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try_sleep(bar, parity, kWaitSleepNs))
-    if (clock64() - t0 > kWaitCycles) return false;
-  return true;
-}
-
 // Ring position: stage index and phase parity, advanced without division.
 struct Ring {
   int s = 0;
