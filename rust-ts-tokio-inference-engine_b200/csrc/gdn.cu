@@ -65,10 +65,15 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
     for (int s = 1; s < splits; ++s) v += pr[s * split_stride + col];
     return v;
   };
+  // decay / beta inputs of value head kh*R + c (threads c < R), requested
+  // with the token's conv input rather than after the q / k barrier
+  const int gh = kh * R + (c < R ? c : 0);
+  const float gdt = c < R ? dt_bias[gh] : 0.f, galog = c < R ? a_log[gh] : 0.f;
   for (int i = 0; i < d.count; ++i) {
     const int t = t0 + i;
     const float* pr = proj + size_t(t) * ld;
     const float cur = P(pr, gc);
+    const float ga = c < R ? P(pr, cd + vd + gh) : 0.f, gbeta = c < R ? P(pr, cd + vd + hv + gh) : 0.f;
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < 7; ++j)
@@ -102,11 +107,10 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
       else dst[DK + (c - DK)] = act * (rinv * rsqrtf(float(DK)));
     }
     if (c < R) {
-      const int h = kh * R + c;
-      const float av = P(pr, cd + vd + h) + dt_bias[h];
+      const float av = ga + gdt;
       const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
-      gb_out[(size_t(t) * hv + h) * 2 + 0] = expf(-expf(a_log[h]) * sp);
-      gb_out[(size_t(t) * hv + h) * 2 + 1] = sigmoidf_(P(pr, cd + vd + hv + h));
+      gb_out[(size_t(t) * hv + gh) * 2 + 0] = expf(-expf(galog) * sp);
+      gb_out[(size_t(t) * hv + gh) * 2 + 1] = sigmoidf_(gbeta);
     }
   }
   if (d.cand < 0) {
@@ -154,8 +158,17 @@ __global__ void __launch_bounds__(256)
       for (int j = 0; j < CPL; ++j) S[i][j] = 0.f;
     }
   }
+  const float gw = threadIdx.x < DV ? gnorm[threadIdx.x] : 0.f;
   for (int it = 0; it < d.count; ++it) {
     const int t = t0 + it;
+    // the gate input z of this thread's output channel, requested with the
+    // token's other inputs instead of after the row barrier
+    float z = 0.f;
+    if (threadIdx.x < DV) {
+      const float* pz = proj + size_t(t) * ld + cd + head * DV + threadIdx.x;
+      z = pz[0];
+      for (int sp = 1; sp < splits; ++sp) z += pz[sp * split_stride];
+    }
     const float* qkt = qk + ((size_t(t) * hk + kh) * 2) * DK;
     float qq[CPL], kq[CPL];
     {
@@ -210,10 +223,7 @@ __global__ void __launch_bounds__(256)
       float tot = 0.f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) tot += red[w];
-      const float* pr = proj + size_t(t) * ld + cd + head * DV + threadIdx.x;
-      float z = pr[0];
-      for (int sp = 1; sp < splits; ++sp) z += pr[sp * split_stride];
-      const float y = o * rsqrtf(tot / DV + eps) * gnorm[threadIdx.x] * siluf_(z);
+      const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
       out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
     }
     __syncthreads();

@@ -94,7 +94,25 @@ def _prefix_batch(seed, n, vocab, lo=1, hi=256):
 
 def test_cfg0_prefill_then_decode_matches_oracle(tiny):
     """8 sequences, prefixes U[1, 256], one greedy decode token."""
-    pkg, cfg, store, sess, model = tiny
+    _prefill_then_decode(*tiny)
+
+
+def test_conv3_prefill_then_decode_matches_oracle(pkg, O, cuda_ok):
+    """configs[0] with a 3-tap DeltaNet conv (the conv width is a runtime
+    parameter of the DeltaNet kernels; every preset uses 4)."""
+    O.set_routing_slack(ROUTING_SLACK)
+    cfg, ocfg = pkg.config0(), O.config0()
+    cfg.conv = ocfg.conv = 3
+    store = pkg.WeightStore().synthetic(cfg, SEED)
+    sess = pkg.DeviceSession(store, cfg, slots=64, budget_bytes=4 << 30)
+    try:
+        _prefill_then_decode(pkg, cfg, store, sess, O.Model(ocfg, SEED))
+    finally:
+        sess.close()
+        store.close()
+
+
+def _prefill_then_decode(pkg, cfg, store, sess, model):
     lens, toks = _prefix_batch(0, 8, cfg.vocab)
     sess.set_capture(True)
     outs, sampled, _ = sess.step_ragged([None] * 8, [0] * 8, lens, np.concatenate(toks),
