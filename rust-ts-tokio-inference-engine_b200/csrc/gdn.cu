@@ -10,16 +10,20 @@
 //              conv history before writing the child's, so the update is safe
 //              in place (consumed parents).
 //  gdn_update: CTA = (sequence, value head), 8 warps. The head's fp32 state
-//              S[dv][dk] stays in registers for the step (warp w owns rows
-//              [w*dv/8, (w+1)*dv/8), lane l columns [l*dk/32, ...), loaded and
-//              stored as 16-byte vectors); per token S *= g; m = S k;
-//              delta = beta (v - m); S += delta k^T; o = S q; then the gated
-//              RMSNorm y = rms(o) * w * silu(z) is written as bf16.
+//              S[dv][dk] is staged in shared memory by four bulk copies (one
+//              per two warps' rows, each completing its own mbarrier), so a
+//              CTA holds 64 KiB of state without registers and three CTAs fit
+//              per SM; warp w owns rows [w*dv/8, (w+1)*dv/8), lane l columns
+//              [l*dk/32, ...). Per token S *= g; m = S k; delta = beta (v - m);
+//              S += delta k^T; o = S q; rows go back to shared memory, or
+//              straight to the child's slot after the last token; then the
+//              gated RMSNorm y = rms(o) * w * silu(z) is written as bf16.
 // The state read + write (2 x 64 KiB per head for dk = dv = 128) is the
 // HBM traffic that bounds the layer.
 #include <atomic>
 
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace qwen {
 
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
 }
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 3)
     gdn_update_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                       int hk, int hv, const float* __restrict__ qk, const float* __restrict__ vv,
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
@@ -131,9 +135,15 @@ __global__ void __launch_bounds__(256)
   pdl_wait();
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
   constexpr int RPW = DV / 8;   // rows per warp
+  constexpr int CROWS = 2 * RPW;  // rows per bulk copy: two warps' rows
+  constexpr int CHUNKS = DV / CROWS;
+  constexpr uint32_t CBYTES = CROWS * DK * 4;
   using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
+  extern __shared__ __align__(128) float st[];  // the head's state S[dv][dk]
+  __shared__ uint64_t full[CHUNKS];
   __shared__ float os[DV];
   __shared__ float red[8];
+  __shared__ int abort_flag;
   const int seq = blockIdx.x, head = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const SeqDesc d = descs[seq];
@@ -144,21 +154,25 @@ __global__ void __launch_bounds__(256)
   const float* src = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl + size_t(head) * DV * DK
                                    : nullptr;
   float* dst = pool.state + (size_t(d.child) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
-  float S[RPW][CPL];
-#pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int r = warp * RPW + i;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
     if (src) {
-      const Vec v = *reinterpret_cast<const Vec*>(src + size_t(r) * DK + lane * CPL);
-      const float* f = reinterpret_cast<const float*>(&v);
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) S[i][j] = f[j];
-    } else {
+      for (int c = 0; c < CHUNKS; ++c) mbar_init(&full[c], 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) S[i][j] = 0.f;
+      for (int c = 0; c < CHUNKS; ++c) {
+        mbar_expect_tx(&full[c], CBYTES);
+        bulk_load(st + c * CROWS * DK, src + c * CROWS * DK, CBYTES, &full[c]);
+      }
     }
   }
+  if (!src)
+    for (int i = threadIdx.x; i < DV * DK / 4; i += blockDim.x) reinterpret_cast<float4*>(st)[i] = float4{0.f, 0.f, 0.f, 0.f};
   const float gw = threadIdx.x < DV ? gnorm[threadIdx.x] : 0.f;
+  __syncthreads();
+  bool ready = src == nullptr;  // this warp's rows are in shared memory
+  bool finite = true;
   for (int it = 0; it < d.count; ++it) {
     const int t = t0 + it;
     // the gate input z of this thread's output channel, requested with the
@@ -182,35 +196,43 @@ __global__ void __launch_bounds__(256)
     }
     const float g = gb[(size_t(t) * hv + head) * 2], beta = gb[(size_t(t) * hv + head) * 2 + 1];
     const float* vt = vv + size_t(t) * vd + head * DV;
+    if (!ready) {
+      mbar_wait(&full[warp * RPW / CROWS], 0, &abort_flag, err);
+      ready = true;
+    }
+    const bool last = it + 1 == d.count;
+    float* cs = d.cand >= 0 ? pool.state + (size_t(cand_slots[d.cand + it]) * pool.n_gdn + li) * sl +
+                                  size_t(head) * DV * DK
+                            : nullptr;
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const int r = warp * RPW + i;
+      Vec row = *reinterpret_cast<const Vec*>(st + r * DK + lane * CPL);
+      float* S = reinterpret_cast<float*>(&row);
       float mem = 0.f;
 #pragma unroll
       for (int j = 0; j < CPL; ++j) {
-        S[i][j] *= g;
-        mem += S[i][j] * kq[j];
+        S[j] *= g;
+        mem += S[j] * kq[j];
       }
       mem = warp_sum(mem);
       const float delta = (vt[r] - mem) * beta;
       float rd = 0.f;
 #pragma unroll
       for (int j = 0; j < CPL; ++j) {
-        S[i][j] += delta * kq[j];
-        rd += S[i][j] * qq[j];
+        S[j] += delta * kq[j];
+        rd += S[j] * qq[j];
       }
       rd = warp_sum(rd);
       if (lane == 0) os[r] = rd;
-    }
-    if (d.cand >= 0) {  // verify step: the state after this token is candidate `it`'s state
-      float* cs = pool.state + (size_t(cand_slots[d.cand + it]) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
+      // verify step: the state after this token is candidate `it`'s state
+      if (cs) *reinterpret_cast<Vec*>(cs + size_t(r) * DK + lane * CPL) = row;
+      if (last) {
 #pragma unroll
-      for (int i = 0; i < RPW; ++i) {
-        Vec v;
-        float* f = reinterpret_cast<float*>(&v);
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) f[j] = S[i][j];
-        *reinterpret_cast<Vec*>(cs + size_t(warp * RPW + i) * DK + lane * CPL) = v;
+        for (int j = 0; j < CPL; ++j) finite &= isfinite(S[j]);
+        if (d.cand < 0) *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = row;
+      } else {
+        *reinterpret_cast<Vec*>(st + r * DK + lane * CPL) = row;
       }
     }
     __syncthreads();
@@ -226,22 +248,30 @@ __global__ void __launch_bounds__(256)
       const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
       out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
     }
-    __syncthreads();
   }
-  bool finite = true;
+  if (d.count == 0) {  // no token: the child carries the parent's state
+    if (!ready) mbar_wait(&full[warp * RPW / CROWS], 0, &abort_flag, err);
 #pragma unroll
-  for (int i = 0; i < RPW; ++i) {
-    const int r = warp * RPW + i;
-    Vec v;
-    float* f = reinterpret_cast<float*>(&v);
+    for (int i = 0; i < RPW; ++i) {
+      const int r = warp * RPW + i;
+      const Vec row = *reinterpret_cast<const Vec*>(st + r * DK + lane * CPL);
+      const float* S = reinterpret_cast<const float*>(&row);
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      f[j] = S[i][j];
-      finite &= isfinite(S[i][j]);
+      for (int j = 0; j < CPL; ++j) finite &= isfinite(S[j]);
+      if (d.cand < 0) *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = row;
     }
-    if (d.cand < 0) *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = v;
   }
   if (!finite) atomicOr(err, kErrNonFinite);
+  // after a timed-out wait, copies may still be landing: wait for them (bounded) before exiting
+  __syncthreads();
+  if (threadIdx.x == 0 && src && abort_flag) {
+#pragma unroll 1
+    for (int c = 0; c < CHUNKS; ++c) {
+      const long long c0 = clock64();
+      while (!mbar_try_sleep(&full[c], 0, kWaitSleepNs) && clock64() - c0 < kWaitCycles) {
+      }
+    }
+  }
 }
 
 }  // namespace
@@ -258,7 +288,17 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
     launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
         proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
         ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf, cand_slots);                                                \
-    launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, 0, s, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
+    static const bool smem_set_##DK_##_##R_ = [] {                                                               \
+      const int bytes = DV_ * DK_ * 4;                                                                           \
+      QWEN_CUDA(cudaFuncSetAttribute(gdn_update_kernel<DK_, DV_>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                     bytes));                                                                    \
+      QWEN_CUDA(cudaFuncSetAttribute(gdn_update_kernel<DK_, DV_>,                                                \
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,                             \
+                                     int(cudaSharedmemCarveoutMaxShared)));                                     \
+      return true;                                                                                               \
+    }();                                                                                                         \
+    (void)smem_set_##DK_##_##R_;                                                                                 \
+    launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, size_t(DV_) * DK_ * 4, s, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
                                                                 qk_buf, v_buf, gb_buf, proj, ld_proj, splits,    \
                                                                 split_stride, d.cd, ly.gnorm, d.eps, out, err,   \
                                                                 cand_slots);                                     \
