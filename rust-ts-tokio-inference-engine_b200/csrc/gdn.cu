@@ -31,8 +31,23 @@ extern std::atomic<uint64_t> g_kernel_launches;
 
 namespace {
 
+constexpr int kGdnMaxSplits = 8;
+
+// Sum of the split-K partials at column `col` of one token's projection row,
+// in split order; the loads are independent and issued together.
+__device__ __forceinline__ float split_sum(const float* pr, int col, int splits, size_t split_stride) {
+  float part[kGdnMaxSplits];
+#pragma unroll
+  for (int s = 0; s < kGdnMaxSplits; ++s) part[s] = s < splits ? pr[s * split_stride + col] : 0.f;
+  float v = part[0];
+#pragma unroll
+  for (int s = 1; s < kGdnMaxSplits; ++s)
+    if (s < splits) v += part[s];
+  return v;
+}
+
 template <int DK, int DV, int R>
-__global__ void __launch_bounds__(2 * DK + R * DV)
+__global__ void __launch_bounds__(2 * DK + R * DV, 2)
     gdn_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
                     const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                     int hk, int hv, int conv, const float* __restrict__ conv_w, const float* __restrict__ a_log,
@@ -64,11 +79,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV)
 #pragma unroll
   for (int j = 0; j < 8; ++j)
     if (j == conv - 1) cw_last = cw[j];
-  auto P = [&](const float* pr, int col) {
-    float v = pr[col];
-    for (int s = 1; s < splits; ++s) v += pr[s * split_stride + col];
-    return v;
-  };
+  auto P = [&](const float* pr, int col) { return split_sum(pr, col, splits, split_stride); };
   // decay / beta inputs of value head kh*R + c (threads c < R), requested
   // with the token's conv input rather than after the q / k barrier
   const int gh = kh * R + (c < R ? c : 0);
@@ -177,12 +188,9 @@ __global__ void __launch_bounds__(256, 3)
     const int t = t0 + it;
     // the gate input z of this thread's output channel, requested with the
     // token's other inputs instead of after the row barrier
-    float z = 0.f;
-    if (threadIdx.x < DV) {
-      const float* pz = proj + size_t(t) * ld + cd + head * DV + threadIdx.x;
-      z = pz[0];
-      for (int sp = 1; sp < splits; ++sp) z += pz[sp * split_stride];
-    }
+    const float z = threadIdx.x < DV ? split_sum(proj + size_t(t) * ld, cd + head * DV + threadIdx.x, splits,
+                                                 split_stride)
+                                     : 0.f;
     const float* qkt = qk + ((size_t(t) * hk + kh) * 2) * DK;
     float qq[CPL], kq[CPL];
     {
@@ -282,6 +290,7 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
                 const int32_t* cand_slots, cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
+  if (splits > kGdnMaxSplits) throw std::invalid_argument("DeltaNet input projection split more than 8 ways");
   bool done = false;
 #define QWEN_GDN(DK_, DV_, R_)                                                                                    \
   if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \

@@ -376,6 +376,9 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   __shared__ uint64_t wbest[2][8];
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* lr = logits + size_t(t) * ld;
+  // the shared expert's gate logit (column E): lane sp of warp 0 requests
+  // split sp's partial together with the experts' logits
+  const float sh_part = (threadIdx.x < kSplits && threadIdx.x < splits) ? lr[threadIdx.x * split_stride + E] : 0.f;
   float v[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
@@ -389,6 +392,16 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     for (int sp = 1; sp < kSplits; ++sp)
       if (sp < splits) acc += part[sp];
     v[k] = acc;
+  }
+  __shared__ float s_shared_logit;
+  if (warp == 0) {  // summed in split order
+    float sl = __shfl_sync(0xffffffffu, sh_part, 0);
+#pragma unroll
+    for (int sp = 1; sp < kSplits; ++sp) {
+      const float p = __shfl_sync(0xffffffffu, sh_part, sp);
+      if (sp < splits) sl += p;
+    }
+    if (lane == 0) s_shared_logit = sl;
   }
   if (logits_out) {  // diagnostic capture of the summed router logits
     float* lo = logits_out + size_t(t) * (E + 1);
@@ -431,8 +444,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     if (threadIdx.x == 0) { out_ids[r] = e; out_w[r] = w; }
   }
   if (threadIdx.x == 0) {
-    float shared_logit = lr[E];
-    for (int sp = 1; sp < splits; ++sp) shared_logit += lr[sp * split_stride + E];
+    const float shared_logit = s_shared_logit;
     if (logits_out) logits_out[size_t(t) * (E + 1) + E] = shared_logit;
     for (int r = 0; r < top; ++r) out_w[r] = out_w[r] / denom;
     out_ids[top] = E;
@@ -515,16 +527,16 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __rest
 
 // x[t] += sum_j w[t][j] * y[inv[t*slots+j]] (fixed slot order, deterministic);
 // then optional hb[t] = bf16(rms(x[t]) * norm_w).
-__global__ void moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
+__global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
                                    const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
                                    int slots, const float* __restrict__ norm_w, float eps,
                                    __nv_bfloat16* __restrict__ hb) {
   pdl_trigger();
   pdl_wait();
   // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
-  // Thread i owns column pairs i, i + blockDim, ...; each slot's loads are
-  // issued in groups of kBatch before the ordered adds.
-  constexpr int kPer = 4, kBatch = 8;
+  // Thread i owns column pairs i, i + blockDim, ...; the residual row and up
+  // to kBatch slot rows are requested together before the ordered adds.
+  constexpr int kPer = 4, kBatch = 16;
   __shared__ float red[32];
   __shared__ float sw[64];
   __shared__ int32_t srow[64];
@@ -533,9 +545,15 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
     sw[threadIdx.x] = weights[size_t(t) * slots + threadIdx.x];
     srow[threadIdx.x] = inv[size_t(t) * slots + threadIdx.x];
   }
-  __syncthreads();
   const int H2 = H >> 1;
   float2* xr = reinterpret_cast<float2*>(x + size_t(t) * H);
+  float2 xo[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    xo[k] = c < H2 ? xr[c] : make_float2(0.f, 0.f);
+  }
+  __syncthreads();
   float2 v[kPer];
   float ss = 0.f;
 #pragma unroll
@@ -555,9 +573,8 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
           v[k].y += sw[j0 + b] * yv[b].y;
         }
     }
-    const float2 xo = xr[c];
-    v[k].x += xo.x;
-    v[k].y += xo.y;
+    v[k].x += xo[k].x;
+    v[k].y += xo[k].y;
     xr[c] = v[k];
     ss += v[k].x * v[k].x + v[k].y * v[k].y;
   }
