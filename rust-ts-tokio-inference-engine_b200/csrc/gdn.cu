@@ -282,11 +282,213 @@ __global__ void __launch_bounds__(256, 3)
   }
 }
 
+
+// Decode steps (every sequence feeds one token): the update streamed through a
+// ring of shared-memory row chunks by persistent CTAs. The rows of a head's
+// state are independent (the token's k, v, g, beta update a row from that row
+// alone; only the gated RMSNorm spans rows), so a row is read once, updated,
+// written straight to the child's slot, and its chunk slot refilled at once
+// with the next rows, whichever head they belong to: HBM sees one continuous
+// read stream per CTA instead of a load / compute / store wave per head.
+//   warp 8 (producer): per item (sequence, value head) stages the token inputs
+//     (q, k, v, the gate input z summed over the split-K partials, g, beta, the
+//     output row and the destination) in one of two shared buffers, then
+//     issues one bulk copy per 32-row chunk into the NS-slot ring;
+//   warps 0-7 (consumers): 4 rows of every chunk each, then the gated RMSNorm
+//     of the item over named barrier 1.
+// Every wait is bounded; after a timeout (kErrTimeout) all warps run out their
+// loops with no memory traffic and the same barrier count, and the producer's
+// outstanding copies are waited for (bounded) before the CTA exits.
+template <int DK, int DV>
+__global__ void __launch_bounds__(288, 3)
+    gdn_stream_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
+                      int hk, int hv, int n_items, const float* __restrict__ qk, const float* __restrict__ vv,
+                      const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
+                      size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
+                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int CPL = DK / 32;   // state columns per lane
+  constexpr int CR = 32;         // rows per chunk: 4 per consumer warp
+  constexpr int CPI = DV / CR;   // chunks per item
+  constexpr int NS = 4;          // ring slots
+  constexpr uint32_t CBYTES = CR * DK * 4;
+  using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
+  struct __align__(16) Stage {
+    float qk[2 * DK];
+    float v[DV];
+    float z[DV];
+    float* dst;
+    float g, beta;
+    int t;
+  };
+  extern __shared__ __align__(128) float ring[];  // [NS][CR][DK]
+  __shared__ Stage stg[2];
+  __shared__ uint64_t full[NS], empty[NS], in_full[2], in_empty[2];
+  __shared__ float os[DV];
+  __shared__ float red[8];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&in_full[i], 32);
+      mbar_init(&in_empty[i], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int vd = hv * DV;
+  const size_t sl = size_t(hv) * DV * DK;
+  int issued = 0;  // producer: chunks issued
+  if (warp == 8) {
+    int n = 0, j = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++j) {
+      const int seq = i / hv, head = i % hv, kh = head / (hv / hk);
+      const SeqDesc d = descs[seq];
+      const int t = cu_seqlens[seq];
+      const int b = j & 1;
+      if (!mbar_wait(&in_empty[b], ((j >> 1) & 1) ^ 1u, &abort_flag, err)) break;
+      Stage& S = stg[b];
+      const float* qkt = qk + ((size_t(t) * hk + kh) * 2) * DK;
+      const float* vt = vv + size_t(t) * vd + size_t(head) * DV;
+#pragma unroll
+      for (int c = lane; c < 2 * DK; c += 32) S.qk[c] = qkt[c];
+#pragma unroll
+      for (int c = lane; c < DV; c += 32) {
+        S.v[c] = vt[c];
+        S.z[c] = split_sum(proj + size_t(t) * ld, cd + head * DV + c, splits, split_stride);
+      }
+      if (lane == 0) {
+        S.g = gb[(size_t(t) * hv + head) * 2];
+        S.beta = gb[(size_t(t) * hv + head) * 2 + 1];
+        S.t = t;
+        const int slot = d.cand >= 0 ? cand_slots[d.cand] : d.child;  // one token: its state is the result
+        S.dst = pool.state + (size_t(slot) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
+      }
+      mbar_arrive(&in_full[b]);
+      const float* src = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl +
+                                             size_t(head) * DV * DK
+                                       : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < CPI; ++c, ++n) {
+        const int s = n % NS;
+        if (!mbar_wait(&empty[s], ((n / NS) & 1) ^ 1u, &abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        float* slot = ring + s * CR * DK;
+        if (src) {
+          if (lane == 0) {
+            mbar_expect_tx(&full[s], CBYTES);
+            bulk_load(slot, src + size_t(c) * CR * DK, CBYTES, &full[s]);
+          }
+          issued = n + 1;
+        } else {  // no parent: zero state
+          for (int k = lane; k < CR * DK / 4; k += 32) reinterpret_cast<float4*>(slot)[k] = float4{0.f, 0.f, 0.f, 0.f};
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[s]);
+        }
+      }
+    }
+  } else {
+    const float gw = threadIdx.x < DV ? gnorm[threadIdx.x] : 0.f;
+    bool finite = true;
+    int n = 0, j = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++j) {
+      const int head = i % hv;
+      const int b = j & 1;
+      bool ok = mbar_wait(&in_full[b], (j >> 1) & 1u, &abort_flag, err);
+      const Stage& S = stg[b];
+      float qq[CPL], kq[CPL];
+      {
+        const Vec qv = *reinterpret_cast<const Vec*>(S.qk + lane * CPL);
+        const Vec kv = *reinterpret_cast<const Vec*>(S.qk + DK + lane * CPL);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          qq[c] = reinterpret_cast<const float*>(&qv)[c];
+          kq[c] = reinterpret_cast<const float*>(&kv)[c];
+        }
+      }
+      const float g = S.g, beta = S.beta;
+      float* dst = S.dst;
+#pragma unroll 1
+      for (int c = 0; c < CPI; ++c, ++n) {
+        const int s = n % NS;
+        ok = mbar_wait(&full[s], (n / NS) & 1u, &abort_flag, err) && ok;
+        const float* chunk = ring + s * CR * DK;
+#pragma unroll
+        for (int k = 0; k < CR / 8; ++k) {
+          const int rl = warp * (CR / 8) + k, r = c * CR + rl;
+          Vec row = *reinterpret_cast<const Vec*>(chunk + rl * DK + lane * CPL);
+          float* St = reinterpret_cast<float*>(&row);
+          float mem = 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            St[q] *= g;
+            mem += St[q] * kq[q];
+          }
+          mem = warp_sum(mem);
+          const float delta = (S.v[r] - mem) * beta;
+          float rd = 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            St[q] += delta * kq[q];
+            rd += St[q] * qq[q];
+          }
+          rd = warp_sum(rd);
+          if (lane == 0) os[r] = rd;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) finite &= isfinite(St[q]);
+          if (ok) *reinterpret_cast<Vec*>(dst + size_t(r) * DK + lane * CPL) = row;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // gated RMSNorm over dv (native/qwen_model.inc:203-204)
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float o = threadIdx.x < DV ? os[threadIdx.x] : 0.f;
+      const float z = threadIdx.x < DV ? S.z[threadIdx.x] : 0.f;
+      const int t = S.t;
+      const float ss = warp_sum(o * o);
+      if (lane == 0) red[warp] = ss;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x < DV && ok) {
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
+        out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&in_empty[b]);
+    }
+    if (!finite) atomicOr(err, kErrNonFinite);
+  }
+  __syncthreads();
+  // after a timeout, copies may still be landing in the ring: wait for them (bounded)
+  if (warp == 8 && lane == 0 && abort_flag) {
+#pragma unroll 1
+    for (int n = issued > NS ? issued - NS : 0; n < issued; ++n) {
+      const long long c0 = clock64();
+      while (!mbar_try_sleep(&full[n % NS], (n / NS) & 1u, kWaitSleepNs) && clock64() - c0 < kWaitCycles) {
+      }
+    }
+  }
+}
+
 }  // namespace
 
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
-                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool, int gdn_index,
-                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int /*sm_count*/,
+                const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool, int gdn_index,
+                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int sm_count,
                 const int32_t* cand_slots, cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
@@ -307,10 +509,25 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
       return true;                                                                                               \
     }();                                                                                                         \
     (void)smem_set_##DK_##_##R_;                                                                                 \
-    launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, size_t(DV_) * DK_ * 4, s, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv,  \
-                                                                qk_buf, v_buf, gb_buf, proj, ld_proj, splits,    \
-                                                                split_stride, d.cd, ly.gnorm, d.eps, out, err,   \
-                                                                cand_slots);                                     \
+    if (T == n_seq) { /* one token per sequence: streamed update */                                             \
+      static const bool ring_set_##DK_##_##R_ = [] {                                                             \
+        QWEN_CUDA(cudaFuncSetAttribute(gdn_stream_kernel<DK_, DV_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                       4 * 32 * DK_ * 4));                                                       \
+        QWEN_CUDA(cudaFuncSetAttribute(gdn_stream_kernel<DK_, DV_>,                                              \
+                                       cudaFuncAttributePreferredSharedMemoryCarveout,                           \
+                                       int(cudaSharedmemCarveoutMaxShared)));                                   \
+        return true;                                                                                             \
+      }();                                                                                                       \
+      (void)ring_set_##DK_##_##R_;                                                                               \
+      const int items = n_seq * d.hv;                                                                            \
+      launch_pdl(gdn_stream_kernel<DK_, DV_>, std::min(items, 3 * sm_count), 288, size_t(4) * 32 * DK_ * 4, s,   \
+                 descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, items, qk_buf, v_buf, gb_buf, proj, ld_proj,     \
+                 splits, split_stride, d.cd, ly.gnorm, d.eps, out, err, cand_slots);                             \
+    } else {                                                                                                     \
+      launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, size_t(DV_) * DK_ * 4, s, descs,           \
+                 cu_seqlens, pool, gdn_index, d.hk, d.hv, qk_buf, v_buf, gb_buf, proj, ld_proj, splits,           \
+                 split_stride, d.cd, ly.gnorm, d.eps, out, err, cand_slots);                                     \
+    }                                                                                                            \
     done = true;                                                                                                 \
   }
   QWEN_GDN(128, 128, 2)

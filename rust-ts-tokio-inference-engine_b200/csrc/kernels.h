@@ -91,7 +91,7 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
                           cudaStream_t s);
 void launch_qgemm(const GemmArgs& a, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
-                size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, GdnPool pool,
+                size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool,
                 int gdn_index, __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
                 int sm_count, const int32_t* cand_slots, cudaStream_t s);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,

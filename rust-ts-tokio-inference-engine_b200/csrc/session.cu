@@ -827,7 +827,7 @@ struct Session {
       const int k_out = ly.mixer == 0 ? d.vd : d.Hq * d.D;
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
-        launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, gdn, ly.type_index,
+        launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, T, gdn, ly.type_index,
                    hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, cand_dev.p, s);
         stage(5);  // RecurrentOutput
       } else {
