@@ -34,15 +34,17 @@ namespace {
 constexpr int kGdnMaxSplits = 8;
 
 // Sum of the split-K partials at column `col` of one token's projection row,
-// in split order; the loads are independent and issued together.
+// in split order; the loads are issued in independent batches of four.
 __device__ __forceinline__ float split_sum(const float* pr, int col, int splits, size_t split_stride) {
-  float part[kGdnMaxSplits];
+  float v = pr[col];
+  for (int s0 = 1; s0 < splits; s0 += 4) {
+    float part[4];
 #pragma unroll
-  for (int s = 0; s < kGdnMaxSplits; ++s) part[s] = s < splits ? pr[s * split_stride + col] : 0.f;
-  float v = part[0];
+    for (int k = 0; k < 4; ++k) part[k] = s0 + k < splits ? pr[(s0 + k) * split_stride + col] : 0.f;
 #pragma unroll
-  for (int s = 1; s < kGdnMaxSplits; ++s)
-    if (s < splits) v += part[s];
+    for (int k = 0; k < 4; ++k)
+      if (s0 + k < splits) v += part[k];
+  }
   return v;
 }
 
@@ -484,6 +486,279 @@ __global__ void __launch_bounds__(288, 3)
   }
 }
 
+
+// Decode steps with the 4-tap conv: gdn_prep folded into the streamed update.
+// Item = (sequence, key head): the conv of its q / k channels and of its R
+// value heads' v channels, then the R heads' state rows. Persistent CTAs of
+// 13 warps, two per SM:
+//   warp 8 (issuer): one bulk copy per 32-row chunk of the item's R heads
+//     (contiguous in the slot) into an NS-slot ring, running ahead of the
+//     consumers by the ring's depth, across items;
+//   warps 9-12 (stagers, 128 threads): for the next item, the causal conv +
+//     SiLU of its 2*DK + R*DV channels with gdn_prep's arithmetic (the new
+//     history written to the destination slot), q / k RMS scaling from the same
+//     per-warp partials in the same order, g, beta and the split-summed gate
+//     input z, into one of two stage buffers;
+//   warps 0-7 (consumers): 4 rows of every chunk, then the R gated RMSNorms.
+// The item's history and state are read and written by this CTA only, so a
+// consumed parent is updated in place. Timeouts behave as in gdn_stream_kernel.
+template <int DK, int DV, int R, int CONV>
+__global__ void __launch_bounds__(416, 2)
+    gdn_decode_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
+                      const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
+                      int hk, int hv, int n_items, const float* __restrict__ conv_w, const float* __restrict__ a_log,
+                      const float* __restrict__ dt_bias, const float* __restrict__ gnorm, float eps,
+                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int CPL = DK / 32;      // state columns per lane
+  constexpr int CR = 32;            // rows per chunk: 4 per consumer warp
+  constexpr int HC = DV / CR;       // chunks per value head
+  constexpr int IC = R * HC;        // chunks per item
+  constexpr int NS = 6;             // ring slots
+  constexpr uint32_t CBYTES = CR * DK * 4;
+  constexpr int NCH = 2 * DK + R * DV;  // conv channels per item: q | k | v
+  constexpr int NP = 128;               // stager threads
+  constexpr int NM = (NCH + NP - 1) / NP;
+  constexpr int QW = DK / 32;
+  using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
+  struct __align__(16) Stage {
+    float qk[2 * DK];  // normalised and scaled q | k
+    float v[R * DV];
+    float z[R * DV];
+    float g[R], beta[R];
+    float* dst;        // the item's first value head in the destination slot
+    int t;
+  };
+  extern __shared__ __align__(128) float ring[];  // [NS][CR][DK]
+  __shared__ Stage stg[2];
+  __shared__ uint64_t full[NS], empty[NS], in_full[2], in_empty[2];
+  __shared__ float os[R * DV];
+  __shared__ float red[8];
+  __shared__ float pqk[2][2 * QW];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&in_full[i], NP);
+      mbar_init(&in_empty[i], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int kd = hk * DK, vd = hv * DV, cd = 2 * kd + vd;
+  const size_t sl = size_t(hv) * DV * DK;
+  const size_t cl = size_t(CONV - 1) * cd;
+  int issued = 0;  // issuer: chunks issued
+  if (warp == 8) {
+    int n = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+      const int seq = i / hk, kh = i % hk;
+      const SeqDesc d = descs[seq];
+      const float* src = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl +
+                                             size_t(kh) * R * DV * DK
+                                       : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < IC; ++c, ++n) {
+        const int s = n % NS;
+        if (!mbar_wait(&empty[s], ((n / NS) & 1) ^ 1u, &abort_flag, err)) {
+          ok = false;
+          break;
+        }
+        float* slot = ring + s * CR * DK;
+        if (src) {
+          if (lane == 0) {
+            mbar_expect_tx(&full[s], CBYTES);
+            bulk_load(slot, src + size_t(c) * CR * DK, CBYTES, &full[s]);
+          }
+          issued = n + 1;
+        } else {  // no parent: zero state
+          for (int k = lane; k < CR * DK / 4; k += 32) reinterpret_cast<float4*>(slot)[k] = float4{0.f, 0.f, 0.f, 0.f};
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[s]);
+        }
+      }
+    }
+  } else if (warp > 8) {
+    const int p = threadIdx.x - 9 * 32, pw = p >> 5;
+    int j = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++j) {
+      const int seq = i / hk, kh = i % hk, b = j & 1;
+      const bool ok = mbar_wait(&in_empty[b], ((j >> 1) & 1) ^ 1u, &abort_flag, err);
+      const SeqDesc d = descs[seq];
+      const int t = cu_seqlens[seq];
+      const float* pr = proj + size_t(t) * ld;
+      const float* src_conv = d.parent >= 0 ? pool.conv + (size_t(d.parent) * pool.n_gdn + li) * cl : nullptr;
+      const int wslot = d.cand >= 0 ? cand_slots[d.cand] : d.child;  // one token: its state is the result
+      float* dst_conv = pool.conv + (size_t(wslot) * pool.n_gdn + li) * cl;
+      Stage& S = stg[b];
+      // every input of the thread's channels is requested before the first
+      // history store (the stores could alias later loads)
+      int gc[NM];
+      float cw[NM][CONV], taps[NM][CONV - 1], cur[NM];  // taps[m][0] oldest
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        const int ch = p + NP * m;
+        gc[m] = ch < DK ? kh * DK + ch
+                        : (ch < 2 * DK ? kd + kh * DK + (ch - DK) : 2 * kd + kh * R * DV + (ch - 2 * DK));
+        const bool v = ch < NCH;
+#pragma unroll
+        for (int q = 0; q < CONV; ++q) cw[m][q] = v ? conv_w[size_t(gc[m]) * CONV + q] : 0.f;
+#pragma unroll
+        for (int q = 0; q < CONV - 1; ++q) taps[m][q] = v && src_conv ? src_conv[size_t(q) * cd + gc[m]] : 0.f;
+        cur[m] = v ? split_sum(pr, gc[m], splits, split_stride) : 0.f;
+      }
+      float act[NM];
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < CONV - 1; ++q) acc += taps[m][q] * cw[m][q];
+        acc += cur[m] * cw[m][CONV - 1];
+        if (ok && p + NP * m < NCH) {
+#pragma unroll
+          for (int q = 0; q < CONV - 1; ++q)
+            dst_conv[size_t(q) * cd + gc[m]] = q + 1 < CONV - 1 ? taps[m][q + 1] : cur[m];
+        }
+        act[m] = siluf_(acc);
+      }
+      // q / k sums of squares: one partial per 32 channels, as gdn_prep's warps
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        const int ch0 = NP * m + pw * 32;  // warp-uniform
+        if (ch0 < 2 * DK) {
+          const float ss = warp_sum(act[m] * act[m]);
+          if (lane == 0) pqk[b][ch0 / 32] = ss;
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        const int ch = p + NP * m;
+        if (ch >= 2 * DK && ch < NCH) S.v[ch - 2 * DK] = act[m];
+      }
+      for (int c = p; c < R * DV; c += NP) S.z[c] = split_sum(pr, cd + kh * R * DV + c, splits, split_stride);
+      if (p < R) {
+        const int h = kh * R + p;
+        const float av = split_sum(pr, cd + vd + h, splits, split_stride) + dt_bias[h];
+        const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
+        S.g[p] = expf(-expf(a_log[h]) * sp);
+        S.beta[p] = sigmoidf_(split_sum(pr, cd + vd + hv + h, splits, split_stride));
+      }
+      if (p == 0) {
+        S.t = t;
+        S.dst = pool.state + (size_t(wslot) * pool.n_gdn + li) * sl + size_t(kh) * R * DV * DK;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(NP) : "memory");
+      float tq = 0.f, tk = 0.f;
+#pragma unroll
+      for (int w = 0; w < QW; ++w) {
+        tq += pqk[b][w];
+        tk += pqk[b][QW + w];
+      }
+      const float rq = rsqrtf(tq / DK + 1e-6f), rk = rsqrtf(tk / DK + 1e-6f);
+#pragma unroll
+      for (int m = 0; m < NM; ++m) {
+        const int ch = p + NP * m;
+        if (ch < DK) S.qk[ch] = act[m] * (rq / DK);
+        else if (ch < 2 * DK) S.qk[ch] = act[m] * (rk * rsqrtf(float(DK)));
+      }
+      mbar_arrive(&in_full[b]);
+    }
+  } else {
+    const int tid = threadIdx.x;
+    const float gw = tid < R * DV ? gnorm[tid % DV] : 0.f;
+    bool finite = true;
+    int n = 0, j = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++j) {
+      const int kh = i % hk, b = j & 1;
+      bool ok = mbar_wait(&in_full[b], (j >> 1) & 1u, &abort_flag, err);
+      const Stage& S = stg[b];
+      float qq[CPL], kq[CPL];
+      {
+        const Vec qv = *reinterpret_cast<const Vec*>(S.qk + lane * CPL);
+        const Vec kv = *reinterpret_cast<const Vec*>(S.qk + DK + lane * CPL);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          qq[c] = reinterpret_cast<const float*>(&qv)[c];
+          kq[c] = reinterpret_cast<const float*>(&kv)[c];
+        }
+      }
+      float* dst = S.dst;
+#pragma unroll 1
+      for (int c = 0; c < IC; ++c, ++n) {
+        const int s = n % NS, hh = c / HC;
+        ok = mbar_wait(&full[s], (n / NS) & 1u, &abort_flag, err) && ok;
+        const float g = S.g[hh], beta = S.beta[hh];
+        const float* chunk = ring + s * CR * DK;
+#pragma unroll
+        for (int k = 0; k < CR / 8; ++k) {
+          const int rl = warp * (CR / 8) + k, r = (c % HC) * CR + rl;
+          Vec row = *reinterpret_cast<const Vec*>(chunk + rl * DK + lane * CPL);
+          float* St = reinterpret_cast<float*>(&row);
+          float mem = 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            St[q] *= g;
+            mem += St[q] * kq[q];
+          }
+          mem = warp_sum(mem);
+          const float delta = (S.v[hh * DV + r] - mem) * beta;
+          float rd = 0.f;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            St[q] += delta * kq[q];
+            rd += St[q] * qq[q];
+          }
+          rd = warp_sum(rd);
+          if (lane == 0) os[hh * DV + r] = rd;
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) finite &= isfinite(St[q]);
+          if (ok) *reinterpret_cast<Vec*>(dst + (size_t(hh) * DV + r) * DK + lane * CPL) = row;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // the R gated RMSNorms over dv (native/qwen_model.inc:203-204)
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float o = tid < R * DV ? os[tid] : 0.f;
+      const float z = tid < R * DV ? S.z[tid] : 0.f;
+      const int t = S.t;
+      const float ss = warp_sum(o * o);
+      if (lane == 0) red[warp] = ss;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (tid < R * DV && ok) {
+        const int hh = tid / DV;
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < DV / 32; ++w) tot += red[hh * (DV / 32) + w];
+        const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
+        out[size_t(t) * vd + size_t(kh) * R * DV + tid] = __float2bfloat16_rn(y);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&in_empty[b]);
+    }
+    if (!finite) atomicOr(err, kErrNonFinite);
+  }
+  __syncthreads();
+  // after a timeout, copies may still be landing in the ring: wait for them (bounded)
+  if (warp == 8 && lane == 0 && abort_flag) {
+#pragma unroll 1
+    for (int n = issued > NS ? issued - NS : 0; n < issued; ++n) {
+      const long long c0 = clock64();
+      while (!mbar_try_sleep(&full[n % NS], (n / NS) & 1u, kWaitSleepNs) && clock64() - c0 < kWaitCycles) {
+      }
+    }
+  }
+}
+
 }  // namespace
 
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
@@ -494,6 +769,32 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
   if (splits > kGdnMaxSplits) throw std::invalid_argument("DeltaNet input projection split more than 8 ways");
   bool done = false;
+#define QWEN_GDN_DECODE(DK_, DV_, R_)                                                                             \
+  if (!done && T == n_seq && d.conv == 4 && d.dk == DK_ && d.dv == DV_ && R == R_) {                             \
+    constexpr int ring_bytes = 6 * 32 * DK_ * 4;                                                                 \
+    static const bool set_##DK_##_##R_ = [] {                                                                    \
+      QWEN_CUDA(cudaFuncSetAttribute(gdn_decode_kernel<DK_, DV_, R_, 4>,                                         \
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, ring_bytes));                  \
+      QWEN_CUDA(cudaFuncSetAttribute(gdn_decode_kernel<DK_, DV_, R_, 4>,                                         \
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,                             \
+                                     int(cudaSharedmemCarveoutMaxShared)));                                     \
+      return true;                                                                                               \
+    }();                                                                                                         \
+    (void)set_##DK_##_##R_;                                                                                      \
+    const int items = n_seq * d.hk;                                                                              \
+    const int per_cta = (items + 2 * sm_count - 1) / (2 * sm_count);                                             \
+    launch_pdl(gdn_decode_kernel<DK_, DV_, R_, 4>, (items + per_cta - 1) / per_cta, 416, size_t(ring_bytes), s,   \
+               proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, items,       \
+               ly.conv_w, ly.a_log, ly.dt_bias, ly.gnorm, d.eps, out, err, cand_slots);                           \
+    QWEN_CUDA(cudaGetLastError());                                                                               \
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);                                                   \
+    return;                                                                                                      \
+  }
+  QWEN_GDN_DECODE(128, 128, 2)
+  QWEN_GDN_DECODE(64, 64, 2)
+  QWEN_GDN_DECODE(128, 128, 1)
+  QWEN_GDN_DECODE(64, 64, 1)
+#undef QWEN_GDN_DECODE
 #define QWEN_GDN(DK_, DV_, R_)                                                                                    \
   if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \
     launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
