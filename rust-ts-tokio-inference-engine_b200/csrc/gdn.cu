@@ -489,21 +489,29 @@ __global__ void __launch_bounds__(288, 3)
 
 // Decode steps with the 4-tap conv: gdn_prep folded into the streamed update.
 // Item = (sequence, key head): the conv of its q / k channels and of its R
-// value heads' v channels, then the R heads' state rows. Persistent CTAs of
-// 13 warps, two per SM:
-//   warp 8 (issuer): one bulk copy per 32-row chunk of the item's R heads
-//     (contiguous in the slot) into an NS-slot ring, running ahead of the
-//     consumers by the ring's depth, across items;
-//   warps 9-12 (stagers, 128 threads): for the next item, the causal conv +
-//     SiLU of its 2*DK + R*DV channels with gdn_prep's arithmetic (the new
-//     history written to the destination slot), q / k RMS scaling from the same
-//     per-warp partials in the same order, g, beta and the split-summed gate
-//     input z, into one of two stage buffers;
-//   warps 0-7 (consumers): 4 rows of every chunk, then the R gated RMSNorms.
+// value heads' v channels, then the R heads' state rows. Persistent CTAs
+// (kDecCtasPerSm per SM) with three warp roles:
+//   consumers (the first kDecConsumerWarps warps): their share of the rows of
+//     every chunk, then the R gated RMSNorms over named barrier 1;
+//   issuer (the next warp): one bulk copy per 32-row chunk of the item's R
+//     heads (contiguous in the slot) into a kDecRing-slot ring, running ahead
+//     of the consumers by the ring's depth, across items;
+//   stagers (the last kDecStagerWarps warps): for the next item, the causal
+//     conv + SiLU of its 2*DK + R*DV channels with gdn_prep's arithmetic (the
+//     new history written to the destination slot), q / k RMS scaling from the
+//     same per-32-channel partials in the same order, g, beta and the
+//     split-summed gate input z, into one of two stage buffers.
 // The item's history and state are read and written by this CTA only, so a
 // consumed parent is updated in place. Timeouts behave as in gdn_stream_kernel.
+// Warp roles and ring depth of gdn_decode_kernel.
+constexpr int kDecConsumerWarps = 8;
+constexpr int kDecStagerWarps = 4;
+constexpr int kDecRing = 6;          // 32-row chunks in the ring
+constexpr int kDecCtasPerSm = 2;
+constexpr int kDecThreads = (kDecConsumerWarps + 1 + kDecStagerWarps) * 32;
+
 template <int DK, int DV, int R, int CONV>
-__global__ void __launch_bounds__(416, 2)
+__global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
     gdn_decode_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
                       const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                       int hk, int hv, int n_items, const float* __restrict__ conv_w, const float* __restrict__ a_log,
@@ -512,13 +520,15 @@ __global__ void __launch_bounds__(416, 2)
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;      // state columns per lane
-  constexpr int CR = 32;            // rows per chunk: 4 per consumer warp
+  constexpr int NCW = kDecConsumerWarps, IW = NCW, SW0 = NCW + 1;  // consumer / issuer / first stager warp
+  constexpr int CR = 32;            // rows per chunk
+  constexpr int RPC = CR / NCW;     // rows of a chunk per consumer warp
   constexpr int HC = DV / CR;       // chunks per value head
   constexpr int IC = R * HC;        // chunks per item
-  constexpr int NS = 6;             // ring slots
+  constexpr int NS = kDecRing;      // ring slots
   constexpr uint32_t CBYTES = CR * DK * 4;
   constexpr int NCH = 2 * DK + R * DV;  // conv channels per item: q | k | v
-  constexpr int NP = 128;               // stager threads
+  constexpr int NP = kDecStagerWarps * 32;  // stager threads
   constexpr int NM = (NCH + NP - 1) / NP;
   constexpr int QW = DK / 32;
   using Vec = typename std::conditional<CPL == 4, float4, float2>::type;
@@ -534,7 +544,7 @@ __global__ void __launch_bounds__(416, 2)
   __shared__ Stage stg[2];
   __shared__ uint64_t full[NS], empty[NS], in_full[2], in_empty[2];
   __shared__ float os[R * DV];
-  __shared__ float red[8];
+  __shared__ float red[R * DV / 32];
   __shared__ float pqk[2][2 * QW];
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -543,12 +553,12 @@ __global__ void __launch_bounds__(416, 2)
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 8);
+      mbar_init(&empty[i], NCW);
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       mbar_init(&in_full[i], NP);
-      mbar_init(&in_empty[i], 8);
+      mbar_init(&in_empty[i], NCW);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -557,7 +567,7 @@ __global__ void __launch_bounds__(416, 2)
   const size_t sl = size_t(hv) * DV * DK;
   const size_t cl = size_t(CONV - 1) * cd;
   int issued = 0;  // issuer: chunks issued
-  if (warp == 8) {
+  if (warp == IW) {
     int n = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
@@ -587,8 +597,8 @@ __global__ void __launch_bounds__(416, 2)
         }
       }
     }
-  } else if (warp > 8) {
-    const int p = threadIdx.x - 9 * 32, pw = p >> 5;
+  } else if (warp >= SW0) {
+    const int p = threadIdx.x - SW0 * 32, pw = p >> 5;
     int j = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++j) {
       const int seq = i / hk, kh = i % hk, b = j & 1;
@@ -674,7 +684,10 @@ __global__ void __launch_bounds__(416, 2)
     }
   } else {
     const int tid = threadIdx.x;
-    const float gw = tid < R * DV ? gnorm[tid % DV] : 0.f;
+    constexpr int NO = (R * DV + NCW * 32 - 1) / (NCW * 32);  // norm channels per consumer thread
+    float gw[NO];
+#pragma unroll
+    for (int u = 0; u < NO; ++u) gw[u] = tid + u * NCW * 32 < R * DV ? gnorm[(tid + u * NCW * 32) % DV] : 0.f;
     bool finite = true;
     int n = 0, j = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++j) {
@@ -699,8 +712,8 @@ __global__ void __launch_bounds__(416, 2)
         const float g = S.g[hh], beta = S.beta[hh];
         const float* chunk = ring + s * CR * DK;
 #pragma unroll
-        for (int k = 0; k < CR / 8; ++k) {
-          const int rl = warp * (CR / 8) + k, r = (c % HC) * CR + rl;
+        for (int k = 0; k < RPC; ++k) {
+          const int rl = warp * RPC + k, r = (c % HC) * CR + rl;
           Vec row = *reinterpret_cast<const Vec*>(chunk + rl * DK + lane * CPL);
           float* St = reinterpret_cast<float*>(&row);
           float mem = 0.f;
@@ -726,21 +739,31 @@ __global__ void __launch_bounds__(416, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
-      // the R gated RMSNorms over dv (native/qwen_model.inc:203-204)
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      const float o = tid < R * DV ? os[tid] : 0.f;
-      const float z = tid < R * DV ? S.z[tid] : 0.f;
-      const int t = S.t;
-      const float ss = warp_sum(o * o);
-      if (lane == 0) red[warp] = ss;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (tid < R * DV && ok) {
-        const int hh = tid / DV;
-        float tot = 0.f;
+      // the R gated RMSNorms over dv (native/qwen_model.inc:203-204); red[g]
+      // holds the sum of squares of channels [32g, 32g + 32)
+      asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+      float o[NO], z[NO];
 #pragma unroll
-        for (int w = 0; w < DV / 32; ++w) tot += red[hh * (DV / 32) + w];
-        const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
-        out[size_t(t) * vd + size_t(kh) * R * DV + tid] = __float2bfloat16_rn(y);
+      for (int u = 0; u < NO; ++u) {
+        const int ch = tid + u * NCW * 32;
+        o[u] = ch < R * DV ? os[ch] : 0.f;
+        z[u] = ch < R * DV ? S.z[ch] : 0.f;
+        const float ss = warp_sum(o[u] * o[u]);
+        if (lane == 0 && ch < R * DV) red[ch / 32] = ss;
+      }
+      const int t = S.t;
+      asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32) : "memory");
+#pragma unroll
+      for (int u = 0; u < NO; ++u) {
+        const int ch = tid + u * NCW * 32;
+        if (ch < R * DV && ok) {
+          const int hh = ch / DV;
+          float tot = 0.f;
+#pragma unroll
+          for (int w = 0; w < DV / 32; ++w) tot += red[hh * (DV / 32) + w];
+          const float y = o[u] * rsqrtf(tot / DV + eps) * gw[u] * siluf_(z[u]);
+          out[size_t(t) * vd + size_t(kh) * R * DV + ch] = __float2bfloat16_rn(y);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&in_empty[b]);
@@ -749,7 +772,7 @@ __global__ void __launch_bounds__(416, 2)
   }
   __syncthreads();
   // after a timeout, copies may still be landing in the ring: wait for them (bounded)
-  if (warp == 8 && lane == 0 && abort_flag) {
+  if (warp == IW && lane == 0 && abort_flag) {
 #pragma unroll 1
     for (int n = issued > NS ? issued - NS : 0; n < issued; ++n) {
       const long long c0 = clock64();
@@ -771,7 +794,7 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   bool done = false;
 #define QWEN_GDN_DECODE(DK_, DV_, R_)                                                                             \
   if (!done && T == n_seq && d.conv == 4 && d.dk == DK_ && d.dv == DV_ && R == R_) {                             \
-    constexpr int ring_bytes = 6 * 32 * DK_ * 4;                                                                 \
+    constexpr int ring_bytes = kDecRing * 32 * DK_ * 4;                                                                 \
     static const bool set_##DK_##_##R_ = [] {                                                                    \
       QWEN_CUDA(cudaFuncSetAttribute(gdn_decode_kernel<DK_, DV_, R_, 4>,                                         \
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, ring_bytes));                  \
@@ -782,8 +805,8 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
     }();                                                                                                         \
     (void)set_##DK_##_##R_;                                                                                      \
     const int items = n_seq * d.hk;                                                                              \
-    const int per_cta = (items + 2 * sm_count - 1) / (2 * sm_count);                                             \
-    launch_pdl(gdn_decode_kernel<DK_, DV_, R_, 4>, (items + per_cta - 1) / per_cta, 416, size_t(ring_bytes), s,   \
+    const int per_cta = (items + kDecCtasPerSm * sm_count - 1) / (kDecCtasPerSm * sm_count);                                             \
+    launch_pdl(gdn_decode_kernel<DK_, DV_, R_, 4>, (items + per_cta - 1) / per_cta, kDecThreads, size_t(ring_bytes), s,   \
                proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, items,       \
                ly.conv_w, ly.a_log, ly.dt_bias, ly.gnorm, d.eps, out, err, cand_slots);                           \
     QWEN_CUDA(cudaGetLastError());                                                                               \
