@@ -1,5 +1,9 @@
-// Gated-DeltaNet mixer (native/qwen_model.inc:154-206, native/operator_reference.h:19-45)
-// as two kernels per layer:
+// Gated-DeltaNet mixer (native/qwen_model.inc:154-206, native/operator_reference.h:19-45).
+// Decode steps (one token per sequence) run gdn_decode_kernel, one kernel per
+// layer that streams the state through a shared-memory ring (gdn_stream_kernel
+// after gdn_prep for conv widths other than 4, described below). Steps that
+// feed several tokens to a sequence (prefill, speculative verify) run two
+// kernels per layer:
 //
 //  gdn_prep:   CTA = (sequence, key head). Causal depthwise conv1d (K taps,
 //              tap 0 oldest) over [conv history; new qkv rows] + SiLU for the key
