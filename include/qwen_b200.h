@@ -75,6 +75,52 @@ int rs_mlx_weight_bytes(void* store, const char* name, const int32_t* shape, siz
                         int dtype, size_t offset, uint8_t* output, size_t count, char* error,
                         size_t capacity);
 
+/* Replaces rs_qwen_forward (native/mlx_bridge.h:56-57, native/qwen_model.inc:278-377;
+ * declared at src/serving/native_qwen.rs:566): one-shot forward of `count`
+ * (1..chunk <= 8) tokens at `offset`. old_state (rs_qwen_state_count floats,
+ * NULL / 0 iff offset == 0) is the state before the tokens in the reference
+ * layout; new_state (same layout and count) receives the state after them and
+ * logits (vocab floats) the last token's logits. gpu must be 1 (this backend
+ * has no CPU path). projection_checks, projection_outputs and trace are MLX
+ * diagnostics this backend does not provide: they must be 0 / NULL. Uses a
+ * private device session kept in the store (rebuilt when `config` changes),
+ * so calls on one store must come from one thread at a time. K/V rows of
+ * old_state are held in the session's bf16 cache. */
+int rs_qwen_forward(void* store, int gpu, const rs_qwen_config* config, const rs_qwen_layer* layers,
+                    size_t layer_count, const uint32_t* tokens, size_t count, size_t offset,
+                    const float* old_state, size_t old_count, float* new_state, size_t new_count,
+                    float* logits, size_t logits_count, int projection_checks,
+                    const uint32_t* projection_outputs, size_t projection_output_count, float* trace,
+                    size_t trace_count, char* error, size_t capacity);
+
+/* ---- MLX graph builder (native/mlx_bridge.h:8-43; declared at
+ * src/serving/native_mlx.rs:574-636). The reference's in-process MLX graph
+ * executor has no counterpart on this backend: rs_mlx_create returns NULL and
+ * the other builders return -1, each with a message; rs_mlx_destroy and
+ * rs_mlx_cleanup do nothing. They exist so the Rust crate links unchanged. */
+/* Replaces rs_mlx_create (native/mlx_bridge.h:8). */
+void* rs_mlx_create(int gpu, char* error, size_t capacity);
+/* Replaces rs_mlx_destroy (native/mlx_bridge.h:9). */
+void rs_mlx_destroy(void* graph);
+/* Replaces rs_mlx_input (native/mlx_bridge.h:10-11). */
+int rs_mlx_input(void* graph, int dtype, const void* data, const int32_t* shape, size_t rank, char* error,
+                 size_t capacity);
+/* Replaces rs_mlx_op (native/mlx_bridge.h:12-13). */
+int rs_mlx_op(void* graph, int op, const uint32_t* inputs, size_t count, int group, float epsilon,
+              char* error, size_t capacity);
+/* Replaces rs_mlx_finish (native/mlx_bridge.h:14-15). */
+int rs_mlx_finish(void* graph, uint32_t output, void* data, size_t elements, char* error, size_t capacity);
+/* Replaces rs_mlx_kernel (native/mlx_bridge.h:41-43). */
+int rs_mlx_kernel(void* graph, int op, const uint32_t* inputs, size_t count, const int32_t* ints, size_t ni,
+                  const float* floats, size_t nf, char* error, size_t capacity);
+/* Replaces rs_mlx_parameter (native/mlx_bridge.h:33-34). */
+int rs_mlx_parameter(void* graph, void* store, const char* name, const int32_t* shape, size_t rank,
+                     int dtype, char* error, size_t capacity);
+/* Replaces rs_mlx_cleanup (native/mlx_bridge.h:23; native/mlx_bridge.cpp:96
+ * clears MLX streams at executor-thread exit). Sessions own their CUDA streams,
+ * so there is nothing per-thread to release. */
+void rs_mlx_cleanup(void);
+
 /* NEW (no reference counterpart; the reference loads a private checkpoint,
  * src/serving/qwen_tests.rs:17-243 builds a synthetic one): fill `store` with
  * seeded random-init weights of the given architecture, generated on the
@@ -293,8 +339,8 @@ int rs_qwen_device_timing(void* session, double* out, size_t count, char* error,
 
 /* NEW diagnostic: run one dense 4-bit GEMM of the model on caller inputs.
  * which: 0 = layer `layer` mixer input projection, 1 = its output projection,
- * 2 = its MoE router (+ shared gate), 3 = lm_head. x: T rows of bf16 bits
- * (row width = the matrix's input width). y: T x rows fp32 (split-K partials
+ * 2 = its MoE router (+ shared gate), 3 = lm_head. x: T rows of IEEE half
+ * bits, the projection input type (row width = the matrix's input width). y: T x rows fp32 (split-K partials
  * summed). engine: 0 = tcgen05 kernel, 1 = CUDA-core reference kernel.
  * ms: device time of the GEMM launch(es). Returns 0/-1. */
 int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, size_t T, float* y,
@@ -308,15 +354,16 @@ int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, s
  * cudaFree would synchronise the device. It allocates nothing, on the device
  * or the host, when it succeeds.
  *
- * y_device (fp32, T x rows, device) = x_device (bf16 bits, T x k, device,
+ * y_device (fp32, T x rows, device) = x_device (IEEE half, T x k, device,
  * 16-byte aligned) times the selected matrix; `which` and `layer` select it
  * as in rs_qwen_debug_gemm (tcgen05 engine). The split-K partials live in a
  * fixed 16 MiB static device array per device, so T x rows may not exceed
  * 4,194,240 floats; larger calls return -1 with an error naming the limit.
- * Work is enqueued on `stream` (NULL: the session's stream), and the call
- * returns once it has finished. The first call on each device resolves the
- * scratch address (a one-time set-up); make that call before any stream
- * capture begins. Every call on a device shares the one array: calls that
+ * Work is enqueued on `stream` (NULL: the session's stream); the call then
+ * synchronises that stream and returns once the result is in y_device. It
+ * runs on the session's device and leaves the calling thread's current device
+ * as it found it. The first call on each device resolves the scratch address
+ * (a one-time set-up); make that call before any stream capture begins. Every call on a device shares the one array: calls that
  * overlap in time (several host threads, or several sessions on one device)
  * race and corrupt each other's results, so serialise them. Returns 0/-1. */
 int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_device, size_t T,

@@ -45,11 +45,28 @@ def build(force: bool = False) -> Path:
     return LIB
 
 
+def reference_root() -> Path | None:
+    """Location of the reference checkout: the QWEN_REFERENCE environment
+    variable, else BASELINE.json's "reference_path". None when neither names
+    an existing directory (the GPU box has no reference tree)."""
+    where = os.environ.get("QWEN_REFERENCE")
+    if not where:
+        meta = HERE.parent / "BASELINE.json"
+        if meta.exists():
+            import json
+
+            where = json.loads(meta.read_text()).get("reference_path")
+    if where and Path(where).is_dir():
+        return Path(where)
+    return None
+
+
 def build_ref() -> Path | None:
     """Compile oracle/_ref/libref_oracle.so from the reference's own oracle
-    headers when the reference checkout is present (this container only)."""
-    ref = Path(os.environ.get("QWEN_REFERENCE", "/root/reference")) / "native"
-    if not (ref / "operator_reference.h").exists():
+    headers when the reference checkout is present (see reference_root)."""
+    root = reference_root()
+    ref = root / "native" if root else None
+    if ref is None or not (ref / "operator_reference.h").exists():
         return REF_LIB if REF_LIB.exists() else None
     subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
     return REF_LIB
@@ -67,6 +84,7 @@ def lib():
                                  C.POINTER(C.c_int32), C.POINTER(C.c_uint32), C.c_size_t)
         L.orc_last_error.restype = C.c_char_p
         L.orc_set_routing_slack.argtypes = [C.c_double]
+        L.orc_set_emulation.argtypes = [C.c_int]
         L.orc_state_count.restype = SZ
         L.orc_state_count.argtypes = [C.POINTER(RsQwenConfig)]
         L.orc_model_create.restype = P
@@ -199,6 +217,15 @@ class Model:
 
 def set_routing_slack(slack: float):
     lib().orc_set_routing_slack(slack)
+
+
+# Error-analysis knobs of the oracle (0 = exact FP64): round a class of values
+# the way a 16-bit device datapath stores them (qwen_oracle.cpp, g_emulate).
+EMU_WEIGHTS, EMU_ACTIVATIONS, EMU_KV, EMU_ATTN_QP, EMU_HALF = 1, 2, 4, 8, 256
+
+
+def set_emulation(bits: int):
+    lib().orc_set_emulation(int(bits))
 
 
 def argmax(logits) -> int:

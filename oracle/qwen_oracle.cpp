@@ -43,6 +43,21 @@ namespace {
 thread_local std::string g_error;
 double g_routing_slack = 2e-3;
 
+// Error-analysis knobs (default 0 = exact FP64). Each bit rounds one class of
+// values the way a 16-bit device datapath stores them, so the contribution of
+// each rounding to the end-to-end error can be measured on the CPU:
+//   1 dequantised weights of the projections (scale*q + bias, one rounding)
+//   2 projection input activations
+//   4 attention K / V cache entries
+//   8 attention queries and the unnormalised softmax weights of P.V
+//   256: the 16-bit type is IEEE half instead of bfloat16
+int g_emulate = 0;
+
+double round16(double v) {
+  if (g_emulate & 256) return double(float(_Float16(float(v))));
+  return double(synth::bf16_to_float(synth::bf16_rne(float(v))));
+}
+
 template <class F>
 int guarded(F f) {
   try {
@@ -169,24 +184,33 @@ struct QTensor {
     });
   }
   // Dequantized row (native/projection_reference.h:74 element formula).
-  void row(size_t r, double* out) {
+  // `projection`: the row feeds a projection (emulation bit 1 may round it).
+  void row(size_t r, double* out, bool projection = false) {
     const Block& blk = block(r / 128);
     size_t lr = r % 128, words = cols / 8, groups = cols / 64;
+    const bool rnd = projection && (g_emulate & 1);
     for (size_t c = 0; c < cols; ++c) {
       unsigned q = (blk.packed[lr * words + c / 8] >> (4 * (c % 8))) & 15u;
       out[c] = double(blk.scale[lr * groups + c / 64]) * q + double(blk.bias[lr * groups + c / 64]);
+      if (rnd) out[c] = round16(out[c]);
     }
   }
   // y[t][o] = sum_c x[t][c] * W[row0+o][c], for o < n_out.
   void project(const double* x, size_t n_tok, size_t row0, size_t n_out, double* y) {
     if (row0 + n_out > rows) throw std::invalid_argument("projection rows out of range: " + name);
     ensure(row0, n_out);
+    std::vector<double> xr;
+    if (g_emulate & 2) {
+      xr.assign(x, x + n_tok * cols);
+      for (auto& v : xr) v = round16(v);
+      x = xr.data();
+    }
     parallel_for(
         n_out,
         [&](size_t b, size_t e) {
           std::vector<double> w(cols);
           for (size_t o = b; o < e; ++o) {
-            row(row0 + o, w.data());
+            row(row0 + o, w.data(), true);
             for (size_t t = 0; t < n_tok; ++t) {
               double s = 0;
               const double* xt = x + t * cols;
@@ -390,6 +414,8 @@ struct Forward {
         rms_rows(src, &q[(t * Hq + hh) * d], 1, d, qn.data(), c.epsilon);
         for (size_t i = 0; i < d; ++i) gate[(t * Hq + hh) * d + i] = src[d + i];
         rope_vec(&q[(t * Hq + hh) * d], c.rope_dims, double(offset + t), c.theta);
+        if (g_emulate & 8)
+          for (size_t i = 0; i < d; ++i) q[(t * Hq + hh) * d + i] = round16(q[(t * Hq + hh) * d + i]);
       }
     for (size_t t = 0; t < T; ++t)
       for (size_t g = 0; g < Hk; ++g) {
@@ -397,8 +423,8 @@ struct Forward {
         rope_vec(tmp.data(), c.rope_dims, double(offset + t), c.theta);
         if (offset + t >= ctx) throw std::invalid_argument("oracle context overflow");
         for (size_t i = 0; i < d; ++i) {
-          Kc[(g * ctx + offset + t) * d + i] = tmp[i];
-          Vc[(g * ctx + offset + t) * d + i] = v[(t * Hk + g) * d + i];
+          Kc[(g * ctx + offset + t) * d + i] = (g_emulate & 4) ? round16(tmp[i]) : tmp[i];
+          Vc[(g * ctx + offset + t) * d + i] = (g_emulate & 4) ? round16(v[(t * Hk + g) * d + i]) : v[(t * Hk + g) * d + i];
         }
       }
     // attention_reference.h:8-21, bottom-right causal window.
@@ -418,6 +444,8 @@ struct Forward {
         }
         double tot = 0;
         for (auto& s : sc) { s = std::exp(s - peak); tot += s; }
+        if (g_emulate & 8)
+          for (auto& s : sc) s = round16(s);  // P enters P.V as 16-bit; the sum stays exact
         for (size_t i = 0; i < d; ++i) {
           double acc = 0;
           for (size_t j = 0; j < visible; ++j) acc += sc[j] / tot * Vc[(g * ctx + j) * d + i];
@@ -524,6 +552,9 @@ const char* orc_last_error() { return g_error.c_str(); }
 // Slack (relative to 1+|logit|) allowed when a forced expert selection is
 // checked against the oracle's own FP64 router logits.
 void orc_set_routing_slack(double slack) { g_routing_slack = slack; }
+
+// Error-analysis knobs (bits documented at g_emulate); 0 restores exact FP64.
+void orc_set_emulation(int bits) { g_emulate = bits; }
 
 size_t orc_state_count(const rs_qwen_config* c) { return state_count(*c); }
 

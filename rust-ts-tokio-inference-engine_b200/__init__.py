@@ -69,6 +69,16 @@ SIGNATURES = {
     "rs_qwen_quant": (C.c_int, [_P, C.c_char_p, C.c_int, C.c_int, _ERR, _SZ]),
     "rs_mlx_weight_bytes": (C.c_int, [_P, C.c_char_p, _I32P, _SZ, C.c_int, _SZ, C.POINTER(C.c_uint8), _SZ, _ERR, _SZ]),
     "rs_qwen_weights_synthetic": (C.c_int, [_P, C.POINTER(RsQwenConfig), C.c_uint64, C.c_int, _ERR, _SZ]),
+    "rs_qwen_forward": (C.c_int, [_P, C.c_int, C.POINTER(RsQwenConfig), C.POINTER(RsQwenLayer), _SZ, _U32P, _SZ, _SZ,
+                                  _F32P, _SZ, _F32P, _SZ, _F32P, _SZ, C.c_int, _U32P, _SZ, _F32P, _SZ, _ERR, _SZ]),
+    "rs_mlx_create": (_P, [C.c_int, _ERR, _SZ]),
+    "rs_mlx_destroy": (None, [_P]),
+    "rs_mlx_input": (C.c_int, [_P, C.c_int, C.c_void_p, _I32P, _SZ, _ERR, _SZ]),
+    "rs_mlx_op": (C.c_int, [_P, C.c_int, _U32P, _SZ, C.c_int, C.c_float, _ERR, _SZ]),
+    "rs_mlx_finish": (C.c_int, [_P, C.c_uint32, C.c_void_p, _SZ, _ERR, _SZ]),
+    "rs_mlx_kernel": (C.c_int, [_P, C.c_int, _U32P, _SZ, _I32P, _SZ, _F32P, _SZ, _ERR, _SZ]),
+    "rs_mlx_parameter": (C.c_int, [_P, _P, C.c_char_p, _I32P, _SZ, C.c_int, _ERR, _SZ]),
+    "rs_mlx_cleanup": (None, []),
     "rs_qwen_device_create": (_P, [_P, C.c_int, C.POINTER(RsQwenConfig), C.POINTER(RsQwenLayer), _SZ, _SZ,
                                    C.c_uint64, _ERR, _SZ]),
     "rs_qwen_device_destroy": (None, [_P]),
@@ -196,6 +206,19 @@ class WeightStore:
         self.cfg = cfg
         _call("rs_qwen_weights_synthetic", self.h, C.byref(cfg), seed, int(mtp))
         return self
+
+    def forward(self, cfg: RsQwenConfig, tokens, offset: int, old_state=None):
+        """rs_qwen_forward: returns (last-row logits [vocab], new_state [state_count])."""
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        n = state_count(cfg)
+        new = np.zeros(n, np.float32)
+        old = None if old_state is None else np.ascontiguousarray(old_state, np.float32)
+        logits = np.zeros(cfg.vocab, np.float32)
+        layers = layer_program(cfg)
+        _call("rs_qwen_forward", self.h, 1, C.byref(cfg), layers, cfg.layers, _ptr(tok, C.c_uint32), len(tok),
+              offset, _ptr(old, C.c_float), 0 if old is None else old.size, _ptr(new, C.c_float), n,
+              _ptr(logits, C.c_float), logits.size, 0, None, 0, None, 0)
+        return logits, new
 
     def weight_bytes(self, name: str, offset: int, count: int, dtype: int = 2) -> bytes:
         buf = (C.c_uint8 * count)()
@@ -392,9 +415,10 @@ class DeviceSession:
         _call("rs_qwen_device_timing", self.h, out, 22)
         return out[0], out[1], int(out[2]), list(out[3:])
 
-    def debug_gemm(self, which: int, layer: int, x_bf16, rows: int, engine: int = 0):
-        """Run one dense GEMM (0 in_proj, 1 out_proj, 2 router, 3 lm_head); returns (y, ms)."""
-        x = np.ascontiguousarray(x_bf16, np.uint16)
+    def debug_gemm(self, which: int, layer: int, x_f16, rows: int, engine: int = 0):
+        """Run one dense GEMM (0 in_proj, 1 out_proj, 2 router, 3 lm_head) on IEEE-half
+        input bits [T][k]; returns (y, ms)."""
+        x = np.ascontiguousarray(x_f16, np.uint16)
         T = x.shape[0]
         y = np.zeros((T, rows), np.float32)
         ms = C.c_double()
@@ -405,7 +429,7 @@ class DeviceSession:
     def project_noalloc(self, which: int, layer: int, x_device_ptr: int, T: int, y_device_ptr: int, y_count: int,
                         stream_ptr: int = 0):
         """Allocation-free dense projection on device buffers (rs_qwen_project_noalloc):
-        y (fp32 [T][rows]) = x (bf16 [T][k]) . W; raises on error, including T x rows
+        y (fp32 [T][rows]) = x (IEEE half [T][k]) . W; raises on error, including T x rows
         beyond the 16 MiB static scratch."""
         _call("rs_qwen_project_noalloc", self.h, which, layer, C.c_void_p(x_device_ptr), T,
               C.c_void_p(y_device_ptr), y_count, C.c_void_p(stream_ptr or None))

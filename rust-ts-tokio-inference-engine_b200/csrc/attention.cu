@@ -317,12 +317,11 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
   const size_t smem = attn_decode_smem(d.D);
 #define QWEN_ATTN(DD)                                                                                         \
   if (d.D == DD) {                                                                                          \
-    static bool cfg = false;                                                                                \
-    if (!cfg) {                                                                                             \
+    static std::atomic<uint64_t> cfg_##DD{0};                                                               \
+    once_per_device(cfg_##DD, [&] {                                                                         \
       QWEN_CUDA(cudaFuncSetAttribute(attn_decode_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
                                      int(smem)));                                                           \
-      cfg = true;                                                                                           \
-    }                                                                                                       \
+    });                                                                                                     \
     launch_pdl(attn_decode_kernel<DD>, grid, kAttnWarps * 32, smem, s, kvmap, q, token_seq, token_pos, descs,      \
                                                                block_table, bt_stride, items, split_pages,  \
                                                                d.Hq, d.Hkv, G, max_splits, ws, err);        \

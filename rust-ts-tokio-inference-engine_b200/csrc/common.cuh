@@ -1,9 +1,11 @@
 // Shared definitions for the B200 ragged hybrid-Qwen decode step.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -18,9 +20,26 @@
 
 namespace qwen {
 
+// Runs `setup` the first time it is reached on the calling thread's current
+// CUDA device, once per device: kernel attributes such as the dynamic
+// shared-memory limit are per-device state, so a process that drives several
+// GPUs must set them on each. `seen` holds one bit per device (devices past
+// 63 simply repeat the cheap setup on every call).
+template <class F>
+inline void once_per_device(std::atomic<uint64_t>& seen, F setup) {
+  int dev = 0;
+  QWEN_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev >= 0 && dev < 64 ? uint64_t(1) << dev : 0;
+  if (bit && (seen.load(std::memory_order_acquire) & bit)) return;
+  setup();
+  if (bit) seen.fetch_or(bit, std::memory_order_release);
+}
+
 // 4-bit affine g64 weight tile: 128 rows x 64 columns (one quant group per row).
-// Layout: packed nibbles [128 rows][8 uint32 words], then 128 bf16 scales, then
-// 128 bf16 biases. Word w of a row holds columns 8w..8w+7 in pair-interleaved
+// Layout: packed nibbles [128 rows][8 uint32 words], then 128 scales, then 128
+// biases, both IEEE half holding the checkpoint's bf16 values exactly (every
+// bf16 value of magnitude >= 2^-17, and zero, is an fp16 value; the loaders
+// reject others). Word w of a row holds columns 8w..8w+7 in pair-interleaved
 // nibble order: nibble i (bits 4i..4i+3) holds column 8w + nibble_col(i) with
 // nibble_col = {0,2,4,6,1,3,5,7}, so ((word >> 4j) & 0x000F000F) yields the
 // consecutive pair (8w+2j, 8w+2j+1) in the low/high 16-bit halves. A matrix [rows, K] is stored as
@@ -31,6 +50,10 @@ constexpr int kTileK = 64;
 constexpr int kTilePackedBytes = kTileRows * kTileK / 2;  // 4096
 constexpr int kTileBytes = kTilePackedBytes + kTileRows * 2 * 2;  // 4608
 constexpr int kPageTokens = 16;  // paged-KV page size (tokens)
+// Routed experts per MoE layer the routing kernels hold (route_kernel keeps
+// four experts per thread of a 256-thread CTA; the sort's shared tables scale
+// with the expert count).
+constexpr int kMaxExperts = 1024;
 
 // Nibble index holding column c (0..7) of a packed word, and its inverse.
 __host__ __device__ __forceinline__ int nibble_of_col(int c) { return (c & 1) ? 4 + (c >> 1) : (c >> 1); }
@@ -50,6 +73,62 @@ struct QMat {
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
   return __uint_as_float(uint32_t(b) << 16);
+}
+
+// Element type of every projection input (the activations the tcgen05 GEMM
+// reads as its B operand) and of the dequantised weights (its A operand):
+// IEEE half. Its 11-bit significand rounds scale*q + bias and each activation
+// 8x more finely than bfloat16 (the end-to-end logits error of a decode step
+// drops by about that factor), and the values that enter a projection
+// (RMS-normalised rows, gated attention / DeltaNet outputs, SwiGLU products)
+// stay far inside its range.
+using gemm_in_t = __half;
+__device__ __forceinline__ gemm_in_t to_gemm_in(float v) { return __float2half_rn(v); }
+__device__ __forceinline__ __half2 to_gemm_in2(float a, float b) { return __floats2half2_rn(a, b); }
+__host__ __device__ __forceinline__ float half_bits_to_float(uint16_t b) {
+#ifdef __CUDA_ARCH__
+  return __half2float(__ushort_as_half(b));
+#else
+  // host: widen IEEE binary16 exactly
+  const uint32_t sign = uint32_t(b & 0x8000u) << 16, ex = (b >> 10) & 0x1Fu, man = b & 0x3FFu;
+  uint32_t u;
+  if (ex == 0x1F) {
+    u = sign | 0x7F800000u | (man << 13);
+  } else if (ex) {
+    u = sign | ((ex + 112u) << 23) | (man << 13);
+  } else if (!man) {
+    u = sign;
+  } else {  // subnormal: normalise
+    int e = -1;
+    uint32_t m = man;
+    do { m <<= 1; ++e; } while (!(m & 0x400u));
+    u = sign | (uint32_t(112 - e) << 23) | ((m & 0x3FFu) << 13);
+  }
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+// bf16 bits -> the fp16 bits of the same value; false when fp16 cannot hold it exactly.
+__host__ __device__ __forceinline__ bool bf16_to_half_bits(uint16_t b, uint16_t* out) {
+  const uint32_t sign = (b & 0x8000u) ? 0x8000u : 0u;
+  const int ex = (b >> 7) & 0xFF, man = b & 0x7F;
+  if (ex == 0 && man == 0) { *out = uint16_t(sign); return true; }
+  if (ex == 0xFF) return false;
+  const int e = ex - 127;  // value = 1.man * 2^e (bf16 subnormals are below fp16's range)
+  if (ex == 0) return false;
+  if (e > 15) return false;
+  if (e >= -14) { *out = uint16_t(sign | uint32_t(e + 15) << 10 | uint32_t(man) << 3); return true; }
+  // fp16 subnormal: value = m * 2^-24 with m = (128 + man) * 2^(e + 24 - 7)
+  const int shift = e + 17;  // left shift of (128+man) if >= 0
+  if (shift < 0) {
+    const uint32_t full = 128u + uint32_t(man);
+    if (full & ((1u << -shift) - 1u)) return false;
+    *out = uint16_t(sign | (full >> -shift));
+    return true;
+  }
+  *out = uint16_t(sign | ((128u + uint32_t(man)) << shift));
+  return true;
 }
 
 // Round-to-nearest-even narrowing to bf16 bits (matches the host generator).

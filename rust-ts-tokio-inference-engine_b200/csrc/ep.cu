@@ -16,7 +16,7 @@
 //                    order (then the source's sort order), and the shared
 //                    expert's local rows last -> group offsets over E + 1
 //                    experts for the grouped GEMM (non-local experts empty);
-//   ep_gather        those rows into one bf16 matrix, with each row's origin;
+//   ep_gather        those rows into one fp16 matrix, with each row's origin;
 //   grouped GEMMs    (unchanged) over the local rows;
 //   ep_return_pack   each result row into its source's return stage (fp32);
 //   transport        the same way back (flags / NCCL);
@@ -81,10 +81,10 @@ __device__ __forceinline__ void ep_signal_last(uint32_t* const* flag_dst, int wo
   if (threadIdx.x < world) st_release_sys(flag_dst[threadIdx.x], epoch);
 }
 
-// Stage layout: [hdr_ints int32 counts (padded to 16 B)] [cap rows x H bf16]
+// Stage layout: [hdr_ints int32 counts (padded to 16 B)] [cap rows x H fp16]
 // Rows come straight from the MoE input: sorted position q is row perm[q] / div
 // of `src` (stride ld), so no gathered copy is made first.
-__global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ src, int ld, const int32_t* __restrict__ perm,
+__global__ void ep_pack_kernel(const gemm_in_t* __restrict__ src, int ld, const int32_t* __restrict__ perm,
                                int div, const int32_t* __restrict__ counts,
                                const int32_t* __restrict__ offsets, uint8_t* const* __restrict__ dst,
                                int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
@@ -98,7 +98,7 @@ __global__ void ep_pack_kernel(const __nv_bfloat16* __restrict__ src, int ld, co
     for (int j = threadIdx.x; j < hdr_ints; j += blockDim.x)
       reinterpret_cast<int32_t*>(st)[j] = j < per_rank ? counts[e0 + j] : 0;
   const int r0 = offsets[e0], n = offsets[e0 + per_rank] - r0;
-  __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(st + size_t(hdr_ints) * 4);
+  gemm_in_t* rows = reinterpret_cast<gemm_in_t*>(st + size_t(hdr_ints) * 4);
   const int h8 = H / 8;
   for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * h8; idx += gridDim.x * blockDim.x) {
     if (idx / h8 >= cap) break;  // cannot happen: n <= cap is checked by the planner of the step
@@ -188,9 +188,9 @@ __global__ void ep_plan_kernel(const uint8_t* const* __restrict__ srcs, int worl
 // stage row for routed rows, -1 - sorted position for shared rows.
 __global__ void ep_gather_kernel(const uint8_t* const* __restrict__ srcs, int world, int per_rank, int hdr_ints,
                                  int E, const int32_t* __restrict__ goff, const int32_t* __restrict__ seg,
-                                 const int32_t* __restrict__ offsets, const __nv_bfloat16* __restrict__ xsrc, int ld,
+                                 const int32_t* __restrict__ offsets, const gemm_in_t* __restrict__ xsrc, int ld,
                                  const int32_t* __restrict__ perm, int div,
-                                 __nv_bfloat16* __restrict__ xloc, int32_t* __restrict__ origin, int cap, int H,
+                                 gemm_in_t* __restrict__ xloc, int32_t* __restrict__ origin, int cap, int H,
                                  int rank) {
   pdl_trigger();
   pdl_wait();
@@ -265,7 +265,7 @@ __global__ void ep_return_unpack_kernel(const float* const* __restrict__ rsrcs, 
 
 }  // namespace
 
-void launch_ep_pack(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, const int32_t* counts,
+void launch_ep_pack(const gemm_in_t* src, int ld, const int32_t* perm, int div, const int32_t* counts,
                     const int32_t* offsets, uint8_t* const* dst,
                     int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                     uint32_t* done, cudaStream_t s) {
@@ -277,9 +277,9 @@ void launch_ep_pack(const __nv_bfloat16* src, int ld, const int32_t* perm, int d
 }
 
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
-                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xsrc, int ld,
+                           const int32_t* counts, const int32_t* offsets, const gemm_in_t* xsrc, int ld,
                            const int32_t* perm, int div, int32_t* goff,
-                           int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
+                           int32_t* seg, int32_t* n_rows, gemm_in_t* xloc, int32_t* origin, int cap, int H,
                            int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
                            cudaStream_t s) {
   const size_t n = size_t(world) * per_rank;

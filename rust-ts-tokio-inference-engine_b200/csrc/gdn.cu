@@ -21,7 +21,7 @@
 //              [l*dk/32, ...). Per token S *= g; m = S k; delta = beta (v - m);
 //              S += delta k^T; o = S q; rows go back to shared memory, or
 //              straight to the child's slot after the last token; then the
-//              gated RMSNorm y = rms(o) * w * silu(z) is written as bf16.
+//              gated RMSNorm y = rms(o) * w * silu(z) is written as fp16 (the out_proj input).
 // The state read + write (2 x 64 KiB per head for dk = dv = 128) is the
 // HBM traffic that bounds the layer.
 #include <atomic>
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(256, 3)
                       int hk, int hv, const float* __restrict__ qk, const float* __restrict__ vv,
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
-                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+                      gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(256, 3)
 #pragma unroll
       for (int w = 0; w < 8; ++w) tot += red[w];
       const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
-      out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
+      out[size_t(t) * vd + head * DV + threadIdx.x] = to_gemm_in(y);
     }
   }
   if (d.count == 0) {  // no token: the child carries the parent's state
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(288, 3)
                       int hk, int hv, int n_items, const float* __restrict__ qk, const float* __restrict__ vv,
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
-                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+                      gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;   // state columns per lane
@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(288, 3)
 #pragma unroll
         for (int w = 0; w < 8; ++w) tot += red[w];
         const float y = o * rsqrtf(tot / DV + eps) * gw * siluf_(z);
-        out[size_t(t) * vd + head * DV + threadIdx.x] = __float2bfloat16_rn(y);
+        out[size_t(t) * vd + head * DV + threadIdx.x] = to_gemm_in(y);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&in_empty[b]);
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
                       const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                       int hk, int hv, int n_items, const float* __restrict__ conv_w, const float* __restrict__ a_log,
                       const float* __restrict__ dt_bias, const float* __restrict__ gnorm, float eps,
-                      __nv_bfloat16* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+                      gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;      // state columns per lane
@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
 #pragma unroll
           for (int w = 0; w < DV / 32; ++w) tot += red[hh * (DV / 32) + w];
           const float y = o[u] * rsqrtf(tot / DV + eps) * gw[u] * siluf_(z[u]);
-          out[size_t(t) * vd + size_t(kh) * R * DV + ch] = __float2bfloat16_rn(y);
+          out[size_t(t) * vd + size_t(kh) * R * DV + ch] = to_gemm_in(y);
         }
       }
       __syncwarp();
@@ -790,7 +790,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
 
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
                 const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool, int gdn_index,
-                __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int sm_count,
+                gemm_in_t* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int sm_count,
                 const int32_t* cand_slots, cudaStream_t s) {
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
@@ -799,15 +799,14 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
 #define QWEN_GDN_DECODE(DK_, DV_, R_)                                                                             \
   if (!done && T == n_seq && d.conv == 4 && d.dk == DK_ && d.dv == DV_ && R == R_) {                             \
     constexpr int ring_bytes = kDecRing * 32 * DK_ * 4;                                                                 \
-    static const bool set_##DK_##_##R_ = [] {                                                                    \
+    static std::atomic<uint64_t> set_##DK_##_##R_{0};                                                            \
+    once_per_device(set_##DK_##_##R_, [] {                                                                       \
       QWEN_CUDA(cudaFuncSetAttribute(gdn_decode_kernel<DK_, DV_, R_, 4>,                                         \
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, ring_bytes));                  \
       QWEN_CUDA(cudaFuncSetAttribute(gdn_decode_kernel<DK_, DV_, R_, 4>,                                         \
                                      cudaFuncAttributePreferredSharedMemoryCarveout,                             \
                                      int(cudaSharedmemCarveoutMaxShared)));                                     \
-      return true;                                                                                               \
-    }();                                                                                                         \
-    (void)set_##DK_##_##R_;                                                                                      \
+    });                                                                                                          \
     const int items = n_seq * d.hk;                                                                              \
     const int per_cta = (items + kDecCtasPerSm * sm_count - 1) / (kDecCtasPerSm * sm_count);                                             \
     launch_pdl(gdn_decode_kernel<DK_, DV_, R_, 4>, (items + per_cta - 1) / per_cta, kDecThreads, size_t(ring_bytes), s,   \
@@ -827,26 +826,24 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
     launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
         proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
         ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf, cand_slots);                                                \
-    static const bool smem_set_##DK_##_##R_ = [] {                                                               \
+    static std::atomic<uint64_t> smem_set_##DK_##_##R_{0};                                                       \
+    once_per_device(smem_set_##DK_##_##R_, [] {                                                                  \
       const int bytes = DV_ * DK_ * 4;                                                                           \
       QWEN_CUDA(cudaFuncSetAttribute(gdn_update_kernel<DK_, DV_>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
                                      bytes));                                                                    \
       QWEN_CUDA(cudaFuncSetAttribute(gdn_update_kernel<DK_, DV_>,                                                \
                                      cudaFuncAttributePreferredSharedMemoryCarveout,                             \
                                      int(cudaSharedmemCarveoutMaxShared)));                                     \
-      return true;                                                                                               \
-    }();                                                                                                         \
-    (void)smem_set_##DK_##_##R_;                                                                                 \
+    });                                                                                                          \
     if (T == n_seq) { /* one token per sequence: streamed update */                                             \
-      static const bool ring_set_##DK_##_##R_ = [] {                                                             \
+      static std::atomic<uint64_t> ring_set_##DK_##_##R_{0};                                                     \
+      once_per_device(ring_set_##DK_##_##R_, [] {                                                                \
         QWEN_CUDA(cudaFuncSetAttribute(gdn_stream_kernel<DK_, DV_>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                        4 * 32 * DK_ * 4));                                                       \
         QWEN_CUDA(cudaFuncSetAttribute(gdn_stream_kernel<DK_, DV_>,                                              \
                                        cudaFuncAttributePreferredSharedMemoryCarveout,                           \
                                        int(cudaSharedmemCarveoutMaxShared)));                                   \
-        return true;                                                                                             \
-      }();                                                                                                       \
-      (void)ring_set_##DK_##_##R_;                                                                               \
+      });                                                                                                        \
       const int items = n_seq * d.hv;                                                                            \
       launch_pdl(gdn_stream_kernel<DK_, DV_>, std::min(items, 3 * sm_count), 288, size_t(4) * 32 * DK_ * 4, s,   \
                  descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, items, qk_buf, v_buf, gb_buf, proj, ld_proj,     \

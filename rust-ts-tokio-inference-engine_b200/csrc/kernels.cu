@@ -95,10 +95,10 @@ __global__ void cow_kernel(KvPool kv, const SeqDesc* __restrict__ descs,
 }
 
 // ---------------------------------------------------------- embed + norms --
-// x[t] = dequant(embed[token[t]]) (fp32 residual), hb[t] = bf16(rms(x[t]) * w).
+// x[t] = dequant(embed[token[t]]) (fp32 residual), hb[t] = fp16(rms(x[t]) * w).
 __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ tokens,
                                   const float* __restrict__ norm_w, float eps, float* x,
-                                  __nv_bfloat16* hb) {
+                                  gemm_in_t* hb) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[32];
@@ -111,8 +111,8 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
     const uint8_t* tile = embed.tile(int(tok / kTileRows), c0 / kTileK);
     const int r = tok % kTileRows;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + r * 32 + (c0 % kTileK) / 2);
-    const float sc = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
-    const float bi = bf16_bits_to_float(
+    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+    const float bi = half_bits_to_float(
         reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -124,15 +124,15 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
   const float tot = block_sum(ss, red);
   const float inv = rsqrtf(tot / H + eps);
   for (int c = threadIdx.x; c < H; c += blockDim.x)
-    hb[size_t(t) * H + c] = __float2bfloat16_rn(xr[c] * inv * norm_w[c]);
+    hb[size_t(t) * H + c] = to_gemm_in(xr[c] * inv * norm_w[c]);
 }
 
 // Row r: t = out_token ? out_token[r] : r. x[t] += sum of split partials
-// (only when partial != null); then hb[r] = bf16(rms(x[t]) * w) and optionally
+// (only when partial != null); then hb[r] = fp16(rms(x[t]) * w) and optionally
 // hidden[r] = fp32 normalized row.
 __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restrict__ partial, int splits,
                                      size_t split_stride, int H, const float* __restrict__ norm_w,
-                                     float eps, __nv_bfloat16* __restrict__ hb,
+                                     float eps, gemm_in_t* __restrict__ hb,
                                      const int32_t* __restrict__ out_token, float* __restrict__ hidden) {
   pdl_trigger();
   pdl_wait();
@@ -177,7 +177,7 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
     if (c < H2) {
       const float2 w = reinterpret_cast<const float2*>(norm_w)[c];
       const float y0 = v[k].x * inv * w.x, y1 = v[k].y * inv * w.y;
-      reinterpret_cast<__nv_bfloat162*>(hb + size_t(r) * H)[c] = __floats2bfloat162_rn(y0, y1);
+      reinterpret_cast<__half2*>(hb + size_t(r) * H)[c] = to_gemm_in2(y0, y1);
       if (hidden) reinterpret_cast<float2*>(hidden + size_t(r) * H)[c] = make_float2(y0, y1);
     }
   }
@@ -310,12 +310,12 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
   }
 }
 
-// Merge split partials, apply the output gate sigmoid(gate), write bf16.
+// Merge split partials, apply the output gate sigmoid(gate), write fp16 (the o_proj input).
 // The split weights exp(m_s - M) / sum_s l_s exp(m_s - M) are computed once
 // per (token, head) into shared memory (dynamic: max_splits floats).
 __global__ void attention_merge_kernel(const float* __restrict__ ws, const float* __restrict__ gate,
                                        const int32_t* __restrict__ token_pos, int Hq, int D, int spl,
-                                       int max_splits, __nv_bfloat16* out) {
+                                       int max_splits, gemm_in_t* out) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float wsplit[];
@@ -357,7 +357,7 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
     float num = 0.f;
     for (int s = 0; s < n; ++s) num += base[s * (D + 2) + 2 + i] * wsplit[s];
     const float y = num * inv * sigmoidf_(gate[(size_t(t) * Hq + h) * D + i]);
-    out[size_t(t) * Hq * D + h * D + i] = __float2bfloat16_rn(y);
+    out[size_t(t) * Hq * D + h * D + i] = to_gemm_in(y);
   }
 }
 
@@ -526,11 +526,11 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __rest
 }
 
 // x[t] += sum_j w[t][j] * y[inv[t*slots+j]] (fixed slot order, deterministic);
-// then optional hb[t] = bf16(rms(x[t]) * norm_w).
+// then optional hb[t] = fp16(rms(x[t]) * norm_w).
 __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
                                    const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
                                    int slots, const float* __restrict__ norm_w, float eps,
-                                   __nv_bfloat16* __restrict__ hb) {
+                                   gemm_in_t* __restrict__ hb) {
   pdl_trigger();
   pdl_wait();
   // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
@@ -586,16 +586,16 @@ __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x
     const int c = threadIdx.x + k * blockDim.x;
     if (c < H2) {
       const float2 w = reinterpret_cast<const float2*>(norm_w)[c];
-      reinterpret_cast<__nv_bfloat162*>(hb + size_t(t) * H)[c] =
-          __floats2bfloat162_rn(v[k].x * inv_r * w.x, v[k].y * inv_r * w.y);
+      reinterpret_cast<__half2*>(hb + size_t(t) * H)[c] =
+          to_gemm_in2(v[k].x * inv_r * w.x, v[k].y * inv_r * w.y);
     }
   }
 }
 
 // X_perm[p] = X[perm[p] / slots]: expert-sorted copy of the MoE input rows
 // (contiguous per expert, so the GEMM's TMA loads one box per expert).
-__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int ld, const int32_t* __restrict__ perm,
-                                   int div, int H, __nv_bfloat16* dst) {
+__global__ void gather_rows_kernel(const gemm_in_t* __restrict__ src, int ld, const int32_t* __restrict__ perm,
+                                   int div, int H, gemm_in_t* dst) {
   pdl_trigger();
   pdl_wait();
   const int p = blockIdx.x;
@@ -673,11 +673,11 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
 }
 
 // MTP draft input (native/qwen_mtp.inc:157-161): per token t,
-// cat[t] = [bf16(rms(embed(token_t)) * w_e), bf16(rms(hidden_t) * w_h)]
+// cat[t] = [fp16(rms(embed(token_t)) * w_e), fp16(rms(hidden_t) * w_h)]
 // (the embedding dequantised from the 4-bit table as in embed_norm_kernel).
 __global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens, const float* __restrict__ hidden,
                                  const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
-                                 __nv_bfloat16* __restrict__ cat) {
+                                 gemm_in_t* __restrict__ cat) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[32];
@@ -690,8 +690,8 @@ __global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens
     const uint8_t* tile = embed.tile(int(tok / kTileRows), c0 / kTileK);
     const int r = tok % kTileRows;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + r * 32 + (c0 % kTileK) / 2);
-    const float sc = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
-    const float bi = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
+    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+    const float bi = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float v = fmaf(sc, float(nibble(word, j)), bi);
@@ -704,10 +704,10 @@ __global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens
   const float tot_e = block_sum(se, red);
   const float tot_h = block_sum(sh, red);
   const float ie = rsqrtf(tot_e / H + eps), ih = rsqrtf(tot_h / H + eps);
-  __nv_bfloat16* out = cat + size_t(t) * 2 * H;
+  gemm_in_t* out = cat + size_t(t) * 2 * H;
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
-    out[c] = __float2bfloat16_rn(erow[c] * ie * w_e[c]);
-    out[H + c] = __float2bfloat16_rn(hr[c] * ih * w_h[c]);
+    out[c] = to_gemm_in(erow[c] * ie * w_e[c]);
+    out[H + c] = to_gemm_in(hr[c] * ih * w_h[c]);
   }
 }
 
@@ -849,13 +849,13 @@ void launch_cow(KvPool kv, const SeqDesc* descs, int n_seq, const int32_t* new_p
 }
 
 void launch_embed_norm(const QMat& embed, const uint32_t* tokens, int T, const float* norm_w,
-                       float eps, float* x, __nv_bfloat16* hb, cudaStream_t s) {
+                       float eps, float* x, gemm_in_t* hb, cudaStream_t s) {
   launch_pdl(embed_norm_kernel, T, 256, 0, s, embed, tokens, norm_w, eps, x, hb);
   count_launch();
 }
 
 void launch_residual_norm(float* x, const float* partial, int splits, size_t split_stride, int T,
-                          int H, const float* norm_w, float eps, __nv_bfloat16* hb,
+                          int H, const float* norm_w, float eps, gemm_in_t* hb,
                           const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   const int n = out_token ? rows : T;
   if (n <= 0) return;
@@ -890,7 +890,7 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
 }
 
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s) {
+                            int split_pages, int max_splits, gemm_in_t* out, cudaStream_t s) {
   if (T <= 0) return;
   launch_pdl(attention_merge_kernel, dim3(T, d.Hq), 128, size_t(max_splits) * sizeof(float), s, ws, gate, token_pos,
              d.Hq, d.D, split_pages * kPageTokens,
@@ -911,18 +911,17 @@ void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t
                         int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s) {
   const size_t smem = size_t(3 * n_experts) * 4 + size_t(32) * n_experts * 2;
   if (smem > 200 * 1024) throw std::invalid_argument("expert sort exceeds shared memory");
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
     QWEN_CUDA(cudaFuncSetAttribute(expert_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    200 * 1024));
-    configured = true;
-  }
+  });
   launch_pdl(expert_sort_kernel, 1, 1024, smem, s, ids, n_assign, n_experts, counts, offsets, perm, inv);
   count_launch();
 }
 
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, const float* weights,
-                        int T, int H, int slots, const float* norm_w, float eps, __nv_bfloat16* hb,
+                        int T, int H, int slots, const float* norm_w, float eps, gemm_in_t* hb,
                         const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
@@ -932,15 +931,15 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
   count_launch();
 }
 
-void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
-                        __nv_bfloat16* dst, cudaStream_t s) {
+void launch_gather_rows(const gemm_in_t* src, int ld, const int32_t* perm, int div, int n, int H,
+                        gemm_in_t* dst, cudaStream_t s) {
   if (n <= 0) return;
   launch_pdl(gather_rows_kernel, n, 128, 0, s, src, ld, perm, div, H, dst);
   count_launch();
 }
 
 void launch_mtp_input(const QMat& embed, const uint32_t* tokens, int T, const float* hidden, const float* w_e,
-                      const float* w_h, float eps, __nv_bfloat16* cat, cudaStream_t s) {
+                      const float* w_h, float eps, gemm_in_t* cat, cudaStream_t s) {
   if (T <= 0) return;
   launch_pdl(mtp_input_kernel, T, 256, size_t(embed.k) * sizeof(float), s, embed, tokens, hidden, w_e, w_h, eps, cat);
   count_launch();

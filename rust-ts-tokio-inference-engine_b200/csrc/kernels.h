@@ -54,7 +54,7 @@ struct GdnPool {
 // GEMM descriptor for the 4-bit affine g64 grouped GEMM.
 enum GemmMode : int {
   kGemmStoreF32 = 0,  // Y[t][n] = acc (split s writes Y + s*split_stride)
-  kGemmGateUp = 1,    // grouped experts: act[p][j] = silu(gate)*up as bf16
+  kGemmGateUp = 1,    // grouped experts: act[p][j] = silu(gate)*up as fp16
   kGemmDown = 2,      // grouped experts: Y[p][n] = acc (fp32)
 };
 
@@ -62,7 +62,7 @@ struct GemmArgs {
   QMat W;
   int mode = kGemmStoreF32;
   int expert_tiles = 0;  // row tiles per expert (grouped modes)
-  const __nv_bfloat16* X = nullptr;
+  const gemm_in_t* X = nullptr;
   int ldx = 0;
   const int32_t* x_row = nullptr;  // grouped: X row of sorted position p = x_row[p] / x_div
   int x_div = 1;
@@ -73,7 +73,7 @@ struct GemmArgs {
   size_t split_stride = 0;
   float* Y = nullptr;
   int ldy = 0;
-  __nv_bfloat16* Yb = nullptr;
+  gemm_in_t* Yb = nullptr;
   int ldyb = 0;
 };
 
@@ -84,15 +84,15 @@ void launch_pack(const SeqDesc* descs, int n_seq, const int32_t* new_pages, int3
 void launch_cow(KvPool kv, const SeqDesc* descs, int n_seq, const int32_t* new_pages,
                 cudaStream_t s);
 void launch_embed_norm(const QMat& embed, const uint32_t* tokens, int T, const float* norm_w,
-                       float eps, float* x, __nv_bfloat16* hb, cudaStream_t s);
+                       float eps, float* x, gemm_in_t* hb, cudaStream_t s);
 void launch_residual_norm(float* x, const float* partial, int splits, size_t split_stride, int T,
-                          int H, const float* norm_w, float eps, __nv_bfloat16* hb,
+                          int H, const float* norm_w, float eps, gemm_in_t* hb,
                           const int32_t* out_token, int rows, float* hidden_f32,
                           cudaStream_t s);
 void launch_qgemm(const GemmArgs& a, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                 size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool,
-                int gdn_index, __nv_bfloat16* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
+                int gdn_index, gemm_in_t* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
                 int sm_count, const int32_t* cand_slots, cudaStream_t s);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
@@ -103,10 +103,10 @@ void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t
                         int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s);
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
-                        float eps, __nv_bfloat16* hb, const int32_t* out_token, int rows,
+                        float eps, gemm_in_t* hb, const int32_t* out_token, int rows,
                         float* hidden_f32, cudaStream_t s);
 void launch_mtp_input(const QMat& embed, const uint32_t* tokens, int T, const float* hidden, const float* w_e,
-                      const float* w_h, float eps, __nv_bfloat16* cat, cudaStream_t s);
+                      const float* w_h, float eps, gemm_in_t* cat, cudaStream_t s);
 void launch_accept(const SeqDesc* descs, int n, const int32_t* cu_seqlens, const uint32_t* tokens,
                    const uint32_t* sampled, const uint32_t* eos, int n_eos, int ctx, int32_t* acc, uint32_t* emitted,
                    int emit_stride, uint32_t* n_emitted, cudaStream_t s);
@@ -120,14 +120,14 @@ void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int positi
 // Expert parallelism (ep.cu): stage packing, local row plan / gather, result
 // return. Per-peer destination tables; flag tables / wait flags non-null for
 // the direct NVLink transport (null with NCCL).
-void launch_ep_pack(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, const int32_t* counts,
+void launch_ep_pack(const gemm_in_t* src, int ld, const int32_t* perm, int div, const int32_t* counts,
                     const int32_t* offsets, uint8_t* const* dst,
                     int world, int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                     uint32_t* done, cudaStream_t s);
 void launch_ep_plan_gather(const uint8_t* const* srcs, int world, int rank, int per_rank, int hdr_ints, int E,
-                           const int32_t* counts, const int32_t* offsets, const __nv_bfloat16* xsrc, int ld,
+                           const int32_t* counts, const int32_t* offsets, const gemm_in_t* xsrc, int ld,
                            const int32_t* perm, int div, int32_t* goff,
-                           int32_t* seg, int32_t* n_rows, __nv_bfloat16* xloc, int32_t* origin, int cap, int H,
+                           int32_t* seg, int32_t* n_rows, gemm_in_t* xloc, int32_t* origin, int cap, int H,
                            int max_rows, uint32_t* err, const uint32_t* wait_flags, uint32_t epoch, int sm_count,
                            cudaStream_t s);
 void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n_rows, float* const* rdst,
@@ -136,7 +136,7 @@ void launch_ep_return(const float* yloc, const int32_t* origin, const int32_t* n
 void launch_ep_return_unpack(const float* const* rsrcs, const int32_t* offsets, float* y_sorted, int world,
                              int per_rank, int H, int max_rows, const uint32_t* wait_flags, uint32_t epoch,
                              uint32_t* err, int sm_count, cudaStream_t s);
-void launch_gather_rows(const __nv_bfloat16* src, int ld, const int32_t* perm, int div, int n, int H,
-                        __nv_bfloat16* dst, cudaStream_t s);
+void launch_gather_rows(const gemm_in_t* src, int ld, const int32_t* perm, int div, int n, int H,
+                        gemm_in_t* dst, cudaStream_t s);
 
 }  // namespace qwen

@@ -75,6 +75,10 @@ struct WeightStore {
   size_t bytes = 0;
   std::map<std::string, TensorLoc> index;
   std::map<std::string, std::pair<int, int>> quant;  // rs_qwen_quant overrides
+  // rs_qwen_forward's private device session for this store, with the
+  // config bytes it was made for (rebuilt when they change; dies with the store)
+  std::shared_ptr<void> forward_session;
+  std::vector<uint8_t> forward_key;
   ~WeightStore();
   void synthesize(const rs_qwen_config& c, uint64_t seed, bool with_mtp);
   void export_bytes(const std::string& name, size_t offset, uint8_t* out, size_t count) const;

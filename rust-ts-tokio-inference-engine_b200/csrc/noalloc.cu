@@ -87,7 +87,7 @@ __global__ void reduce_partials_kernel(const float* __restrict__ part, int split
 
 size_t noalloc_scratch_bytes() { return kScratchBytes; }
 
-int project_noalloc(const QMat& W, int max_splits, const __nv_bfloat16* x, int T, float* y, int sm_count,
+int project_noalloc(const QMat& W, int max_splits, const gemm_in_t* x, int T, float* y, int sm_count,
                     cudaStream_t s, char* error, size_t capacity) {
   if (!x || !y || T <= 0 || size_t(T) > kPartialFloats) {
     fail(error, capacity, "no-alloc projection: null buffer or token count outside [1, %zu]", kPartialFloats);

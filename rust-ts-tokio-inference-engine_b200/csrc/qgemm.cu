@@ -1,4 +1,4 @@
-// 4-bit affine (group 64, bf16 scale/bias) grouped GEMM: Y = X * deq(W)^T.
+// 4-bit affine (group 64 scale/bias) grouped GEMM on CUDA cores: Y = X * deq(W)^T.
 //
 // CUDA-core implementation: one CTA per 128-row weight tile; each thread owns
 // one weight row, dequantizes its 64-column slice of each tile in registers
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
         if (i < nt) {
           const int p = tb + i;
           const int xr = a.x_row ? a.x_row[p] / a.x_div : p;
-          v = __bfloat162float(a.X[size_t(xr) * a.ldx + c * kTileK + k]);
+          v = __half2float(a.X[size_t(xr) * a.ldx + c * kTileK + k]);
         }
         xs[i][k] = v;
       }
@@ -60,8 +60,8 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
       const uint8_t* tile = a.W.tile(row_tile, c);
       const uint4* pk = reinterpret_cast<const uint4*>(tile + r * 32);
       const uint4 w0 = pk[0], w1 = pk[1];
-      const float sc = bf16_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
-      const float bi = bf16_bits_to_float(
+      const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+      const float bi = half_bits_to_float(
           reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
       const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
       float w[kTileK];
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
         const int j = blockIdx.x * 64 + r;
         for (int i = 0; i < nt; ++i) {
           const float gv = ex[r][i], uv = ex[r + 64][i];
-          a.Yb[size_t(tb + i) * a.ldyb + j] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
+          a.Yb[size_t(tb + i) * a.ldyb + j] = to_gemm_in(gv / (1.f + __expf(-gv)) * uv);
         }
       }
     }

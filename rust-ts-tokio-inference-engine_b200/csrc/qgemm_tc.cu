@@ -1,4 +1,5 @@
-// tcgen05 grouped GEMM over 4-bit affine (group 64, bf16 scale/bias) weights.
+// tcgen05 grouped GEMM over 4-bit affine (group 64 scale/bias) weights, IEEE
+// half operands (dequantised weights in TMEM, activations in shared memory).
 //
 //   D[w_row, token] = sum_k deq(W)[w_row, k] * X[token, k]
 //
@@ -22,10 +23,10 @@
 //           separate commits, so units amortise the fixed costs;
 //   warps 3-14 dequantise (three warpgroups taking whole units round-robin):
 //           each thread owns one weight row, turns its 64 nibbles per chunk
-//           into 32 bf16x2 words (scale*q + bias, one bf16 rounding) and stores
+//           into 32 f16x2 words (scale*q + bias, one fp16 rounding) and stores
 //           them into TMEM with tcgen05.st (the A operand);
 //   warps 15-18 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
-//           partial store / SwiGLU (bf16) / fp32 store.
+//           partial store / SwiGLU (fp16) / fp32 store.
 // The dequantised weights never touch shared memory. A unit's TMEM A stages
 // are released together by its commit. Units never straddle work items (split-K ranges are
 // multiples of U). Every mbarrier wait is bounded (~1 s); on expiry the kernel
@@ -52,16 +53,17 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 12;       // shared-memory ring = TMEM A stages (32 columns each)
 constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
 constexpr int kTmemCols = 512;
-// Two bf16 (q0*s+b, q1*s+b) packed low/high from the nibble pair (q0, q1) at
-// bits [0,4) and [16,20) of `w`: one lop3 places them as 128+q in bf16
-// ((w & 0x000F000F) | 0x43004300), add.rn subtracts 128 exactly and fma.rn
-// rounds scale*q + bias once. `mask` / `magic` / `neg128` live in registers.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t w, uint32_t mask, uint32_t magic, uint32_t neg128,
+// Two fp16 (q0*s+b, q1*s+b) packed low/high from the nibble pair (q0, q1) at
+// bits [0,4) and [16,20) of `w`: one lop3 places them as 1024+q in fp16
+// ((w & 0x000F000F) | 0x64006400; the fp16 spacing at 1024 is 1), add.rn
+// subtracts 1024 exactly and fma.rn rounds scale*q + bias once to 11
+// significant bits. `mask` / `magic` / `neg1024` live in registers.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t w, uint32_t mask, uint32_t magic, uint32_t neg1024,
                                              uint32_t s2, uint32_t b2) {
   uint32_t x, q, y;
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(x) : "r"(w), "r"(mask), "r"(magic));
-  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(x), "r"(neg128));
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(q), "r"(s2), "r"(b2));
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(q) : "r"(x), "r"(neg1024));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(q), "r"(s2), "r"(b2));
   return y;
 }
 
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer (converged warp, elected lane issues) ----------------
     int st = 0, bs = 0;
     uint32_t ph = 0, bph = 0, acc_it = 0;
-    const uint32_t idesc = idesc_bf16(box);
+    const uint32_t idesc = idesc_f16(box);
     bool ok = true;
     for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
       const Work w = item_at(a, i, goff, act);
@@ -260,9 +262,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const uint32_t ring_w_s = smem_u32(ring_w);
-    // dequant constants in registers (lop3 and the bf16x2 ops take no immediates)
-    uint32_t k_mask = 0x000F000Fu, k_magic = 0x43004300u, k_neg128 = 0xC300C300u;
-    asm volatile("" : "+r"(k_mask), "+r"(k_magic), "+r"(k_neg128));
+    // dequant constants in registers (lop3 and the f16x2 ops take no immediates)
+    uint32_t k_mask = 0x000F000Fu, k_magic = 0x64006400u, k_neg1024 = 0xE400E400u;
+    asm volatile("" : "+r"(k_mask), "+r"(k_magic), "+r"(k_neg1024));
     // This warpgroup takes units n = wg, wg + 3, ... of the CTA's unit
     // sequence. NS, kWSlots and NSB are multiples of 3, so its TMEM slot,
     // weight slot and released activation slot (of unit n - NS) each advance
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t v[32];
 #define QWEN_DEQ_WORD(WD, W)                                                            \
   _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
-      deq_pair((W) >> (4 * j), k_mask, k_magic, k_neg128, s2, b2);
+      deq_pair((W) >> (4 * j), k_mask, k_magic, k_neg1024, s2, b2);
             QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
             QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
 #undef QWEN_DEQ_WORD
@@ -360,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 8; ++j)
                 if (j0 + j < nvalid) {
                   const float gv = __uint_as_float(v[j]), uv = xchg[r * 9 + j];
-                  a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = __float2bfloat16_rn(gv / (1.f + __expf(-gv)) * uv);
+                  a.Yb[size_t(tb + j0 + j) * a.ldyb + jj] = to_gemm_in(gv / (1.f + __expf(-gv)) * uv);
                 }
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -424,11 +426,10 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   if (a.b_stages % a.unit || a.b_stages < a.stages || (a.b_stages / a.unit) % kDequantGroups)
     throw std::logic_error("GEMM activation ring geometry");
   const size_t smem = qgemm_tc_smem(a.box_rows, a.stages, a.unit);
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
     QWEN_CUDA(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    configured = true;
-  }
+  });
   const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
   const int grid = std::max(1, std::min(items, sm_count));
   if (smem > 227 * 1024) throw std::invalid_argument("tcgen05 GEMM shared memory above 227 KB");
@@ -463,7 +464,7 @@ CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows) {
   const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
   const cuuint32_t box[2] = {cuuint32_t(kTileK), cuuint32_t(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
@@ -479,7 +480,7 @@ CUtensorMap make_act_map3d(const void* base, int rows, int k, int box_rows, int 
   const cuuint64_t strides[2] = {cuuint64_t(k) * 2, cuuint64_t(kTileK) * 2};
   const cuuint32_t box[3] = {cuuint32_t(kTileK), cuuint32_t(box_rows), cuuint32_t(unit)};
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D activations) failed: " + std::to_string(int(r)));

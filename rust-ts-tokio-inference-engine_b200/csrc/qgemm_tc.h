@@ -22,12 +22,12 @@ struct TcArgs {
   int unit = 1;        // chunks per MMA unit (set by the launcher)
   float* Y = nullptr;
   int ldy = 0;
-  __nv_bfloat16* Yb = nullptr;
+  gemm_in_t* Yb = nullptr;  // kGemmGateUp output (the down GEMM input)
   int ldyb = 0;
   uint32_t* err = nullptr;
 };
 
-// Tensor map over a row-major bf16 activation matrix [rows, k] with a
+// Tensor map over a row-major fp16 activation matrix [rows, k] with a
 // (64 columns x box_rows) box and 128-byte swizzle (the UMMA K-major layout).
 CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows);
 // The same matrix viewed as [k/64 chunks][rows][64]: one box brings `unit`
@@ -43,7 +43,7 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
                         const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
                         cudaStream_t s);
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int split_pages, int max_splits, __nv_bfloat16* out, cudaStream_t s);
+                            int split_pages, int max_splits, gemm_in_t* out, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
 size_t qgemm_tc_smem(int box_rows, int stages, int unit);
 int qgemm_tc_stages(int box_rows);

@@ -166,7 +166,8 @@ struct Session {
   bool mtp_on = false;
   std::unique_ptr<StateTable<DraftVersion>> drafts;
   KvPool mkv;
-  DevBuf<__nv_bfloat16> mkv_mem, mcat;
+  DevBuf<__nv_bfloat16> mkv_mem;
+  DevBuf<gemm_in_t> mcat;
   CUtensorMap mkv_map;
   DevBuf<int32_t> mbt;
   DevBuf<float> mhidden;
@@ -176,7 +177,7 @@ struct Session {
   size_t draft_residents() const { return drafts ? drafts->residents() : 0; }
   uint64_t draft_bytes() const { return drafts ? drafts->bytes() : 0; }
   int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
-  DevBuf<__nv_bfloat16> hb, hb2, act, xperm, hb_out;
+  DevBuf<gemm_in_t> hb, hb2, act, xperm, hb_out;  // projection inputs (fp16)
   int sm_count = 148;
   int cur_layer = 0;
   bool simple_gemm = false;  // debugging aid: CUDA-core GEMM instead of tcgen05
@@ -195,7 +196,7 @@ struct Session {
   static int box_for(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
 
   // Dense Y[t][n] (+ split partials) = X[t] . deq(W)[n]; returns the split count.
-  int dense(const QMat& W, const __nv_bfloat16* X, int rows_cap, int T, float* Y, int ldy,
+  int dense(const QMat& W, const gemm_in_t* X, int rows_cap, int T, float* Y, int ldy,
             size_t split_stride, int max_splits, cudaStream_t s) {
     if (simple_gemm) {
       GemmArgs g;
@@ -292,7 +293,7 @@ struct Session {
     std::vector<void*> peer_windows;      // p2p: opened peer mappings (nullptr for this rank)
     DevBuf<uint8_t> send, recv;           // nccl: per-peer stages
     DevBuf<float> rsend, rrecv, yloc;
-    DevBuf<__nv_bfloat16> xloc, actloc;
+    DevBuf<gemm_in_t> xloc, actloc;
     DevBuf<int32_t> goff, seg, origin, n_rows;
     DevBuf<uint32_t> done;                // last-CTA counters (pack, return)
     // device pointer tables, world entries each: where this rank writes for
@@ -330,8 +331,10 @@ struct Session {
     }
   }
 
+  // step_tokens: per-step token budget that sizes the scratch (0: the
+  // QWEN_STEP_TOKENS environment variable, else 4096).
   void init(WeightStore* w, int gpu, const rs_qwen_config& c, const rs_qwen_layer* layers,
-            size_t count, size_t n_slots, uint64_t bytes) {
+            size_t count, size_t n_slots, uint64_t bytes, int step_tokens = 0) {
     if (gpu != 1) throw std::invalid_argument("device session requires gpu=1: this backend has no CPU path");
     if (!w || !w->ready) throw std::invalid_argument("weight store is empty");
     store = w;
@@ -383,7 +386,7 @@ struct Session {
 
     // scratch sizing
     const char* env = std::getenv("QWEN_STEP_TOKENS");
-    max_tokens = env ? std::max(1, atoi(env)) : 4096;
+    max_tokens = step_tokens > 0 ? step_tokens : env ? std::max(1, atoi(env)) : 4096;
     max_rows = std::min(max_tokens, 1024);
     max_seqs = max_tokens;
     bt_stride = (d.ctx + kPageTokens - 1) / kPageTokens;
@@ -862,13 +865,121 @@ struct Session {
     stage(17);  // FinalProjection
     if (keep_hidden)  // post-norm hidden rows of every token (fp32)
       launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb.p, nullptr, 0, hidden_stage.p, s);
-    // compact bf16 rows of the output tokens for the vocabulary projection
+    // compact fp16 rows of the output tokens for the vocabulary projection
     launch_residual_norm(x.p, nullptr, 0, 0, T, d.H, m.final_norm, d.eps, hb_out.p, out_token.p, R, nullptr, s);
     logits.ensure(size_t(R) * d.V);
     dense(m.lm_head, hb_out.p, max_rows, R, logits.p, d.V, size_t(R) * d.V, 1, s);
     stage(18);  // StateValidation (finite check + greedy selection)
     launch_argmax(logits.p, R, d.V, sampled.p, err.p, argmax_part.p, argmax_done.p, s);
     launches += 1;
+  }
+
+  // ------------------------------------------------- reference-layout state
+  // Writes version `id` in the layout of native/qwen_model.inc:268-271 (per
+  // layer: DeltaNet conv history then recurrent state; attention K then V as
+  // [kv][context][d]; all fp32, positions past the version's length zero).
+  void export_snapshot(const StateId& id, float* output, size_t count) {
+    const Version& v = table->get(id);
+    if (count != d.state_count()) throw std::invalid_argument("snapshot capacity");
+    set_device();
+    QWEN_CUDA(cudaStreamSynchronize(stream));
+    size_t off = 0;
+    const size_t slot = id.slot, pos = id.position;
+    std::vector<__nv_bfloat16> page(kv.page_elems());
+    for (int li = 0; li < d.L; ++li) {
+      const LayerDev& ly = store->model.layers[li];
+      if (ly.mixer == 0) {
+        const size_t cl = gdn.conv_elems, sl = gdn.state_elems;
+        QWEN_CUDA(cudaMemcpy(output + off, gdn.conv + (slot * d.n_gdn + ly.type_index) * cl, cl * 4,
+                             cudaMemcpyDeviceToHost));
+        off += cl;
+        QWEN_CUDA(cudaMemcpy(output + off, gdn.state + (slot * d.n_gdn + ly.type_index) * sl, sl * 4,
+                             cudaMemcpyDeviceToHost));
+        off += sl;
+      } else {
+        const size_t per = size_t(d.Hkv) * d.ctx * d.D;
+        std::fill(output + off, output + off + 2 * per, 0.f);
+        for (size_t pi = 0; pi < v.pages.size(); ++pi) {
+          QWEN_CUDA(cudaMemcpy(page.data(), kv.page(ly.type_index, v.pages[pi]), page.size() * 2,
+                               cudaMemcpyDeviceToHost));
+          for (int kvsel = 0; kvsel < 2; ++kvsel)
+            for (int g = 0; g < d.Hkv; ++g)
+              for (int o = 0; o < kPageTokens; ++o) {
+                const size_t p = pi * kPageTokens + o;
+                if (p >= pos) continue;
+                const __nv_bfloat16* src = page.data() + ((size_t(kvsel) * d.Hkv + g) * kPageTokens + o) * d.D;
+                float* dst = output + off + kvsel * per + (size_t(g) * d.ctx + p) * d.D;
+                for (int i = 0; i < d.D; ++i) dst[i] = __bfloat162float(src[i]);
+              }
+        }
+        off += 2 * per;
+      }
+    }
+    if (off != count) throw std::runtime_error("snapshot accounting");
+    exports += count * 4;
+  }
+
+  // The inverse: a new version at `position` holding a reference-layout state
+  // (rs_qwen_forward's old_state). K/V rows are stored in the bf16 cache.
+  StateId import_snapshot(const float* flat, size_t position) {
+    if (!position || position > size_t(d.ctx)) throw std::invalid_argument("imported state position");
+    set_device();
+    const int n_pages = d.n_attn > 0 ? int((position + kPageTokens - 1) / kPageTokens) : 0;
+    if (n_pages > int(free_pages.size())) throw std::runtime_error("KV page pool exhausted");
+    if (table->residents() + draft_residents() + 1 > slots) throw std::runtime_error("combined resident budget exhausted");
+    StateId id = table->reserve(position, version_bytes(n_pages, 0));
+    Version v;
+    for (int j = 0; j < n_pages; ++j) {
+      const int32_t p = free_pages.back();
+      free_pages.pop_back();
+      page_ref[p] = 1;
+      page_filled[p] = uint8_t(std::min<size_t>(kPageTokens, position - size_t(j) * kPageTokens));
+      v.pages.push_back(p);
+    }
+    try {
+      QWEN_CUDA(cudaStreamSynchronize(stream));
+      if (n_pages)
+        QWEN_CUDA(cudaMemcpy(block_table.p + id.slot * size_t(bt_stride), v.pages.data(), size_t(n_pages) * 4,
+                             cudaMemcpyHostToDevice));
+      std::vector<uint16_t> page(kv.page_elems());
+      size_t off = 0;
+      for (int li = 0; li < d.L; ++li) {
+        const LayerDev& ly = store->model.layers[li];
+        if (ly.mixer == 0) {
+          const size_t cl = gdn.conv_elems, sl = gdn.state_elems;
+          QWEN_CUDA(cudaMemcpy(gdn.conv + (id.slot * d.n_gdn + ly.type_index) * cl, flat + off, cl * 4,
+                               cudaMemcpyHostToDevice));
+          off += cl;
+          QWEN_CUDA(cudaMemcpy(gdn.state + (id.slot * d.n_gdn + ly.type_index) * sl, flat + off, sl * 4,
+                               cudaMemcpyHostToDevice));
+          off += sl;
+        } else {
+          const size_t per = size_t(d.Hkv) * d.ctx * d.D;
+          for (int pi = 0; pi < n_pages; ++pi) {
+            std::fill(page.begin(), page.end(), uint16_t(0));
+            for (int kvsel = 0; kvsel < 2; ++kvsel)
+              for (int g = 0; g < d.Hkv; ++g)
+                for (int o = 0; o < kPageTokens; ++o) {
+                  const size_t p = size_t(pi) * kPageTokens + o;
+                  if (p >= position) continue;
+                  const float* src = flat + off + kvsel * per + (size_t(g) * d.ctx + p) * d.D;
+                  uint16_t* dst = page.data() + ((size_t(kvsel) * d.Hkv + g) * kPageTokens + o) * d.D;
+                  for (int i = 0; i < d.D; ++i) dst[i] = float_to_bf16_bits(src[i]);
+                }
+            QWEN_CUDA(cudaMemcpy(kv.page(ly.type_index, v.pages[pi]), page.data(), page.size() * 2,
+                                 cudaMemcpyHostToDevice));
+          }
+          off += 2 * per;
+        }
+      }
+      if (off != d.state_count()) throw std::runtime_error("imported state accounting");
+    } catch (...) {
+      unref_pages(v.pages);
+      table->rollback(id);
+      throw;
+    }
+    table->publish(id, std::move(v));
+    return id;
   }
 
   // ------------------------------------------------------------ MTP draft head
@@ -1336,6 +1447,32 @@ Session* S(void* h) {
   return static_cast<Session*>(h);
 }
 
+// rs_qwen_forward's session: two state slots (the imported parent, then the
+// child that consumes it in place), KV pages for one full context, scratch
+// for one chunk. Kept in the weight store and remade when the config changes.
+Session& forward_session(WeightStore* w, const rs_qwen_config& c, const rs_qwen_layer* layers, size_t count) {
+  const uint8_t* key = reinterpret_cast<const uint8_t*>(&c);
+  if (w->forward_session && w->forward_key.size() == sizeof(c) &&
+      std::memcmp(w->forward_key.data(), key, sizeof(c)) == 0)
+    return *static_cast<Session*>(w->forward_session.get());
+  w->forward_session.reset();
+  w->forward_key.clear();
+  const Dims d = Dims::from(c);
+  const uint64_t gdn_slot = uint64_t(d.n_gdn) * (size_t(d.hv) * d.dv * d.dk + size_t(d.conv - 1) * d.cd) * 4;
+  const uint64_t page = uint64_t(d.n_attn) * 2 * d.Hkv * kPageTokens * d.D * 2;
+  const uint64_t pages = d.ctx > 0 ? uint64_t(d.ctx + kPageTokens - 1) / kPageTokens + 2 : 0;
+  auto sess = std::make_unique<Session>();
+  sess->init(w, 1, c, layers, count, 2, 2 * gdn_slot + pages * page + 1, std::max(1, c.chunk));
+  w->forward_session = std::shared_ptr<void>(sess.release(), [](void* p) {
+    auto* ss = static_cast<Session*>(p);
+    cudaSetDevice(ss->device);
+    cudaStreamSynchronize(ss->stream);
+    delete ss;
+  });
+  w->forward_key.assign(key, key + sizeof(c));
+  return *static_cast<Session*>(w->forward_session.get());
+}
+
 }  // namespace
 
 // ----------------------------------------------------------------- C ABI --
@@ -1375,6 +1512,110 @@ int rs_qwen_quant(void* store, const char* module, int group, int bits, char* er
     static_cast<WeightStore*>(store)->quant[module] = {group, bits};
   });
 }
+
+// One-shot forward of `count` tokens at `offset` from a reference-layout state
+// (native/qwen_model.inc:278-373 semantics): old_state in, new_state and the
+// last row's logits out. Runs the same ragged CUDA step as the device session.
+int rs_qwen_forward(void* store, int gpu, const rs_qwen_config* config, const rs_qwen_layer* layers,
+                    size_t layer_count, const uint32_t* tokens, size_t count, size_t offset, const float* old_state,
+                    size_t old_count, float* new_state, size_t new_count, float* logits, size_t logits_count,
+                    int projection_checks, const uint32_t* projection_outputs, size_t projection_output_count,
+                    float* trace, size_t trace_count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    if (!store || !config || !layers || !tokens || !new_state || !logits)
+      throw std::invalid_argument("invalid model descriptor");
+    const rs_qwen_config& c = *config;
+    if (c.chunk <= 0 || c.chunk > 8 || c.context <= 0 || count == 0 || count > size_t(c.chunk) ||
+        offset + count > size_t(c.context) || logits_count != size_t(c.vocab))
+      throw std::invalid_argument("model geometry/capacity");
+    if (gpu != 1) throw std::invalid_argument("rs_qwen_forward: the CUDA backend has no CPU path (gpu must be 1)");
+    if (projection_checks || projection_outputs || projection_output_count || trace || trace_count)
+      throw std::invalid_argument("rs_qwen_forward: projection checks and layer traces are MLX diagnostics the "
+                                  "CUDA backend does not provide");
+    const Dims d = Dims::from(c);
+    if (new_count != d.state_count() || (offset ? (old_count != d.state_count() || !old_state) : old_count != 0))
+      throw std::invalid_argument("model state length");
+    for (size_t i = 0; i < count; ++i)
+      if (tokens[i] >= uint32_t(c.vocab)) throw std::invalid_argument("token outside vocabulary");
+    auto* w = static_cast<WeightStore*>(store);
+    if (!w->ready) throw std::invalid_argument("weight store is empty");
+    int caller_device = 0;
+    QWEN_CUDA(cudaGetDevice(&caller_device));
+    try {
+      Session& s = forward_session(w, c, layers, layer_count);
+      StateId parent{};
+      const bool have = offset > 0;
+      if (have) parent = s.import_snapshot(old_state, offset);
+      Session::SeqIn in{have ? &parent : nullptr, uint32_t(offset), uint32_t(count), tokens};
+      StateId out{};
+      s.step({in}, RS_QWEN_RAGGED_LOGITS | (have ? RS_QWEN_RAGGED_CONSUME : 0u), &out, nullptr, logits);
+      try {
+        s.export_snapshot(out, new_state, new_count);
+      } catch (...) {
+        std::vector<int32_t> pages = s.table->get(out).pages;
+        s.table->release(out);
+        s.unref_pages(pages);
+        throw;
+      }
+      std::vector<int32_t> pages = s.table->get(out).pages;
+      s.table->release(out);
+      s.unref_pages(pages);
+    } catch (...) {
+      w->forward_session.reset();  // a failed call leaves no half-imported state behind
+      w->forward_key.clear();
+      cudaSetDevice(caller_device);
+      throw;
+    }
+    QWEN_CUDA(cudaSetDevice(caller_device));
+  });
+}
+
+// The reference's generic MLX graph builder (native/mlx_bridge.h:8-43), used by
+// its in-process MLX executor (src/serving/native_mlx.rs). This backend runs
+// no MLX graphs: each entry point reports that with the ABI's error
+// convention, so a caller built against the full surface links and fails
+// cleanly at run time.
+static const char kNoGraph[] = "the MLX graph interface is not provided by the CUDA backend (no MLX graphs run here)";
+
+void* rs_mlx_create(int gpu, char* error, size_t capacity) {
+  (void)gpu;
+  report(error, capacity, kNoGraph);
+  return nullptr;
+}
+void rs_mlx_destroy(void* graph) { (void)graph; }
+int rs_mlx_input(void* graph, int dtype, const void* data, const int32_t* shape, size_t rank, char* error,
+                 size_t capacity) {
+  (void)graph, (void)dtype, (void)data, (void)shape, (void)rank;
+  report(error, capacity, kNoGraph);
+  return -1;
+}
+int rs_mlx_op(void* graph, int op, const uint32_t* inputs, size_t count, int group, float epsilon, char* error,
+              size_t capacity) {
+  (void)graph, (void)op, (void)inputs, (void)count, (void)group, (void)epsilon;
+  report(error, capacity, kNoGraph);
+  return -1;
+}
+int rs_mlx_finish(void* graph, uint32_t output, void* data, size_t elements, char* error, size_t capacity) {
+  (void)graph, (void)output, (void)data, (void)elements;
+  report(error, capacity, kNoGraph);
+  return -1;
+}
+int rs_mlx_kernel(void* graph, int op, const uint32_t* inputs, size_t count, const int32_t* ints, size_t ni,
+                  const float* floats, size_t nf, char* error, size_t capacity) {
+  (void)graph, (void)op, (void)inputs, (void)count, (void)ints, (void)ni, (void)floats, (void)nf;
+  report(error, capacity, kNoGraph);
+  return -1;
+}
+int rs_mlx_parameter(void* graph, void* store, const char* name, const int32_t* shape, size_t rank, int dtype,
+                     char* error, size_t capacity) {
+  (void)graph, (void)store, (void)name, (void)shape, (void)rank, (void)dtype;
+  report(error, capacity, kNoGraph);
+  return -1;
+}
+// The reference clears MLX's per-thread streams when an executor thread exits
+// (native/mlx_bridge.cpp:96); sessions here own their CUDA streams, so there is
+// nothing per-thread to release.
+void rs_mlx_cleanup(void) {}
 
 int rs_mlx_weight_bytes(void* store, const char* name, const int32_t* shape, size_t rank, int dtype,
                         size_t offset, uint8_t* output, size_t count, char* error, size_t capacity) {
@@ -1522,45 +1763,7 @@ int rs_qwen_device_snapshot(void* session, const StateId* id, float* output, siz
   return checked(error, capacity, [&] {
     Session* s = S(session);
     if (!id || !output) throw std::invalid_argument("snapshot descriptor");
-    const Version& v = s->table->get(*id);
-    const Dims& d = s->d;
-    if (count != d.state_count()) throw std::invalid_argument("snapshot capacity");
-    s->set_device();
-    QWEN_CUDA(cudaStreamSynchronize(s->stream));
-    size_t off = 0;
-    const size_t slot = id->slot, pos = id->position;
-    std::vector<__nv_bfloat16> page(s->kv.page_elems());
-    for (int li = 0; li < d.L; ++li) {
-      const LayerDev& ly = s->store->model.layers[li];
-      if (ly.mixer == 0) {
-        const size_t cl = s->gdn.conv_elems, sl = s->gdn.state_elems;
-        QWEN_CUDA(cudaMemcpy(output + off, s->gdn.conv + (slot * d.n_gdn + ly.type_index) * cl, cl * 4,
-                             cudaMemcpyDeviceToHost));
-        off += cl;
-        QWEN_CUDA(cudaMemcpy(output + off, s->gdn.state + (slot * d.n_gdn + ly.type_index) * sl, sl * 4,
-                             cudaMemcpyDeviceToHost));
-        off += sl;
-      } else {
-        const size_t per = size_t(d.Hkv) * d.ctx * d.D;
-        std::fill(output + off, output + off + 2 * per, 0.f);
-        for (size_t pi = 0; pi < v.pages.size(); ++pi) {
-          QWEN_CUDA(cudaMemcpy(page.data(), s->kv.page(ly.type_index, v.pages[pi]), page.size() * 2,
-                               cudaMemcpyDeviceToHost));
-          for (int kvsel = 0; kvsel < 2; ++kvsel)
-            for (int g = 0; g < d.Hkv; ++g)
-              for (int o = 0; o < kPageTokens; ++o) {
-                const size_t p = pi * kPageTokens + o;
-                if (p >= pos) continue;
-                const __nv_bfloat16* src = page.data() + ((size_t(kvsel) * d.Hkv + g) * kPageTokens + o) * d.D;
-                float* dst = output + off + kvsel * per + (size_t(g) * d.ctx + p) * d.D;
-                for (int i = 0; i < d.D; ++i) dst[i] = __bfloat162float(src[i]);
-              }
-        }
-        off += 2 * per;
-      }
-    }
-    if (off != count) throw std::runtime_error("snapshot accounting");
-    s->exports += count * 4;
+    s->export_snapshot(*id, output, count);
   });
 }
 
@@ -1806,7 +2009,7 @@ int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, s
     if (which < 0 || which > 3) throw std::invalid_argument("debug gemm matrix");
     if (y_count != T * size_t(W.rows)) throw std::invalid_argument("debug gemm output capacity");
     s->set_device();
-    __nv_bfloat16* xin = which == 1 ? s->hb2.p : which == 3 ? s->hb_out.p : s->hb.p;
+    gemm_in_t* xin = which == 1 ? s->hb2.p : which == 3 ? s->hb_out.p : s->hb.p;
     if (which == 3 && T > size_t(s->max_rows)) throw std::invalid_argument("debug gemm rows");
     QWEN_CUDA(cudaMemcpyAsync(xin, x, T * W.k * 2, cudaMemcpyHostToDevice, s->stream));
     QWEN_CUDA(cudaMemsetAsync(s->err.p, 0, 4, s->stream));
@@ -1861,14 +2064,25 @@ int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_d
     report(error, capacity, "no-alloc projection: output capacity must be T x rows of the selected matrix");
     return -1;
   }
-  const cudaError_t rc = cudaSetDevice(s->device);
+  // run on the session's device and give the caller back its own current device
+  int caller_device = -1;
+  cudaError_t rc = cudaGetDevice(&caller_device);
+  if (rc == cudaSuccess) rc = cudaSetDevice(s->device);
   if (rc != cudaSuccess) {
     report(error, capacity, cudaGetErrorString(rc));
     return -1;
   }
-  return project_noalloc(W, which == 3 ? 1 : kMaxSplits, static_cast<const __nv_bfloat16*>(x_device), int(T),
-                         y_device, s->sm_count, stream ? static_cast<cudaStream_t>(stream) : s->stream, error,
-                         capacity);
+  const int status = project_noalloc(W, which == 3 ? 1 : kMaxSplits, static_cast<const gemm_in_t*>(x_device),
+                                     int(T), y_device, s->sm_count,
+                                     stream ? static_cast<cudaStream_t>(stream) : s->stream, error, capacity);
+  if (caller_device != s->device) {
+    rc = cudaSetDevice(caller_device);
+    if (rc != cudaSuccess && status == 0) {
+      report(error, capacity, cudaGetErrorString(rc));
+      return -1;
+    }
+  }
+  return status;
 }
 
 int rs_qwen_ep_unique_id(uint8_t* out, size_t out_bytes, char* error, size_t capacity) {

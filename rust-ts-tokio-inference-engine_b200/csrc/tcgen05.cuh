@@ -123,9 +123,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A/B bf16, D f32, both K-major, M=128.
-__device__ __forceinline__ uint32_t idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+// Instruction descriptor: kind::f16, A and B IEEE half (type code 0 in bits
+// 7-9 and 10-12), D f32 (bits 4-5 = 1), both K-major, N in bits 17-22 (>>3),
+// M = 128 in bits 24-28 (>>4).
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  return (1u << 4) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,

@@ -6,6 +6,8 @@
 // affine with bf16 scale and bias (scale = (max-min)/15, bias = min). Only
 // integer arithmetic and single correctly-rounded float operations are used,
 // so a CPU restatement reproduces the bytes exactly (the test oracle does).
+// The tiles hold each bf16 scale and bias as the fp16 of the same value (the
+// GEMM's operand type); a value fp16 cannot hold exactly raises `inexact`.
 #include <cstring>
 #include <stdexcept>
 
@@ -58,7 +60,7 @@ __device__ inline int device_row(int mode, int row, int row_offset, int per_expe
 // One thread per (logical row, 64-column group).
 __global__ void synth_qmat_kernel(uint8_t* tiles, int k_chunks, long long rows, int cols,
                                   uint64_t key, float k, int mode, int row_offset,
-                                  int per_expert) {
+                                  int per_expert, uint32_t* inexact) {
   long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   int groups = cols / 64;
   if (idx >= rows * groups) return;
@@ -88,8 +90,10 @@ __global__ void synth_qmat_kernel(uint8_t* tiles, int k_chunks, long long rows, 
   uint4* dst = reinterpret_cast<uint4*>(tile + r * 32);
   dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
   dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-  reinterpret_cast<uint16_t*>(tile + kTilePackedBytes)[r] = sb;
-  reinterpret_cast<uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r] = bb;
+  uint16_t sh = 0, bh = 0;
+  if (!bf16_to_half_bits(sb, &sh) || !bf16_to_half_bits(bb, &bh)) atomicAdd(inexact, 1u);
+  reinterpret_cast<uint16_t*>(tile + kTilePackedBytes)[r] = sh;
+  reinterpret_cast<uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r] = bh;
 }
 
 __global__ void synth_vector_kernel(float* out, size_t n, uint64_t key, float k, int gain) {
@@ -128,6 +132,7 @@ struct PendingGen {  // one logical tensor written into a fused matrix
 }  // namespace
 
 WeightStore::~WeightStore() {
+  forward_session.reset();  // rs_qwen_forward's session reads this store's tensors
   if (base) {
     int prev = 0;
     cudaGetDevice(&prev);
@@ -146,6 +151,8 @@ void WeightStore::synthesize(const rs_qwen_config& c, uint64_t seed, bool with_m
     throw std::invalid_argument(
         "synthetic architecture unsupported: hidden must be a multiple of 128, head/expert "
         "widths multiples of 64, shared expert width equal to expert width");
+  if (d.E > kMaxExperts)
+    throw std::invalid_argument("architecture unsupported: the routing kernels hold at most 1024 routed experts");
   config = c;
   dims = d;
   Planner plan;
@@ -258,11 +265,14 @@ void WeightStore::synthesize(const rs_qwen_config& c, uint64_t seed, bool with_m
     loc.len = pv.len;
     index[pv.name] = loc;
   }
+  uint32_t* inexact = nullptr;
+  QWEN_CUDA(cudaMalloc(&inexact, 4));
+  QWEN_CUDA(cudaMemset(inexact, 0, 4));
   for (auto& g : gens) {
     long long threads = g.rows * (g.cols / 64);
     synth_qmat_kernel<<<unsigned((threads + 255) / 256), 256>>>(
         const_cast<uint8_t*>(g.mat->tiles), g.cols / 64, g.rows, g.cols, key_of(seed, g.name), k,
-        g.mode, g.row_offset, g.per_expert);
+        g.mode, g.row_offset, g.per_expert, inexact);
     QWEN_CUDA(cudaGetLastError());
     TensorLoc loc;
     loc.quantized = true;
@@ -275,6 +285,12 @@ void WeightStore::synthesize(const rs_qwen_config& c, uint64_t seed, bool with_m
     index[g.name] = loc;
   }
   QWEN_CUDA(cudaDeviceSynchronize());
+  uint32_t n_inexact = 0;
+  QWEN_CUDA(cudaMemcpy(&n_inexact, inexact, 4, cudaMemcpyDeviceToHost));
+  QWEN_CUDA(cudaFree(inexact));
+  if (n_inexact)
+    throw std::runtime_error("quantized weights carry scales or biases outside the fp16 range (" +
+                             std::to_string(n_inexact) + " groups)");
   ready = true;
 }
 
@@ -332,8 +348,8 @@ void WeightStore::export_bytes(const std::string& full, size_t offset, uint8_t* 
         uint16_t bits;
         size_t off = kTilePackedBytes + (part == ".scales" ? 0 : kTileRows * 2) + lr * 2;
         QWEN_CUDA(cudaMemcpy(&bits, t + off, 2, cudaMemcpyDeviceToHost));
-        uint32_t u = uint32_t(bits) << 16;
-        std::memcpy(rowbuf.data() + g * 4, &u, 4);
+        const float v = half_bits_to_float(bits);  // the checkpoint's bf16 value, widened exactly
+        std::memcpy(rowbuf.data() + g * 4, &v, 4);
       }
     }
     size_t row_begin = r * row_bytes;

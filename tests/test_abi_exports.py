@@ -47,3 +47,32 @@ def test_struct_layouts(pkg):
 def test_state_count_matches_oracle(pkg, O):
     for cfg_p, cfg_o in ((pkg.config0(), O.config0()), (pkg.config1(layers=8, context=4096), O.config1(layers=8, context=4096))):
         assert pkg.state_count(cfg_p) == O.lib().orc_state_count(C.byref(cfg_o))
+
+
+def test_library_exports_every_symbol_the_rust_crate_links(pkg):
+    """Every `extern "C"` name the reference's Rust crate declares (committed
+    list, tests/golden/make_ffi_list.py) is declared in include/*.h and
+    exported by the library, so the crate links unchanged."""
+    wanted = (ROOT / "tests" / "golden" / "rust_ffi_symbols.txt").read_text().split()
+    assert len(wanted) == 32
+    lib = pkg.load()
+    declared = declared_symbols()
+    assert [s for s in wanted if s not in declared] == []
+    assert [s for s in wanted if not hasattr(lib, s)] == []
+
+
+def test_graph_builder_stubs_report_without_a_gpu(pkg):
+    """The MLX graph builder has no counterpart here: the stubs answer with the
+    ABI's error convention and touch no device."""
+    lib = pkg.load()
+    err = C.create_string_buffer(256)
+    assert lib.rs_mlx_create(1, err, 256) is None
+    assert b"MLX graph" in err.value
+    err = C.create_string_buffer(256)
+    assert lib.rs_mlx_op(None, 0, None, 0, 0, 0.0, err, 256) == -1 and err.value
+    lib.rs_mlx_cleanup()
+    lib.rs_mlx_destroy(None)
+    err = C.create_string_buffer(256)
+    assert lib.rs_qwen_forward(None, 1, None, None, 0, None, 0, 0, None, 0, None, 0, None, 0, 0, None, 0, None, 0,
+                               err, 256) == -1
+    assert b"descriptor" in err.value

@@ -2,8 +2,8 @@
 
 The CUDA-core engine dequantises in fp32 and is pinned to the FP64 oracle by
 the model-level parity tests; the tcgen05 engine rounds each dequantised
-weight to bf16 (the MMA operand type), so the two agree to bf16 precision:
-rel-L2 <= 5e-3 per launch.
+weight once to IEEE half (the MMA operand type, 11 significant bits), so the
+two agree to half precision: rel-L2 <= 1e-3 per launch.
 """
 import numpy as np
 import pytest
@@ -13,9 +13,8 @@ from conftest import has_cuda
 pytestmark = pytest.mark.gpu
 
 
-def bf16_bits(a):
-    u = np.asarray(a, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+def f16_bits(a):
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
 
 
 def rel(a, b):
@@ -50,11 +49,11 @@ def test_tc_engine_matches_cuda_core_engine(pkg, widths):
                 for T in (1, 5, 16, 30, 64, 130):
                     if which == 3 and T > 64:
                         continue
-                    x = bf16_bits(rng.standard_normal((T, k)))
+                    x = f16_bits(rng.standard_normal((T, k)))
                     y_tc, ms_tc = sess.debug_gemm(which, layer, x, rows, engine=0)
                     y_ref, _ = sess.debug_gemm(which, layer, x, rows, engine=1)
                     err = rel(y_tc, y_ref)
-                    assert err < 5e-3, (widths, layer, which, T, err)
+                    assert err < 1e-3, (widths, layer, which, T, err)
     finally:
         sess.close()
         store.close()

@@ -30,8 +30,9 @@ def cuda_ok():
 
 
 # The oracle checks the device's forced expert selection against its own FP64
-# router logits. bf16 GEMM operands (weights and activations) move router
-# logits by up to ~1e-2 after a few layers, and experts tie within that.
+# router logits. 16-bit GEMM operands (fp16 dequantised weights and
+# activations) move router logits by ~1e-3 after a few layers, and experts tie
+# within that.
 ROUTING_SLACK = 5e-2
 
 
@@ -135,15 +136,14 @@ def _prefill_then_decode(pkg, cfg, store, sess, model):
     outs2, sampled2, logits = sess.step_ragged(outs, lens, [1] * 8, nxt,
                                                flags=pkg.RAGGED_SAMPLED | pkg.RAGGED_LOGITS)
     route_dec = sess.debug_routing(8)
-    agree = 0
     for s in range(8):
         lg, _, _, _ = model.forward([nxt[s]], int(lens[s]), old_state=o_states[s],
                                     forced_routing=route_dec[:, s:s + 1, :])
         err = rel_l2(logits[s], lg[0])
         assert err < 1e-2, (s, err)
-        agree += int(sampled2[s] == int(np.argmax(lg[0])))
         assert sampled2[s] == int(np.argmax(logits[s]))
-    assert agree >= 7, agree  # >= 99% in aggregate is checked over larger batches below
+    # the greedy-agreement gate (>= 99 % of tokens) is asserted over 192 tokens
+    # in test_gpu_bench_parity.py
     for o in list(outs) + list(outs2):
         sess.release(o)
     assert sess.stats()[0] == 0
@@ -249,11 +249,13 @@ def test_cfg1_width_decode_from_synthetic_state(wide):
 def test_cfg1_width_mixed_prefill_decode(wide):
     """configs[2] shape at configs[1] widths (4 layers): two prefill chunks and six
     decode tokens in one ragged step over synthetic prefix states.
-    - decode rows match the FP64 oracle (fed the device's routing) within 1e-2;
-    - a chunk's last row matches it within 5e-2: the error of bf16 activations
-      grows along the chunk through the recurrence (measured 0.007 for 1 token,
-      0.02 for 8-17 tokens, 0.027 for 40 tokens on B200), so the chunked path is
-      also checked against the same tokens decoded one step at a time (1e-3);
+    - EVERY row, each position along the 40- and 17-token chunks included,
+      matches the FP64 oracle (fed the device's routing) within 1e-2. Along a
+      chunk the recurrent state comes to hold only the step's own tokens, so
+      the operand rounding of each projection accumulates into it; with fp16
+      operands the oracle's emulation of that rounding puts the worst row at
+      2.7e-3 (bf16 operands: 3.7e-2);
+    - the chunks equal the same tokens decoded one step at a time (1e-3);
     - every sequence's logits equal, bit for bit, those of the sequence stepped
       alone (a token's arithmetic does not depend on the batch it is in)."""
     pkg, cfg, store, sess, model = wide
@@ -263,7 +265,7 @@ def test_cfg1_width_mixed_prefill_decode(wide):
     parents = [sess.synthetic_state(p, 500 + i) for i, p in enumerate(positions)]
     snaps = [sess.snapshot(p) for p in parents]
     toks = [rng.integers(0, cfg.vocab, size=c).astype(np.uint32) for c in counts]
-    flags = pkg.RAGGED_SAMPLED | pkg.RAGGED_LOGITS
+    flags = pkg.RAGGED_SAMPLED | pkg.RAGGED_LOGITS | pkg.RAGGED_ALL_ROWS
     sess.set_capture(True)
     outs, sampled, logits = sess.step_ragged(parents, positions, counts, np.concatenate(toks), flags=flags)
     route = sess.debug_routing(int(sum(counts)))
@@ -272,8 +274,8 @@ def test_cfg1_width_mixed_prefill_decode(wide):
     for s in range(len(parents)):
         lg, st, _, _ = model.forward(toks[s], positions[s], old_state=snaps[s],
                                      forced_routing=route[:, cu[s]:cu[s + 1], :])
-        err = rel_l2(logits[s], lg[-1])
-        assert err < (1e-2 if counts[s] == 1 else 5e-2), (s, err)
+        errs = [rel_l2(logits[cu[s] + j], lg[j]) for j in range(counts[s])]
+        assert max(errs) <= 1e-2, (s, [round(e, 5) for e in errs])
         assert rel_l2(sess.snapshot(outs[s]), st) < 1e-2, s
     for s in (0, 1):  # the chunks against one-token steps of the same tokens
         cur = parents[s]
@@ -282,13 +284,13 @@ def test_cfg1_width_mixed_prefill_decode(wide):
             if cur is not parents[s]:
                 sess.release(cur)
             cur = nxt
-        assert rel_l2(lj[0], logits[s]) < 1e-3, (s, rel_l2(lj[0], logits[s]))
+            assert rel_l2(lj[0], logits[cu[s] + j]) < 1e-3, (s, j, rel_l2(lj[0], logits[cu[s] + j]))
         assert rel_l2(sess.snapshot(cur), sess.snapshot(outs[s])) < 1e-3, s
         sess.release(cur)
     for s in range(len(parents)):
         (o1,), s1, l1 = sess.step_ragged([parents[s]], [positions[s]], [counts[s]], toks[s], flags=flags)
-        assert s1[0] == sampled[s]
-        assert np.array_equal(l1[0], logits[s]), s
+        assert np.array_equal(s1, sampled[cu[s]:cu[s + 1]])
+        assert np.array_equal(l1, logits[cu[s]:cu[s + 1]]), s
         sess.release(o1)
     for o in parents + outs:
         sess.release(o)

@@ -18,9 +18,9 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-6
 
 
-def bf16_bits(a):
-    u = np.asarray(a, np.float32).view(np.uint32)
-    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+def f16_bits(a):
+    """IEEE-half bits: the projection input type."""
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
 
 
 def rel(a, b):
@@ -63,7 +63,7 @@ def test_noalloc_projection_matches_session_path(pkg, widths):
                         continue
                     # two calls in a row on different inputs, each against the session path
                     for _ in range(2):
-                        x = bf16_bits(rng.standard_normal((T, k)))
+                        x = f16_bits(rng.standard_normal((T, k)))
                         y_ref, _ = sess.debug_gemm(which, layer, x, rows, engine=0)
                         y = noalloc(sess, which, layer, x, rows)
                         assert np.all(np.isfinite(y)), (widths, layer, which, T)
@@ -89,9 +89,40 @@ def test_noalloc_rejects_calls_beyond_the_scratch(pkg):
         with pytest.raises(pkg.NativeError, match="scratch"):
             sess.project_noalloc(3, 0, xd.data_ptr(), T, yd.data_ptr(), T * cfg.vocab)
         # the entry point stays usable after a rejection
-        x = bf16_bits(np.random.default_rng(1).standard_normal((3, cfg.hidden)))
+        x = f16_bits(np.random.default_rng(1).standard_normal((3, cfg.hidden)))
         y_ref, _ = sess.debug_gemm(3, 0, x, cfg.vocab, engine=0)
         assert rel(noalloc(sess, 3, 0, x, cfg.vocab), y_ref) <= TOL
     finally:
         sess.close()
         store.close()
+
+
+def test_noalloc_on_a_second_device_keeps_the_callers_device(pkg):
+    """A session on device 1 driven from a thread whose current device is 0:
+    the entry point sets up device 1's kernels and scratch, matches the
+    session path there, and leaves the caller on device 0."""
+    if not has_cuda():
+        pytest.skip("no CUDA device")
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cfg = pkg.config0()
+    torch.cuda.set_device(1)
+    store = pkg.WeightStore().synthetic(cfg, 5)
+    sess = pkg.DeviceSession(store, cfg, slots=4, budget_bytes=1 << 30)
+    try:
+        x = f16_bits(np.random.default_rng(2).standard_normal((5, cfg.hidden)))
+        y_ref, _ = sess.debug_gemm(0, 0, x, in_rows(cfg, 0)[0], engine=0)
+        xd = torch.from_numpy(x.view(np.int16)).to("cuda:1")
+        rows = in_rows(cfg, 0)[0]
+        yd = torch.full((5, rows), float("nan"), dtype=torch.float32, device="cuda:1")
+        torch.cuda.synchronize(1)
+        torch.cuda.set_device(0)
+        for _ in range(2):
+            sess.project_noalloc(0, 0, xd.data_ptr(), 5, yd.data_ptr(), 5 * rows)
+            assert torch.cuda.current_device() == 0
+            assert rel(yd.cpu().numpy(), y_ref) <= TOL
+    finally:
+        sess.close()
+        store.close()
+        torch.cuda.set_device(0)
