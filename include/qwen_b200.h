@@ -249,6 +249,28 @@ int rs_qwen_device_step_ragged(void* session, size_t n_seq, const StateId* paren
                                uint32_t* sampled, size_t sampled_count, float* logits,
                                size_t logits_count, char* error, size_t capacity);
 
+/* rs_qwen_device_step_ragged with constrained greedy selection: the device
+ * version of the reference's host-side select(logits, allowed)
+ * (src/serving/choices.rs:65-98), which the Rust batch transaction applies to
+ * rows that carry an allowed-token set (batch_transaction.rs:193-235). Output
+ * row r (rows as in step_ragged) picks among allowed_ids[allowed_offsets[r],
+ * allowed_offsets[r+1]) the id with the largest logit on the IEEE total order,
+ * the lowest id on ties; a row whose range is empty picks over the whole
+ * vocabulary. allowed_offsets has rows + 1 entries, starts at 0 and ends at
+ * allowed_count. Every logit of every row must be finite (else -1,
+ * "nonfinite device state"); an id >= vocab is rejected ("invalid legal
+ * token"). An empty range means "no constraint", so the reference's
+ * "empty legal token set" error (a constrained row with no legal id) is
+ * raised by the caller before the call. Requires RS_QWEN_RAGGED_SAMPLED;
+ * logits may be returned as well. */
+int rs_qwen_device_step_ragged_choices(void* session, size_t n_seq, const StateId* parents,
+                                       const uint32_t* positions, const uint32_t* counts,
+                                       const uint32_t* tokens_flat, uint32_t flags,
+                                       const uint32_t* allowed_offsets, const uint32_t* allowed_ids,
+                                       size_t allowed_count, StateId* outputs, uint32_t* sampled,
+                                       size_t sampled_count, float* logits, size_t logits_count,
+                                       char* error, size_t capacity);
+
 /* Speculative verify + accept over a ragged batch, on the device.
  * Sequence s: parents[s] is a published version at position p; seeds[s] is
  * the greedy token after it (already emitted, not yet fed) and

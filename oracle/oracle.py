@@ -40,7 +40,7 @@ assert C.sizeof(RsQwenConfig) == 132
 def build(force: bool = False) -> Path:
     """Compile liboracle.so with the committed Makefile (g++ only)."""
     if force or not LIB.exists() or LIB.stat().st_mtime < max(
-            (HERE / f).stat().st_mtime for f in ("qwen_oracle.cpp", "synth.h", "Makefile")):
+            (HERE / f).stat().st_mtime for f in ("qwen_oracle.cpp", "fp32_step.cpp", "synth.h", "Makefile")):
         subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     return LIB
 
@@ -215,6 +215,63 @@ class Model:
         return logits, hid
 
 
+class F32Step:
+    """The timed CPU baseline (fp32_step.cpp): an fp32, std::thread-parallel
+    batched decode step over the same synthetic weights."""
+
+    def __init__(self, cfg: RsQwenConfig, seed: int, threads: int = 0):
+        L = lib()
+        if not getattr(L, "_f32_bound", False):
+            L.f32_last_error.restype = C.c_char_p
+            L.f32_create.restype = C.c_void_p
+            L.f32_create.argtypes = [C.POINTER(RsQwenConfig), C.c_uint64, C.c_int]
+            L.f32_destroy.argtypes = [C.c_void_p]
+            L.f32_threads.argtypes = [C.c_void_p]
+            L.f32_set_batch.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_float),
+                                        C.c_uint64, C.c_size_t]
+            L.f32_step.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_float),
+                                   C.POINTER(C.c_double), C.POINTER(C.c_double)]
+            L.f32_stage_seconds.argtypes = [C.c_void_p, C.POINTER(C.c_double)]
+            L._f32_bound = True
+        self.cfg = cfg
+        self.h = L.f32_create(C.byref(cfg), seed, threads)
+        if not self.h:
+            raise RuntimeError(L.f32_last_error().decode())
+        self.threads = L.f32_threads(self.h)
+        self.n = 0
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().f32_destroy(self.h)
+            self.h = None
+
+    def _check(self, rc):
+        if rc:
+            raise RuntimeError(lib().f32_last_error().decode())
+
+    def set_batch(self, positions, states=None, seed: int = 0, extra: int = 64):
+        pos = np.ascontiguousarray(positions, np.uint32)
+        st = None if states is None else np.ascontiguousarray(states, np.float32)
+        self.n = len(pos)
+        self._check(lib().f32_set_batch(self.h, len(pos), _p(pos, C.c_uint32), _p(st, C.c_float), seed, extra))
+
+    def step(self, tokens, want_logits: bool = False):
+        """One decode token per sequence: (sampled, logits or None, seconds in layers, seconds in the head)."""
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        sampled = np.zeros(self.n, np.uint32)
+        logits = np.zeros((self.n, self.cfg.vocab), np.float32) if want_logits else None
+        tl, th = C.c_double(), C.c_double()
+        self._check(lib().f32_step(self.h, _p(tok, C.c_uint32), _p(sampled, C.c_uint32), _p(logits, C.c_float),
+                                   C.byref(tl), C.byref(th)))
+        return sampled, logits, tl.value, th.value
+
+    def stage_seconds(self):
+        """(DeltaNet mixers, attention mixers, MoE blocks) seconds of the last step."""
+        out = (C.c_double * 3)()
+        lib().f32_stage_seconds(self.h, out)
+        return tuple(out)
+
+
 def set_routing_slack(slack: float):
     lib().orc_set_routing_slack(slack)
 
@@ -231,6 +288,19 @@ def set_emulation(bits: int):
 def argmax(logits) -> int:
     a = _f32(logits)
     return int(lib().orc_argmax(_p(a, C.c_float), a.size))
+
+
+def select(logits, allowed):
+    """Constrained greedy selection (choices.rs:65-98); raises on the reference's errors."""
+    a = _f32(logits)
+    ids = np.ascontiguousarray(allowed, np.uint32)
+    L = lib()
+    L.orc_select.restype = C.c_int64
+    L.orc_select.argtypes = [C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_uint32), C.c_size_t]
+    r = L.orc_select(_p(a, C.c_float), a.size, _p(ids, C.c_uint32), ids.size)
+    if r < 0:
+        raise RuntimeError(L.orc_last_error().decode())
+    return int(r)
 
 
 def topk(logits, top: int):

@@ -897,6 +897,36 @@ int64_t orc_argmax(const float* logits, size_t n) {
   return int64_t(best);
 }
 
+// Constrained greedy selection (src/serving/choices.rs:65-98, `select` with
+// an allowed set): every logit of the row must be finite; the winner is the
+// allowed id with the largest logit on the total order, the lowest id on
+// ties; ids may repeat or come in any order. Returns the id, or -1 with an
+// error for a non-finite row, an id outside the row, or an empty set.
+int64_t orc_select(const float* logits, size_t n, const uint32_t* allowed, size_t n_allowed) {
+  g_error.clear();
+  for (size_t i = 0; i < n; ++i)
+    if (!std::isfinite(logits[i])) {
+      g_error = "invalid logits";
+      return -1;
+    }
+  int64_t winner = -1;
+  for (size_t k = 0; k < n_allowed; ++k) {
+    const uint32_t id = allowed[k];
+    if (id >= n) {
+      g_error = "invalid legal token";
+      return -1;
+    }
+    if (winner < 0) {
+      winner = id;
+      continue;
+    }
+    const uint32_t a = total_key(logits[id]), b = total_key(logits[winner]);
+    if (a > b || (a == b && int64_t(id) < winner)) winner = id;
+  }
+  if (winner < 0) g_error = "empty legal token set";
+  return winner;
+}
+
 // Stable token->expert counting sort. Input: expert id of each flat
 // assignment (token-major, slot-minor), n_assign entries, ids < n_experts.
 // Output: counts[n_experts], offsets[n_experts+1] (exclusive prefix),

@@ -100,6 +100,8 @@ SIGNATURES = {
     "rs_qwen_device_mtp_snapshot": (C.c_int, [_P, _SIDP, _F32P, _SZ, _ERR, _SZ]),
     "rs_qwen_device_step_ragged": (C.c_int, [_P, _SZ, _SIDP, _U32P, _U32P, _U32P, C.c_uint32, _SIDP, _U32P, _SZ,
                                              _F32P, _SZ, _ERR, _SZ]),
+    "rs_qwen_device_step_ragged_choices": (C.c_int, [_P, _SZ, _SIDP, _U32P, _U32P, _U32P, C.c_uint32, _U32P, _U32P,
+                                                     _SZ, _SIDP, _U32P, _SZ, _F32P, _SZ, _ERR, _SZ]),
     "rs_qwen_device_mtp_verify_accept": (C.c_int, [_P, _SZ, _SIDP, _U32P, _U32P, _U32P, _SZ, _U32P, _SZ,
                                                    C.c_uint32, _SIDP, _U32P, _U32P, _U32P, _ERR, _SZ]),
     "rs_qwen_device_synthetic_state": (C.c_int, [_P, _SZ, C.c_uint64, _SIDP, _ERR, _SZ]),
@@ -273,6 +275,34 @@ class DeviceSession:
             logits = logits_out if logits_out is not None else np.zeros((rows, self.cfg.vocab), np.float32)
         _call("rs_qwen_device_step_ragged", self.h, n, par, _ptr(pos, C.c_uint32), _ptr(cnt, C.c_uint32),
               _ptr(tok, C.c_uint32), flags, outs, _ptr(sampled, C.c_uint32), 0 if sampled is None else rows,
+              _ptr(logits, C.c_float), 0 if logits is None else logits.size)
+        return list(outs), sampled, logits
+
+    def step_ragged_choices(self, parents, positions, counts, tokens, allowed, flags=RAGGED_SAMPLED):
+        """step_ragged with constrained greedy selection: allowed[r] is the list of
+        legal ids of output row r (empty / None = unconstrained).
+        Returns (outs, sampled, logits or None)."""
+        n = len(positions)
+        par = (StateId * n)()
+        for i, p in enumerate(parents):
+            if p is not None:
+                par[i] = p
+        pos = np.ascontiguousarray(positions, np.uint32)
+        cnt = np.ascontiguousarray(counts, np.uint32)
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        rows = int(cnt.sum()) if flags & RAGGED_ALL_ROWS else n
+        if len(allowed) != rows:
+            raise ValueError("one allowed list per output row")
+        lens = [0 if a is None else len(a) for a in allowed]
+        offs = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+        ids = np.concatenate([np.asarray(a, np.uint32) for a in allowed if a is not None and len(a)] or
+                             [np.zeros(0, np.uint32)]).astype(np.uint32)
+        outs = (StateId * n)()
+        sampled = np.zeros(rows, np.uint32)
+        logits = np.zeros((rows, self.cfg.vocab), np.float32) if flags & RAGGED_LOGITS else None
+        _call("rs_qwen_device_step_ragged_choices", self.h, n, par, _ptr(pos, C.c_uint32), _ptr(cnt, C.c_uint32),
+              _ptr(tok, C.c_uint32), flags | RAGGED_SAMPLED, _ptr(offs, C.c_uint32),
+              _ptr(ids, C.c_uint32) if ids.size else None, ids.size, outs, _ptr(sampled, C.c_uint32), rows,
               _ptr(logits, C.c_float), 0 if logits is None else logits.size)
         return list(outs), sampled, logits
 

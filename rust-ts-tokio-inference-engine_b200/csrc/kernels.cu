@@ -612,6 +612,42 @@ __global__ void gather_rows_kernel(const gemm_in_t* __restrict__ src, int ld, co
 // in done[row], which it resets) reduces the slice maxima. The packed key
 // (total order << 32 | ~index) makes the result independent of the order.
 constexpr int kArgmaxSplit = 8;
+// Constrained greedy selection (src/serving/choices.rs:65-98): for listed
+// output row rows[k], the id of ids[offsets[k], offsets[k+1]) with the largest
+// logit on the fp32 total order, the lowest id on equal logits (repeats and
+// order of the ids do not matter). One CTA per constrained row; it runs after
+// argmax_kernel, which has checked every logit of the row for finiteness and
+// written the unconstrained winner that this kernel replaces. Ids are checked
+// against the vocabulary on the host.
+__global__ void __launch_bounds__(256) choice_select_kernel(const float* __restrict__ logits, int V,
+                                                           const int32_t* __restrict__ rows,
+                                                           const uint32_t* __restrict__ offsets,
+                                                           const uint32_t* __restrict__ ids, uint32_t* tokens) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ uint64_t red[8];
+  const int k = blockIdx.x, r = rows[k];
+  const float* lr = logits + size_t(r) * V;
+  uint64_t best = 0;
+  for (uint32_t i = offsets[k] + threadIdx.x; i < offsets[k + 1]; i += blockDim.x) {
+    const uint32_t id = ids[i];
+    const uint64_t key = (uint64_t(total_key(lr[id])) << 32) | uint32_t(0xFFFFFFFFu - id);
+    best = key > best ? key : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t b = red[0];
+    for (int w = 1; w < 8; ++w) b = red[w] > b ? red[w] : b;
+    tokens[r] = 0xFFFFFFFFu - uint32_t(b & 0xFFFFFFFFu);
+  }
+}
+
 __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int V, uint32_t* tokens,
                                                      uint32_t* err, uint64_t* part, uint32_t* done) {
   pdl_trigger();
@@ -967,6 +1003,13 @@ void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint3
                    uint32_t* done, cudaStream_t s) {
   if (rows <= 0) return;
   launch_pdl(argmax_kernel, dim3(rows, kArgmaxSplit), 512, 0, s, logits, V, tokens, err, part, done);
+  count_launch();
+}
+
+void launch_choice_select(const float* logits, int V, const int32_t* rows, const uint32_t* offsets,
+                          const uint32_t* ids, int n_rows, uint32_t* tokens, cudaStream_t s) {
+  if (n_rows <= 0) return;
+  launch_pdl(choice_select_kernel, n_rows, 256, 0, s, logits, V, rows, offsets, ids, tokens);
   count_launch();
 }
 

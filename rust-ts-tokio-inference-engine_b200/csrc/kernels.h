@@ -115,6 +115,10 @@ void launch_verify_compact(const SeqDesc* descs, int n, const int32_t* cand_slot
                            float* hidden_pool, int chunk, int H, cudaStream_t s);
 void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err, uint64_t* part,
                    uint32_t* done, cudaStream_t s);
+// Constrained greedy selection for the listed output rows (choices.rs:65-98);
+// runs after launch_argmax on the same logits.
+void launch_choice_select(const float* logits, int V, const int32_t* rows, const uint32_t* offsets,
+                          const uint32_t* ids, int n_rows, uint32_t* tokens, cudaStream_t s);
 void launch_synth_state(KvPool kv, const int32_t* pages, int n_pages, int position, int ctx,
                         GdnPool pool, int slot, const Dims& d, uint64_t seed, cudaStream_t s);
 // Expert parallelism (ep.cu): stage packing, local row plan / gather, result

@@ -483,14 +483,26 @@ struct Session {
     size_t emit_stride;
     uint32_t* n_emitted;
   };
+  // Constrained greedy selection (rs_qwen_device_step_ragged_choices): output
+  // row r chooses among ids[offsets[r], offsets[r+1]); an empty range leaves
+  // the row unconstrained.
+  struct ChoiceIn {
+    const uint32_t* offsets;  // output rows + 1
+    const uint32_t* ids;
+    size_t n_ids;
+  };
+  int n_choice_rows = 0;  // constrained rows of the step being enqueued
+  PinBuf<uint32_t> choice_stage;
+  DevBuf<uint32_t> choice_dev;  // [rows list][offsets][ids]
 
   // Runs one ragged step. Outputs: outs[s], then per output row a sampled
   // token and/or fp32 logits. Throws on any error after rolling back.
   void step(const std::vector<SeqIn>& seqs, uint32_t flags, StateId* outs, uint32_t* sampled_out,
-            float* logits_out, const VerifyIn* vin = nullptr) {
+            float* logits_out, const VerifyIn* vin = nullptr, const ChoiceIn* choice = nullptr) {
     set_device();
     const uint64_t t_start = now_ns();
     ++calls;
+    n_choice_rows = 0;
     const int n = int(seqs.size());
     if (n <= 0) throw std::invalid_argument("ragged step needs at least one sequence");
     if (n > max_seqs) throw std::invalid_argument("too many sequences in one step");
@@ -546,6 +558,30 @@ struct Session {
       attn_n_items = int(items.size());
     }
     if (R > max_rows) throw std::invalid_argument("ragged step exceeds the output-row budget");
+    // constrained rows: validated and compacted on the host (choices.rs:83-86 checks)
+    std::vector<uint32_t> ch_host;
+    if (choice) {
+      if (!sampled_out || vin) throw std::invalid_argument("constrained selection needs sampled tokens");
+      const uint32_t* off = choice->offsets;
+      if (!off || off[0] != 0 || off[R] != choice->n_ids || (choice->n_ids && !choice->ids))
+        throw std::invalid_argument("allowed-token offsets");
+      std::vector<uint32_t> rows_l, offs{0};
+      for (int r = 0; r < R; ++r) {
+        if (off[r + 1] < off[r]) throw std::invalid_argument("allowed-token offsets");
+        if (off[r + 1] == off[r]) continue;
+        rows_l.push_back(uint32_t(r));
+        offs.push_back(offs.back() + (off[r + 1] - off[r]));
+      }
+      for (size_t i = 0; i < choice->n_ids; ++i)
+        if (choice->ids[i] >= uint32_t(d.V)) throw std::invalid_argument("invalid legal token");
+      n_choice_rows = int(rows_l.size());
+      if (n_choice_rows) {
+        ch_host = rows_l;
+        ch_host.insert(ch_host.end(), offs.begin(), offs.end());
+        for (int k = 0; k < n_choice_rows; ++k)  // the ids of the constrained rows, in row order
+          ch_host.insert(ch_host.end(), choice->ids + off[rows_l[k]], choice->ids + off[rows_l[k] + 1]);
+      }
+    }
     // parents must be distinct when consumed
     std::vector<const Version*> par(n, nullptr);
     for (int i = 0; i < n; ++i) {
@@ -693,7 +729,16 @@ struct Session {
         attn_items.ensure(items.size());
         QWEN_CUDA(cudaMemcpyAsync(attn_items.p, hi, items.size() * 8, cudaMemcpyHostToDevice, stream));
       }
-      uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4 + items.size() * 8;
+      if (!ch_host.empty()) {
+        QWEN_CUDA(cudaStreamSynchronize(stream));  // the pinned stage may still feed the previous step's copy
+        choice_stage.ensure(ch_host.size());
+        choice_dev.ensure(ch_host.size());
+        std::memcpy(choice_stage.p, ch_host.data(), ch_host.size() * 4);
+        QWEN_CUDA(cudaMemcpyAsync(choice_dev.p, choice_stage.p, ch_host.size() * 4, cudaMemcpyHostToDevice, stream));
+        uploads += ch_host.size() * 4;
+      }
+      uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4 + items.size() * 8 +
+                 (vin ? cand_host.size() * 4 + vin->n_eos * 4 : 0);
       const uint64_t t_graph = now_ns();
       ev_used = 0;
       ev_marks.clear();
@@ -871,6 +916,11 @@ struct Session {
     dense(m.lm_head, hb_out.p, max_rows, R, logits.p, d.V, size_t(R) * d.V, 1, s);
     stage(18);  // StateValidation (finite check + greedy selection)
     launch_argmax(logits.p, R, d.V, sampled.p, err.p, argmax_part.p, argmax_done.p, s);
+    if (n_choice_rows) {
+      const int32_t* rows_l = reinterpret_cast<const int32_t*>(choice_dev.p);
+      const uint32_t* offs = choice_dev.p + n_choice_rows;
+      launch_choice_select(logits.p, d.V, rows_l, offs, offs + n_choice_rows + 1, n_choice_rows, sampled.p, s);
+    }
     launches += 1;
   }
 
@@ -1682,6 +1732,33 @@ int rs_qwen_device_step_ragged(void* session, size_t n_seq, const StateId* paren
       throw std::invalid_argument("logits output capacity");
     s->step(seqs, flags, outs, (flags & RS_QWEN_RAGGED_SAMPLED) ? sampled : nullptr,
             (flags & RS_QWEN_RAGGED_LOGITS) ? logits : nullptr);
+  });
+}
+
+int rs_qwen_device_step_ragged_choices(void* session, size_t n_seq, const StateId* parents,
+                                       const uint32_t* positions, const uint32_t* counts, const uint32_t* tokens_flat,
+                                       uint32_t flags, const uint32_t* allowed_offsets, const uint32_t* allowed_ids,
+                                       size_t allowed_count, StateId* outs, uint32_t* sampled, size_t sampled_count,
+                                       float* logits, size_t logits_count, char* error, size_t capacity) {
+  return checked(error, capacity, [&] {
+    Session* s = S(session);
+    if (!n_seq || !positions || !counts || !tokens_flat || !outs || !allowed_offsets)
+      throw std::invalid_argument("ragged step descriptor");
+    if (flags & ~uint32_t(31)) throw std::invalid_argument("unknown ragged step flags");
+    if (!(flags & RS_QWEN_RAGGED_SAMPLED)) throw std::invalid_argument("constrained selection needs sampled tokens");
+    std::vector<Session::SeqIn> seqs(n_seq);
+    size_t off = 0, rows = 0;
+    for (size_t i = 0; i < n_seq; ++i) {
+      const bool has_parent = parents && positions[i] != 0;
+      seqs[i] = {has_parent ? &parents[i] : nullptr, positions[i], counts[i], tokens_flat + off};
+      off += counts[i];
+      rows += (flags & RS_QWEN_RAGGED_ALL_ROWS) ? counts[i] : 1;
+    }
+    if (!sampled || sampled_count != rows) throw std::invalid_argument("sampled output capacity");
+    if ((flags & RS_QWEN_RAGGED_LOGITS) && (!logits || logits_count != rows * size_t(s->d.V)))
+      throw std::invalid_argument("logits output capacity");
+    const Session::ChoiceIn ch{allowed_offsets, allowed_ids, allowed_count};
+    s->step(seqs, flags, outs, sampled, (flags & RS_QWEN_RAGGED_LOGITS) ? logits : nullptr, nullptr, &ch);
   });
 }
 

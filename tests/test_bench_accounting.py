@@ -17,18 +17,42 @@ def _cfg(pkg):
 
 
 def test_recurrent_update_bytes_cfg1(pkg):
+    """The DeltaNet term equals what the library itself holds per sequence:
+    the DeltaNet part of the reference-layout state (rs_qwen_state_count minus
+    the attention K/V), read and written once per step, plus each token's
+    projection row in and gated output row out."""
     import bench
     cfg = _cfg(pkg)
     ctx = bench.contexts(64, 0)
     out, _ = bench.stage_bytes(cfg, ctx, None)
-    n_gdn = 36
-    state = 32 * 128 * 128 * 4 * 2            # one sequence's state, read + written
-    cd = 2 * 16 * 128 + 32 * 128
-    history = 3 * cd * 4 * 2                   # conv history, read + written
-    row = (cd + 32 * 128 + 2 * 32) * 4 + 32 * 128 * 2  # projection row in, bf16 output row
-    assert out["RecurrentUpdate"] == n_gdn * 64 * (state + history + row)
-    # the state dominates: 268.4 MB per layer for 64 sequences
-    assert abs(64 * state / 1e6 - 268.4) < 0.1
+    n_attn = cfg.layers // cfg.interval
+    n_gdn = cfg.layers - n_attn
+    kv_floats = n_attn * 2 * cfg.kv_heads * cfg.context * cfg.head_dim
+    gdn_floats = pkg.state_count(cfg) - kv_floats  # conv history + recurrent state, all DeltaNet layers
+    assert gdn_floats * 4 == bench.gdn_slot_bytes(cfg)  # the session's per-version DeltaNet slot
+    in_row = (2 * cfg.key_heads * cfg.key_dim + 2 * cfg.value_heads * cfg.value_dim + 2 * cfg.value_heads) * 4
+    out_row = cfg.value_heads * cfg.value_dim * 2
+    assert out["RecurrentUpdate"] == n_gdn * 64 * (2 * gdn_floats * 4 // n_gdn + in_row + out_row)
+    # the recurrent state dominates: 268.4 MB per layer for 64 sequences
+    assert abs(64 * cfg.value_heads * cfg.value_dim * cfg.key_dim * 4 * 2 / 1e6 - 268.4) < 0.1
+
+
+def test_chunk_tokens_add_rows_not_state(pkg):
+    """Several tokens of one sequence in a step (prefill chunks, verify blocks)
+    move the recurrent state once and one projection row per token; their K/V
+    count once, at the final length."""
+    import bench
+    cfg = _cfg(pkg)
+    ctx = np.array([100, 2000])
+    one, _ = bench.stage_bytes(cfg, ctx, None)
+    four, _ = bench.stage_bytes(cfg, ctx, None, counts=[4, 4])
+    n_gdn = cfg.layers - cfg.layers // cfg.interval
+    in_row = (2 * cfg.key_heads * cfg.key_dim + 2 * cfg.value_heads * cfg.value_dim + 2 * cfg.value_heads) * 4
+    out_row = cfg.value_heads * cfg.value_dim * 2
+    assert four["RecurrentUpdate"] - one["RecurrentUpdate"] == n_gdn * 6 * (in_row + out_row)
+    kv = 2 * cfg.kv_heads * cfg.head_dim * 2 * (cfg.layers // cfg.interval)
+    assert four["AttentionReduction"] - one["AttentionReduction"] == kv * 6 + (cfg.layers // cfg.interval) * 6 * (
+        cfg.q_heads * 2 * cfg.head_dim + 2 * cfg.kv_heads * cfg.head_dim) * 4
 
 
 def test_moe_bytes_count_distinct_experts(pkg):
