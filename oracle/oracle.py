@@ -177,6 +177,17 @@ class Model:
                                     _p(sc, C.c_float), _p(bi, C.c_float)))
         return packed, sc, bi
 
+    def override(self, name: str, bits: int, group: int, packed, scales, biases):
+        """Use rows in another quantization for matrix `name` (orc_model_override)."""
+        pk = np.ascontiguousarray(packed, np.uint32)
+        sc = np.ascontiguousarray(scales, np.float32)
+        bi = np.ascontiguousarray(biases, np.float32)
+        L = lib()
+        L.orc_model_override.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, C.POINTER(C.c_uint32),
+                                         C.POINTER(C.c_float), C.POINTER(C.c_float)]
+        check(L.orc_model_override(self.h, name.encode(), bits, group, _p(pk, C.c_uint32), _p(sc, C.c_float),
+                                   _p(bi, C.c_float)))
+
     def vector(self, name: str, n: int):
         out = np.zeros(n, np.float32)
         check(lib().orc_model_vector(self.h, name.encode(), _p(out, C.c_float), n))

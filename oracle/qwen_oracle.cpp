@@ -143,6 +143,15 @@ struct QTensor {
     std::vector<float> scale, bias;  // 128 * cols/64 (bf16 widened)
   };
   std::unordered_map<size_t, std::unique_ptr<Block>> blocks;
+  // Replacement data in any reference quantization (bits 2..8, group 32/64/128;
+  // a checkpoint module with a quantization override): rows of LSB-first
+  // `bits`-bit values, float scales and biases per group.
+  struct Override {
+    int bits = 4, group = 64;
+    std::vector<uint32_t> packed;
+    std::vector<float> scale, bias;
+  };
+  std::unique_ptr<Override> ov;
 
   const Block& block(size_t b) {
     {
@@ -178,6 +187,7 @@ struct QTensor {
     return ref;
   }
   void ensure(size_t row0, size_t n) {
+    if (ov) return;
     size_t b0 = row0 / 128, b1 = (row0 + n - 1) / 128;
     parallel_for(b1 - b0 + 1, [&](size_t b, size_t e) {
       for (size_t i = b; i < e; ++i) block(b0 + i);
@@ -186,9 +196,24 @@ struct QTensor {
   // Dequantized row (native/projection_reference.h:74 element formula).
   // `projection`: the row feeds a projection (emulation bit 1 may round it).
   void row(size_t r, double* out, bool projection = false) {
+    const bool rnd = projection && (g_emulate & 1);
+    if (ov) {  // native/projection_reference.h:8-22 with the override's bits and group
+      const size_t words = cols * ov->bits / 32, groups = cols / ov->group;
+      const uint32_t* rw = &ov->packed[r * words];
+      for (size_t c = 0; c < cols; ++c) {
+        const size_t bit = c * ov->bits, w = bit / 32;
+        const unsigned sh = unsigned(bit % 32);
+        uint64_t v = rw[w];
+        if (sh + ov->bits > 32) v |= uint64_t(rw[w + 1]) << 32;
+        const unsigned q = unsigned(v >> sh) & ((1u << ov->bits) - 1u);
+        const size_t g = r * groups + c / ov->group;
+        out[c] = double(ov->scale[g]) * q + double(ov->bias[g]);
+        if (rnd) out[c] = round16(out[c]);
+      }
+      return;
+    }
     const Block& blk = block(r / 128);
     size_t lr = r % 128, words = cols / 8, groups = cols / 64;
-    const bool rnd = projection && (g_emulate & 1);
     for (size_t c = 0; c < cols; ++c) {
       unsigned q = (blk.packed[lr * words + c / 8] >> (4 * (c % 8))) & 15u;
       out[c] = double(blk.scale[lr * groups + c / 64]) * q + double(blk.bias[lr * groups + c / 64]);
@@ -594,6 +619,27 @@ int orc_model_qrows(void* model, const char* name, size_t row0, size_t n, uint32
     }
   });
 }
+// Replaces a matrix's synthetic data with rows in another quantization
+// (bits 2..8, group 32/64/128): packed [rows][cols*bits/32] LSB-first words,
+// scales / biases [rows][cols/group] (values as loaded, widened to float).
+int orc_model_override(void* model, const char* name, int bits, int group, const uint32_t* packed,
+                       const float* scales, const float* biases) {
+  return guarded([&] {
+    auto& t = static_cast<Model*>(model)->Q(name);
+    if (bits < 2 || bits > 8 || bits == 7 || (group != 32 && group != 64 && group != 128) || t.cols % group ||
+        (t.cols * bits) % 32)
+      throw std::invalid_argument("override quantization");
+    auto ov = std::make_unique<QTensor::Override>();
+    ov->bits = bits;
+    ov->group = group;
+    const size_t words = t.cols * bits / 32, groups = t.cols / group;
+    ov->packed.assign(packed, packed + t.rows * words);
+    ov->scale.assign(scales, scales + t.rows * groups);
+    ov->bias.assign(biases, biases + t.rows * groups);
+    t.ov = std::move(ov);
+  });
+}
+
 int orc_model_vector(void* model, const char* name, float* out, size_t count) {
   return guarded([&] {
     const auto& v = static_cast<Model*>(model)->V(name);

@@ -209,6 +209,17 @@ class WeightStore:
         _call("rs_qwen_weights_synthetic", self.h, C.byref(cfg), seed, int(mtp))
         return self
 
+    def load(self, path):
+        """Read one safetensors shard (rs_mlx_weights_load); the device layout is
+        built when the first session is created on the store."""
+        _call("rs_mlx_weights_load", self.h, str(path).encode())
+        return self
+
+    def quant(self, module: str, group: int, bits: int):
+        """Per-module quantization override (rs_qwen_quant)."""
+        _call("rs_qwen_quant", self.h, module.encode(), group, bits)
+        return self
+
     def forward(self, cfg: RsQwenConfig, tokens, offset: int, old_state=None):
         """rs_qwen_forward: returns (last-row logits [vocab], new_state [state_count])."""
         tok = np.ascontiguousarray(tokens, np.uint32)

@@ -65,6 +65,10 @@ struct QMat {
   int rows = 0;       // logical output rows
   int row_tiles = 0;  // ceil(rows / 128)
   int k = 0;          // input width (multiple of 64)
+  // true: `tiles` holds dense fp16 rows [rows][k] (checkpoint modules outside
+  // 4-bit g64: quantization overrides or float weights), run by the CUDA-core
+  // dense kernel instead of the tcgen05 GEMM
+  bool dense_f16 = false;
   __host__ __device__ int k_chunks() const { return k / kTileK; }
   __host__ __device__ const uint8_t* tile(int row_tile, int chunk) const {
     return tiles + (size_t(row_tile) * (k / kTileK) + chunk) * kTileBytes;

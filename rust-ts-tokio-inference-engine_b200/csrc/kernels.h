@@ -113,6 +113,8 @@ void launch_accept(const SeqDesc* descs, int n, const int32_t* cu_seqlens, const
 void launch_verify_compact(const SeqDesc* descs, int n, const int32_t* cand_slots, const int32_t* acc,
                            int32_t* block_table, int stride, const float* hidden_stage, const int32_t* cu_seqlens,
                            float* hidden_pool, int chunk, int H, cudaStream_t s);
+// Y[t][n] = X[t] . W[n] for a matrix stored as dense fp16 rows (QMat::dense_f16).
+void launch_dense_f16(const QMat& W, const gemm_in_t* X, int T, float* Y, int ldy, cudaStream_t s);
 void launch_argmax(const float* logits, int rows, int V, uint32_t* tokens, uint32_t* err, uint64_t* part,
                    uint32_t* done, cudaStream_t s);
 // Constrained greedy selection for the listed output rows (choices.rs:65-98);

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "../../include/qwen_b200.h"
+#include "checkpoint.h"
 #include "common.cuh"
 
 namespace qwen {
@@ -75,12 +76,19 @@ struct WeightStore {
   size_t bytes = 0;
   std::map<std::string, TensorLoc> index;
   std::map<std::string, std::pair<int, int>> quant;  // rs_qwen_quant overrides
+  // checkpoint tensors read by rs_mlx_weights_load (kept after the device
+  // layout is built so rs_mlx_weight_bytes returns them byte for byte)
+  std::map<std::string, HostTensor> host;
+  bool shifted_norms = false;  // RMSNorm gains stored as offsets from 1
   // rs_qwen_forward's private device session for this store, with the
   // config bytes it was made for (rebuilt when they change; dies with the store)
   std::shared_ptr<void> forward_session;
   std::vector<uint8_t> forward_key;
   ~WeightStore();
   void synthesize(const rs_qwen_config& c, uint64_t seed, bool with_mtp);
+  void load(const std::string& path);              // one safetensors shard
+  void materialize(const rs_qwen_config& c);       // device layout of the loaded checkpoint
+  void build(const rs_qwen_config& c, bool with_mtp, const uint64_t* seed);
   void export_bytes(const std::string& name, size_t offset, uint8_t* out, size_t count) const;
 };
 

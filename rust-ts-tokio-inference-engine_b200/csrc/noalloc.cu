@@ -89,6 +89,11 @@ size_t noalloc_scratch_bytes() { return kScratchBytes; }
 
 int project_noalloc(const QMat& W, int max_splits, const gemm_in_t* x, int T, float* y, int sm_count,
                     cudaStream_t s, char* error, size_t capacity) {
+  if (W.dense_f16) {
+    fail(error, capacity, "no-alloc projection: the matrix is held as dense fp16 rows (a checkpoint module "
+                          "outside 4-bit g64); this entry point runs the 4-bit tensor-core GEMM only");
+    return -1;
+  }
   if (!x || !y || T <= 0 || size_t(T) > kPartialFloats) {
     fail(error, capacity, "no-alloc projection: null buffer or token count outside [1, %zu]", kPartialFloats);
     return -1;

@@ -101,7 +101,56 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
   }
 }
 
+// Dense fp16 weight rows (checkpoint modules outside 4-bit g64):
+// Y[t][n] = sum_k X[t][k] * W[n][k], fp32 accumulation. One warp per output
+// row and block of 8 tokens; each lane reads 8 consecutive halves (16 bytes) of
+// the row and of each token per step.
+__global__ void __launch_bounds__(256) dense_f16_kernel(const __half* __restrict__ W, int rows, int K,
+                                                        const __half* __restrict__ X, int T, float* __restrict__ Y,
+                                                        int ldy) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp, t0 = blockIdx.y * 8;
+  if (n >= rows) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const __half* w = W + size_t(n) * K;
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wv);
+    float2 wf[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wf[j] = __half22float2(wh[j]);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t0 + t >= T) break;
+      const uint4 xv = *reinterpret_cast<const uint4*>(X + size_t(t0 + t) * K + k);
+      const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 xf = __half22float2(xh[j]);
+        acc[t] = fmaf(wf[j].x, xf.x, acc[t]);
+        acc[t] = fmaf(wf[j].y, xf.y, acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const float v = warp_sum(acc[t]);
+    if (lane == 0 && t0 + t < T) Y[size_t(t0 + t) * ldy + n] = v;
+  }
+}
+
 }  // namespace
+
+void launch_dense_f16(const QMat& W, const gemm_in_t* X, int T, float* Y, int ldy, cudaStream_t s) {
+  if (!W.dense_f16) throw std::logic_error("dense fp16 kernel on a tiled matrix");
+  if (T <= 0) return;
+  if (W.k % 64 || (reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(W.tiles) & 15))
+    throw std::invalid_argument("dense fp16 projection alignment");
+  dim3 grid((W.rows + 7) / 8, (T + 7) / 8);
+  dense_f16_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __half*>(W.tiles), W.rows, W.k, X, T, Y, ldy);
+  QWEN_CUDA(cudaGetLastError());
+  count_launch_external();
+}
 
 void launch_qgemm(const GemmArgs& a, cudaStream_t s) {
   dim3 grid;

@@ -198,6 +198,10 @@ struct Session {
   // Dense Y[t][n] (+ split partials) = X[t] . deq(W)[n]; returns the split count.
   int dense(const QMat& W, const gemm_in_t* X, int rows_cap, int T, float* Y, int ldy,
             size_t split_stride, int max_splits, cudaStream_t s) {
+    if (W.dense_f16) {  // a checkpoint module kept as fp16 rows: one partial
+      launch_dense_f16(W, X, T, Y, ldy, s);
+      return 1;
+    }
     if (simple_gemm) {
       GemmArgs g;
       g.W = W;
@@ -1536,7 +1540,12 @@ void* rs_mlx_weights_create(char* error, size_t capacity) {
   void* out = nullptr;
   checked(error, capacity, [&] {
     auto* w = new WeightStore();
-    QWEN_CUDA(cudaGetDevice(&w->device));
+    // the store binds to the calling thread's current device when its device
+    // layout is built; reading checkpoint shards needs no device
+    if (cudaGetDevice(&w->device) != cudaSuccess) {
+      w->device = -1;
+      cudaGetLastError();
+    }
     out = w;
   });
   return out;
@@ -1547,8 +1556,7 @@ void rs_mlx_weights_destroy(void* store) { delete static_cast<WeightStore*>(stor
 int rs_mlx_weights_load(void* store, const char* file, char* error, size_t capacity) {
   return checked(error, capacity, [&] {
     if (!store || !file) throw std::invalid_argument("invalid weight load descriptor");
-    throw std::runtime_error(
-        "safetensors ingestion is not implemented by the CUDA backend; use rs_qwen_weights_synthetic");
+    static_cast<WeightStore*>(store)->load(file);
   });
 }
 
@@ -1557,9 +1565,9 @@ int rs_qwen_quant(void* store, const char* module, int group, int bits, char* er
     if (!store || !module || !(group == 32 || group == 64 || group == 128) ||
         !(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8))
       throw std::invalid_argument("invalid model quantization");
-    if (group != 64 || bits != 4)
-      throw std::invalid_argument("CUDA backend kernels implement 4-bit affine group 64 only");
-    static_cast<WeightStore*>(store)->quant[module] = {group, bits};
+    auto* w = static_cast<WeightStore*>(store);
+    if (w->ready) throw std::invalid_argument("quantization overrides must precede the device layout");
+    w->quant[module] = {group, bits};
   });
 }
 
@@ -1671,10 +1679,18 @@ int rs_mlx_weight_bytes(void* store, const char* name, const int32_t* shape, siz
                         size_t offset, uint8_t* output, size_t count, char* error, size_t capacity) {
   return checked(error, capacity, [&] {
     if (!store || !name || !output) throw std::invalid_argument("invalid weight bytes descriptor");
-    (void)shape;
-    (void)rank;
-    if (dtype != 0 && dtype != 2) throw std::invalid_argument("weight bytes dtype");
     auto* w = static_cast<WeightStore*>(store);
+    auto hit = w->host.find(name);
+    if (hit != w->host.end()) {  // a checkpoint tensor (native/mlx_bridge.cpp:179-185 checks)
+      const HostTensor& t = hit->second;
+      if (dtype != t.dtype || (shape && (rank != t.shape.size() ||
+                                         !std::equal(t.shape.begin(), t.shape.end(), shape,
+                                                     [](int64_t a, int32_t b) { return a == int64_t(b); }))))
+        throw std::invalid_argument("weight byte export bounds/type");
+      w->export_bytes(name, offset, output, count);
+      return;
+    }
+    if (dtype != 0 && dtype != 2) throw std::invalid_argument("weight bytes dtype");
     QWEN_CUDA(cudaSetDevice(w->device));
     w->export_bytes(name, offset, output, count);
   });
@@ -1685,6 +1701,7 @@ int rs_qwen_weights_synthetic(void* store, const rs_qwen_config* config, uint64_
   return checked(error, capacity, [&] {
     if (!store || !config) throw std::invalid_argument("invalid synthetic weight descriptor");
     auto* w = static_cast<WeightStore*>(store);
+    if (w->device < 0) QWEN_CUDA(cudaGetDevice(&w->device));
     QWEN_CUDA(cudaSetDevice(w->device));
     w->synthesize(*config, seed, with_mtp != 0);
   });
@@ -1695,6 +1712,11 @@ void* rs_qwen_device_create(void* weights, int gpu, const rs_qwen_config* config
   void* out = nullptr;
   checked(error, capacity, [&] {
     if (!weights || !config || !layers) throw std::invalid_argument("device session descriptor");
+    auto* w = static_cast<WeightStore*>(weights);
+    if (!w->ready && !w->host.empty()) {  // a loaded checkpoint: build its device layout on this device
+      QWEN_CUDA(cudaGetDevice(&w->device));
+      w->materialize(*config);
+    }
     auto s = std::make_unique<Session>();
     s->init(static_cast<WeightStore*>(weights), gpu, *config, layers, count, slots, bytes);
     out = s.release();
