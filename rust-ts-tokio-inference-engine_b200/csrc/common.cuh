@@ -37,12 +37,14 @@ inline void once_per_device(std::atomic<uint64_t>& seen, F setup) {
 
 // 4-bit affine g64 weight tile: 128 rows x 64 columns (one quant group per row).
 // Layout: packed nibbles [128 rows][8 uint32 words], then 128 scales, then 128
-// biases, both IEEE half holding the checkpoint's bf16 values exactly (every
-// bf16 value of magnitude >= 2^-17, and zero, is an fp16 value; the loaders
-// reject others). Word w of a row holds columns 8w..8w+7 in pair-interleaved
-// nibble order: nibble i (bits 4i..4i+3) holds column 8w + nibble_col(i) with
-// nibble_col = {0,2,4,6,1,3,5,7}, so ((word >> 4j) & 0x000F000F) yields the
-// consecutive pair (8w+2j, 8w+2j+1) in the low/high 16-bit halves. A matrix [rows, K] is stored as
+// biases, IEEE half. The bias is the checkpoint's bf16 value and the scale is
+// that value times kTileScale (512), both exact (every bf16 value of magnitude
+// >= 2^-17, and zero, is an fp16 value, and so is 512 s for s < 128; the
+// loaders reject others). Word w of a row holds columns 8w..8w+7 with column
+// c in nibble nibble_of_col(c) = {0,2,4,6,1,3,5,7}[c]: the bytes of
+// (word & 0x0F0F0F0F) then hold columns (0,1 | 2,3) and those of
+// ((word >> 4) & 0x0F0F0F0F) columns (4,5 | 6,7), each byte a nibble that an
+// e4m3 conversion reads as exactly q * 2^-9. A matrix [rows, K] is stored as
 // [ceil(rows/128) row tiles][K/64 column chunks] tiles, each 4608 bytes, so one
 // tile is one contiguous bulk copy.
 constexpr int kTileRows = 128;
@@ -56,8 +58,10 @@ constexpr int kPageTokens = 16;  // paged-KV page size (tokens)
 constexpr int kMaxExperts = 1024;
 
 // Nibble index holding column c (0..7) of a packed word, and its inverse.
-__host__ __device__ __forceinline__ int nibble_of_col(int c) { return (c & 1) ? 4 + (c >> 1) : (c >> 1); }
-__host__ __device__ __forceinline__ int col_of_nibble(int i) { return i < 4 ? 2 * i : 2 * (i - 4) + 1; }
+__host__ __device__ __forceinline__ int nibble_of_col(int c) { return c < 4 ? 2 * c : 2 * (c - 4) + 1; }
+__host__ __device__ __forceinline__ int col_of_nibble(int i) { return (i & 1) ? 4 + (i >> 1) : (i >> 1); }
+// Tile scales are stored times this power of two (see above).
+constexpr float kTileScale = 512.f;
 __device__ __forceinline__ uint32_t nibble(uint32_t word, int col) { return (word >> (4 * nibble_of_col(col))) & 15u; }
 
 struct QMat {

@@ -58,9 +58,13 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 2)
                     const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens, GdnPool pool, int li,
                     int hk, int hv, int conv, const float* __restrict__ conv_w, const float* __restrict__ a_log,
                     const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
-                    float* __restrict__ gb_out, const int32_t* __restrict__ cand_slots) {
+                    float* __restrict__ gb_out, const int32_t* __restrict__ cand_slots, int skip_count) {
   pdl_trigger();
   pdl_wait();
+  {
+    const SeqDesc dd = descs[blockIdx.x];
+    if (dd.cand < 0 && dd.count >= skip_count) return;  // a long run: gdn_run_prep owns it
+  }
   // q / k sums of squares: one partial per warp (4 warps each for dk = 128),
   // double-buffered by token parity so one barrier per token suffices
   constexpr int QW = DK / 32;  // warps holding q (and as many holding k)
@@ -147,11 +151,16 @@ __global__ void __launch_bounds__(256, 3)
                       int hk, int hv, const float* __restrict__ qk, const float* __restrict__ vv,
                       const float* __restrict__ gb, const float* __restrict__ proj, int ld, int splits,
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
-                      gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
+                      gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots,
+                      int skip_count) {
   pdl_trigger();
   pdl_wait();
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
   constexpr int RPW = DV / 8;   // rows per warp
+  {
+    const SeqDesc dd = descs[blockIdx.x];
+    if (dd.cand < 0 && dd.count >= skip_count) return;  // a long run: the chunked kernels own it
+  }
   constexpr int CROWS = 2 * RPW;  // rows per bulk copy: two warps' rows
   constexpr int CHUNKS = DV / CROWS;
   constexpr uint32_t CBYTES = CROWS * DK * 4;
@@ -791,7 +800,9 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits, size_t split_stride,
                 const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool, int gdn_index,
                 gemm_in_t* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf, int sm_count,
-                const int32_t* cand_slots, cudaStream_t s) {
+                const int32_t* cand_slots, cudaStream_t s, const GdnChunkPlan* chunked) {
+  const bool use_chunks = chunked && chunked->n_long > 0 && T != n_seq;
+  const int skip_count = use_chunks ? kGdnChunkMin : 0x7fffffff;
   const int R = d.hv / d.hk;
   if (d.conv > 8) throw std::invalid_argument("conv kernel width > 8 unsupported");
   if (splits > kGdnMaxSplits) throw std::invalid_argument("DeltaNet input projection split more than 8 ways");
@@ -825,7 +836,10 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
   if (!done && d.dk == DK_ && d.dv == DV_ && R == R_) {                                                          \
     launch_pdl(gdn_prep_kernel<DK_, DV_, R_>, dim3(n_seq, d.hk), 2 * DK_ + R_ * DV_, 0, s,                               \
         proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, d.conv, ly.conv_w,  \
-        ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf, cand_slots);                                                \
+        ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf, cand_slots, use_chunks ? kGdnChunkMin : 0x7fffffff);        \
+    if (use_chunks)                                                                                              \
+      launch_gdn_run_prep(*chunked, d, ly, proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool,         \
+                          gdn_index, qk_buf, v_buf, gb_buf, s);                                                  \
     static std::atomic<uint64_t> smem_set_##DK_##_##R_{0};                                                       \
     once_per_device(smem_set_##DK_##_##R_, [] {                                                                  \
       const int bytes = DV_ * DK_ * 4;                                                                           \
@@ -849,9 +863,12 @@ void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_pro
                  descs, cu_seqlens, pool, gdn_index, d.hk, d.hv, items, qk_buf, v_buf, gb_buf, proj, ld_proj,     \
                  splits, split_stride, d.cd, ly.gnorm, d.eps, out, err, cand_slots);                             \
     } else {                                                                                                     \
+      if (use_chunks)                                                                                            \
+        launch_gdn_chunked(*chunked, d, ly, proj, ld_proj, splits, split_stride, descs, cu_seqlens, pool,        \
+                           gdn_index, out, err, qk_buf, v_buf, gb_buf, s);                                       \
       launch_pdl(gdn_update_kernel<DK_, DV_>, dim3(n_seq, d.hv), 256, size_t(DV_) * DK_ * 4, s, descs,           \
                  cu_seqlens, pool, gdn_index, d.hk, d.hv, qk_buf, v_buf, gb_buf, proj, ld_proj, splits,           \
-                 split_stride, d.cd, ly.gnorm, d.eps, out, err, cand_slots);                                     \
+                 split_stride, d.cd, ly.gnorm, d.eps, out, err, cand_slots, skip_count);                         \
     }                                                                                                            \
     done = true;                                                                                                 \
   }

@@ -111,7 +111,7 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
     const uint8_t* tile = embed.tile(int(tok / kTileRows), c0 / kTileK);
     const int r = tok % kTileRows;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + r * 32 + (c0 % kTileK) / 2);
-    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]) * (1.f / kTileScale);
     const float bi = half_bits_to_float(
         reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
 #pragma unroll
@@ -726,7 +726,7 @@ __global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens
     const uint8_t* tile = embed.tile(int(tok / kTileRows), c0 / kTileK);
     const int r = tok % kTileRows;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(tile + r * 32 + (c0 % kTileK) / 2);
-    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+    const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]) * (1.f / kTileScale);
     const float bi = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {

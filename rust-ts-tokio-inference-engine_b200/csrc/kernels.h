@@ -90,10 +90,34 @@ void launch_residual_norm(float* x, const float* partial, int splits, size_t spl
                           const int32_t* out_token, int rows, float* hidden_f32,
                           cudaStream_t s);
 void launch_qgemm(const GemmArgs& a, cudaStream_t s);
+// Long token runs of the DeltaNet layers (prefill chunks), gdn_chunk.cu: the
+// sequences of a step that feed at least kGdnChunkMin tokens (and are not
+// verify steps) run the chunked form; gdn_update skips them.
+constexpr int kGdnChunk = 64;      // tokens per chunk
+constexpr int kGdnChunkMin = 64;   // tokens a sequence feeds before it takes the chunked path
+struct GdnChunkPlan {
+  int n_long = 0, n_items = 0, n_tokens = 0;
+  const int32_t* longs = nullptr;   // [n_long][3]: sequence, first chunk item, chunks
+  const int32_t* items = nullptr;   // [n_items][2]: sequence, chunk index
+  const int32_t* tokens = nullptr;  // [n_tokens]: packed indices of those sequences' tokens
+  float* U = nullptr;               // [item][hv][chunk][dv]
+  float* W = nullptr;               // [item][hv][chunk][dk]
+  float* A = nullptr;               // [item][hv][chunk][chunk]
+  float* LG = nullptr;              // [item][hv][chunk] log-decay prefix sums
+};
+// conv + SiLU, q / k scaling, decay and beta of the long runs, chunk-parallel,
+// then the children's conv histories
+void launch_gdn_run_prep(const GdnChunkPlan& cp, const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
+                         int splits, size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens,
+                         GdnPool pool, int li, float* qk_buf, float* v_buf, float* gb_buf, cudaStream_t s);
+void launch_gdn_chunked(const GdnChunkPlan& cp, const Dims& d, const LayerDev& ly, const float* proj, int ld_proj,
+                        int splits, size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens,
+                        GdnPool pool, int li, gemm_in_t* out, uint32_t* err, const float* qk_buf, float* v_buf,
+                        const float* gb_buf, cudaStream_t s);
 void launch_gdn(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                 size_t split_stride, const SeqDesc* descs, const int32_t* cu_seqlens, int n_seq, int T, GdnPool pool,
                 int gdn_index, gemm_in_t* out, uint32_t* err, float* qk_buf, float* v_buf, float* gb_buf,
-                int sm_count, const int32_t* cand_slots, cudaStream_t s);
+                int sm_count, const int32_t* cand_slots, cudaStream_t s, const GdnChunkPlan* chunked = nullptr);
 void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int ld_proj, int splits,
                       size_t split_stride, const int32_t* token_pos, const int64_t* slot_mapping, int T, KvPool kv,
                       int kv_layer, float* q, float* gate, cudaStream_t s);

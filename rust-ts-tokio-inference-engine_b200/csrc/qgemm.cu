@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(128) qgemm_simple_kernel(GemmArgs a) {
       const uint8_t* tile = a.W.tile(row_tile, c);
       const uint4* pk = reinterpret_cast<const uint4*>(tile + r * 32);
       const uint4 w0 = pk[0], w1 = pk[1];
-      const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]);
+      const float sc = half_bits_to_float(reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes)[r]) * (1.f / kTileScale);
       const float bi = half_bits_to_float(
           reinterpret_cast<const uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r]);
       const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};

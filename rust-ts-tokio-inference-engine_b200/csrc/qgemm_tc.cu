@@ -23,7 +23,8 @@
 //           separate commits, so units amortise the fixed costs;
 //   warps 3-14 dequantise (three warpgroups taking whole units round-robin):
 //           each thread owns one weight row, turns its 64 nibbles per chunk
-//           into 32 f16x2 words (scale*q + bias, one fp16 rounding) and stores
+//           into 32 f16x2 words (e4m3 conversion of nibble bytes, then
+//           scale*q + bias with one fp16 rounding) and stores
 //           them into TMEM with tcgen05.st (the A operand);
 //   warps 15-18 epilogue: tcgen05.ld of the fp32 accumulator, then split-K
 //           partial store / SwiGLU (fp16) / fp32 store.
@@ -53,18 +54,28 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 12;       // shared-memory ring = TMEM A stages (32 columns each)
 constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
 constexpr int kTmemCols = 512;
-// Two fp16 (q0*s+b, q1*s+b) packed low/high from the nibble pair (q0, q1) at
-// bits [0,4) and [16,20) of `w`: one lop3 places them as 1024+q in fp16
-// ((w & 0x000F000F) | 0x64006400; the fp16 spacing at 1024 is 1), add.rn
-// subtracts 1024 exactly and fma.rn rounds scale*q + bias once to 11
-// significant bits. `mask` / `magic` / `neg1024` live in registers.
-__device__ __forceinline__ uint32_t deq_pair(uint32_t w, uint32_t mask, uint32_t magic, uint32_t neg1024,
-                                             uint32_t s2, uint32_t b2) {
-  uint32_t x, q, y;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(x) : "r"(w), "r"(mask), "r"(magic));
-  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(q) : "r"(x), "r"(neg1024));
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(q), "r"(s2), "r"(b2));
-  return y;
+// One packed word (8 columns) into four f16x2 A-operand registers
+// (columns 0-1, 2-3, 4-5, 6-7): the bytes of (w & 0x0F0F0F0F) and of
+// ((w >> 4) & 0x0F0F0F0F) each hold one nibble q, which the e4m3 -> f16x2
+// conversion turns into exactly q * 2^-9; fma.rn with the tile's scale (stored
+// times 2^9) and bias then rounds scale * q + bias once to fp16. `m` =
+// 0x0F0F0F0F lives in a register.
+__device__ __forceinline__ void deq_word(uint32_t w, uint32_t m, uint32_t s2, uint32_t b2, uint32_t* out) {
+  const uint32_t lo = w & m, hi = (w >> 4) & m;
+  uint32_t c0, c1, c2, c3;
+  asm("{\n\t.reg .b16 l, u;\n\t"
+      "mov.b32 {l, u}, %4;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, u;\n\t"
+      "mov.b32 {l, u}, %5;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %2, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %3, u;\n\t}"
+      : "=r"(c0), "=r"(c1), "=r"(c2), "=r"(c3)
+      : "r"(lo), "r"(hi));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[0]) : "r"(c0), "r"(s2), "r"(b2));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[1]) : "r"(c1), "r"(s2), "r"(b2));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[2]) : "r"(c2), "r"(s2), "r"(b2));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[3]) : "r"(c3), "r"(s2), "r"(b2));
 }
 
 struct Work {
@@ -262,9 +273,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + lane;        // weight row within the tile
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     const uint32_t ring_w_s = smem_u32(ring_w);
-    // dequant constants in registers (lop3 and the f16x2 ops take no immediates)
-    uint32_t k_mask = 0x000F000Fu, k_magic = 0x64006400u, k_neg1024 = 0xE400E400u;
-    asm volatile("" : "+r"(k_mask), "+r"(k_magic), "+r"(k_neg1024));
+    // nibble-byte mask in a register
+    uint32_t k_mask = 0x0F0F0F0Fu;
+    asm volatile("" : "+r"(k_mask));
     // This warpgroup takes units n = wg, wg + 3, ... of the CTA's unit
     // sequence. NS, kWSlots and NSB are multiples of 3, so its TMEM slot,
     // weight slot and released activation slot (of unit n - NS) each advance
@@ -294,9 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bb = lds_u16(tile + kTilePackedBytes + kTileRows * 2 + r * 2);
             const uint32_t s2 = __byte_perm(sb, 0, 0x1010), b2 = __byte_perm(bb, 0, 0x1010);
             uint32_t v[32];
-#define QWEN_DEQ_WORD(WD, W)                                                            \
-  _Pragma("unroll") for (int j = 0; j < 4; ++j) v[(WD) * 4 + j] =                      \
-      deq_pair((W) >> (4 * j), k_mask, k_magic, k_neg1024, s2, b2);
+#define QWEN_DEQ_WORD(WD, W) deq_word((W), k_mask, s2, b2, v + (WD) * 4);
             QWEN_DEQ_WORD(0, p0.x) QWEN_DEQ_WORD(1, p0.y) QWEN_DEQ_WORD(2, p0.z) QWEN_DEQ_WORD(3, p0.w)
             QWEN_DEQ_WORD(4, p1.x) QWEN_DEQ_WORD(5, p1.y) QWEN_DEQ_WORD(6, p1.z) QWEN_DEQ_WORD(7, p1.w)
 #undef QWEN_DEQ_WORD

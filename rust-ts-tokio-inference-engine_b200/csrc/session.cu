@@ -498,6 +498,11 @@ struct Session {
   int n_choice_rows = 0;  // constrained rows of the step being enqueued
   PinBuf<uint32_t> choice_stage;
   DevBuf<uint32_t> choice_dev;  // [rows list][offsets][ids]
+  // chunked DeltaNet for long token runs: work lists and per-(chunk, head) scratch
+  GdnChunkPlan gplan;
+  PinBuf<int32_t> gplan_stage;
+  DevBuf<int32_t> gplan_dev;
+  DevBuf<float> gplan_u, gplan_w, gplan_a, gplan_lg;
 
   // Runs one ragged step. Outputs: outs[s], then per output row a sampled
   // token and/or fp32 logits. Throws on any error after rolling back.
@@ -562,6 +567,22 @@ struct Session {
       attn_n_items = int(items.size());
     }
     if (R > max_rows) throw std::invalid_argument("ragged step exceeds the output-row budget");
+    // DeltaNet runs of at least kGdnChunkMin tokens (not verify steps) take the chunked kernels
+    gplan = GdnChunkPlan();
+    std::vector<int32_t> gl_longs, gl_items, gl_tokens;
+    if (d.n_gdn > 0 && !vin && T != n) {
+      int off = 0;
+      for (int i = 0; i < n; ++i) {
+        const int cnt = int(seqs[i].count);
+        if (cnt >= kGdnChunkMin) {
+          const int chunks = (cnt + kGdnChunk - 1) / kGdnChunk;
+          gl_longs.insert(gl_longs.end(), {i, int(gl_items.size() / 2), chunks});
+          for (int j = 0; j < chunks; ++j) gl_items.insert(gl_items.end(), {i, j});
+          for (int j = 0; j < cnt; ++j) gl_tokens.push_back(off + j);
+        }
+        off += cnt;
+      }
+    }
     // constrained rows: validated and compacted on the host (choices.rs:83-86 checks)
     std::vector<uint32_t> ch_host;
     if (choice) {
@@ -733,6 +754,31 @@ struct Session {
         attn_items.ensure(items.size());
         QWEN_CUDA(cudaMemcpyAsync(attn_items.p, hi, items.size() * 8, cudaMemcpyHostToDevice, stream));
       }
+      if (!gl_longs.empty()) {
+        const size_t nl = gl_longs.size(), ni = gl_items.size(), nt = gl_tokens.size();
+        gplan_stage.ensure(nl + ni + nt);
+        gplan_dev.ensure(nl + ni + nt);
+        std::memcpy(gplan_stage.p, gl_longs.data(), nl * 4);
+        std::memcpy(gplan_stage.p + nl, gl_items.data(), ni * 4);
+        std::memcpy(gplan_stage.p + nl + ni, gl_tokens.data(), nt * 4);
+        QWEN_CUDA(cudaMemcpyAsync(gplan_dev.p, gplan_stage.p, (nl + ni + nt) * 4, cudaMemcpyHostToDevice, stream));
+        uploads += (nl + ni + nt) * 4;
+        const size_t units = ni / 2 * size_t(d.hv) * kGdnChunk;  // (chunk, head) pairs x chunk tokens
+        gplan_u.ensure(units * d.dv);
+        gplan_w.ensure(units * d.dk);
+        gplan_a.ensure(units * kGdnChunk);
+        gplan_lg.ensure(units);
+        gplan.n_long = int(nl / 3);
+        gplan.n_items = int(ni / 2);
+        gplan.n_tokens = int(nt);
+        gplan.longs = gplan_dev.p;
+        gplan.items = gplan_dev.p + nl;
+        gplan.tokens = gplan_dev.p + nl + ni;
+        gplan.U = gplan_u.p;
+        gplan.W = gplan_w.p;
+        gplan.A = gplan_a.p;
+        gplan.LG = gplan_lg.p;
+      }
       if (!ch_host.empty()) {
         QWEN_CUDA(cudaStreamSynchronize(stream));  // the pinned stage may still feed the previous step's copy
         choice_stage.ensure(ch_host.size());
@@ -880,7 +926,7 @@ struct Session {
       if (ly.mixer == 0) {
         stage(4);  // RecurrentUpdate (conv + prepare + recurrence + gated norm)
         launch_gdn(d, ly, partial.p, proj_w, ps, proj_stride, descs.p, cu_seqlens.p, n, T, gdn, ly.type_index,
-                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, cand_dev.p, s);
+                   hb2.p, err.p, gdn_qk.p, gdn_v.p, gdn_gb.p, sm_count, cand_dev.p, s, &gplan);
         stage(5);  // RecurrentOutput
       } else {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)

@@ -96,7 +96,10 @@ __global__ void synth_qmat_kernel(uint8_t* tiles, int k_chunks, long long rows, 
   dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
   dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
   uint16_t sh = 0, bh = 0;
-  if (!bf16_to_half_bits(sb, &sh) || !bf16_to_half_bits(bb, &bh)) atomicAdd(inexact, 1u);
+  // the scale times kTileScale (exact: a power of two, checked against overflow)
+  const float s512 = s * kTileScale;
+  sh = __half_as_ushort(__float2half_rn(s512));
+  if (__half2float(__ushort_as_half(sh)) != s512 || !bf16_to_half_bits(bb, &bh)) atomicAdd(inexact, 1u);
   reinterpret_cast<uint16_t*>(tile + kTilePackedBytes)[r] = sh;
   reinterpret_cast<uint16_t*>(tile + kTilePackedBytes + kTileRows * 2)[r] = bh;
 }
@@ -211,9 +214,9 @@ struct SourceRows {
 };
 
 uint16_t half_bits(double v) { return __half_as_ushort(__float2half_rn(float(v))); }
-// the bf16 / fp16 / fp32 scale or bias as the fp16 bits of the same value (tile format)
-uint16_t exact_half(const HostTensor& t, size_t i, const std::string& name) {
-  const double v = t.at(i);
+// factor times the bf16 / fp16 / fp32 scale or bias as exact fp16 bits (tile format)
+uint16_t exact_half(const HostTensor& t, size_t i, const std::string& name, double factor) {
+  const double v = t.at(i) * factor;
   const uint16_t h = half_bits(v);
   if (double(half_bits_to_float(h)) != v)
     throw std::invalid_argument("scale or bias not representable in the fp16 tile format: " + name);
@@ -455,8 +458,8 @@ void WeightStore::build(const rs_qwen_config& c, bool with_mtp, const uint64_t* 
             for (int cc = 0; cc < 64; ++cc)  // canonical nibble cc%8 of word cc/8 -> pair-interleaved order
               words[cc / 8] |= ((row[gq * 8 + cc / 8] >> (4 * (cc % 8))) & 15u) << (4 * nibble_of_col(cc % 8));
             std::memcpy(tile + tr * 32, words, 32);
-            const uint16_t sh = exact_half(*sr.s, r * sr.groups + gq, g.name);
-            const uint16_t bh = exact_half(*sr.b, r * sr.groups + gq, g.name);
+            const uint16_t sh = exact_half(*sr.s, r * sr.groups + gq, g.name, kTileScale);
+            const uint16_t bh = exact_half(*sr.b, r * sr.groups + gq, g.name, 1.0);
             std::memcpy(tile + kTilePackedBytes + tr * 2, &sh, 2);
             std::memcpy(tile + kTilePackedBytes + kTileRows * 2 + tr * 2, &bh, 2);
           }
@@ -557,7 +560,8 @@ void WeightStore::export_bytes(const std::string& full, size_t offset, uint8_t* 
         uint16_t bits;
         size_t off = kTilePackedBytes + (part == ".scales" ? 0 : kTileRows * 2) + lr * 2;
         QWEN_CUDA(cudaMemcpy(&bits, t + off, 2, cudaMemcpyDeviceToHost));
-        const float v = half_bits_to_float(bits);  // the checkpoint's bf16 value, widened exactly
+        // the checkpoint's bf16 value, widened exactly (scales are stored times kTileScale)
+        const float v = half_bits_to_float(bits) / (part == ".scales" ? kTileScale : 1.f);
         std::memcpy(rowbuf.data() + g * 4, &v, 4);
       }
     }

@@ -8,7 +8,7 @@ the FP64 logits within the slack), so the comparison isolates the arithmetic:
 last-row logits, the draft's hidden rows and its KV within rel-L2 1e-2, greedy
 token equal. The autoregressive step (draft_source = 1) is checked from the
 device's own draft state (KV and last hidden row), so each step's error is
-measured on its own.
+measured on its own. Runs at configs[0] and at configs[1] widths.
 """
 import numpy as np
 import pytest
@@ -26,15 +26,20 @@ def rel(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-@pytest.fixture(scope="module")
-def mtp(pkg, O):
+@pytest.fixture(scope="module", params=["cfg0", "cfg1"])
+def mtp(pkg, O, request):
+    """configs[0], and configs[1] widths (hidden 2048, 512 experts top-10,
+    16q/2kv/256, vocab 151936) on a 4-layer slice plus the MTP layer."""
     if not has_cuda():
         pytest.skip("no CUDA device")
-    cfg = pkg.config0()
+    if request.param == "cfg0":
+        cfg, ocfg = pkg.config0(), O.config0()
+    else:
+        cfg, ocfg = pkg.config1(layers=4, context=1024), O.config1(layers=4, context=1024)
     store = pkg.WeightStore().synthetic(cfg, 21, mtp=True)
-    sess = pkg.DeviceSession(store, cfg, slots=32, budget_bytes=1 << 30)
+    sess = pkg.DeviceSession(store, cfg, slots=32, budget_bytes=4 << 30)
     sess.mtp_attach(store)
-    model = O.Model(O.config0(), 21, mtp=True)
+    model = O.Model(ocfg, 21, mtp=True)
     O.set_routing_slack(ROUTING_SLACK)
     yield pkg, cfg, sess, model
     sess.close()

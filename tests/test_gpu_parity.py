@@ -294,3 +294,33 @@ def test_cfg1_width_mixed_prefill_decode(wide):
         sess.release(o1)
     for o in parents + outs:
         sess.release(o)
+
+
+def test_cfg1_width_long_prefill_runs(wide):
+    """Runs of >= 64 tokens take the chunked DeltaNet kernels (64-token chunks,
+    token-parallel conv preparation, the rows of each head's state carried
+    chunk to chunk): a 100-token prefill from an empty state, a 64-token run
+    and an 80-token run from synthetic prefix states, next to a decode row.
+    Every row's logits and every sequence's state match the FP64 oracle (fed
+    the device's routing) within 1e-2."""
+    pkg, cfg, store, sess, model = wide
+    rng = np.random.default_rng(77)
+    positions = [0, 100, 900, 2000]
+    counts = [100, 64, 80, 1]
+    parents = [None] + [sess.synthetic_state(p, 800 + i) for i, p in enumerate(positions[1:])]
+    snaps = [None] + [sess.snapshot(p) for p in parents[1:]]
+    toks = [rng.integers(0, cfg.vocab, size=c).astype(np.uint32) for c in counts]
+    flags = pkg.RAGGED_SAMPLED | pkg.RAGGED_LOGITS | pkg.RAGGED_ALL_ROWS
+    sess.set_capture(True)
+    outs, sampled, logits = sess.step_ragged(parents, positions, counts, np.concatenate(toks), flags=flags)
+    route = sess.debug_routing(int(sum(counts)))
+    sess.set_capture(False)
+    cu = np.concatenate([[0], np.cumsum(counts)])
+    for s in range(len(counts)):
+        lg, st, _, _ = model.forward(toks[s], positions[s], old_state=snaps[s],
+                                     forced_routing=route[:, cu[s]:cu[s + 1], :])
+        errs = [rel_l2(logits[cu[s] + j], lg[j]) for j in range(counts[s])]
+        assert max(errs) <= 1e-2, (s, max(errs), int(np.argmax(errs)))
+        assert rel_l2(sess.snapshot(outs[s]), st) <= 1e-2, s
+    for o in [p for p in parents if p is not None] + outs:
+        sess.release(o)

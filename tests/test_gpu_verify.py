@@ -8,7 +8,8 @@ the accepted count and emitted tokens of the reference's plan() rule (the
 oracle's orc_accept, pinned to src/serving/native_speculative.rs's cases)
 bit-exactly, and its output version must equal the replayed version after
 [seed, d_0 .. d_{accepted-1}] bit-for-bit: KV, DeltaNet state, conv history
-(the snapshot) and the kept hidden rows.
+(the snapshot) and the kept hidden rows. Runs at configs[0] and at
+configs[1] widths.
 """
 import numpy as np
 import pytest
@@ -33,13 +34,14 @@ def greedy_chain(pkg, sess, parent, pos, seed, steps):
     return versions, rows, hidden
 
 
-@pytest.fixture(scope="module")
-def setup(pkg):
+@pytest.fixture(scope="module", params=["cfg0", "cfg1"])
+def setup(pkg, request):
+    """configs[0], and configs[1] widths on a 4-layer slice."""
     if not has_cuda():
         pytest.skip("no CUDA device")
-    cfg = pkg.config0()
+    cfg = pkg.config0() if request.param == "cfg0" else pkg.config1(layers=4, context=1024)
     store = pkg.WeightStore().synthetic(cfg, 7)
-    sess = pkg.DeviceSession(store, cfg, slots=96, budget_bytes=2 << 30)
+    sess = pkg.DeviceSession(store, cfg, slots=96, budget_bytes=4 << 30)
     rng = np.random.default_rng(11)
     lens = [5, 9, 3, 12, 7]
     prompts = [rng.integers(0, cfg.vocab, size=n).astype(np.uint32) for n in lens]
