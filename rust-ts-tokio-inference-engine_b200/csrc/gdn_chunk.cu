@@ -39,20 +39,39 @@ namespace {
 
 constexpr int C = kGdnChunk;  // tokens per chunk
 constexpr int kScanRows = 32;   // state rows per scan CTA
-constexpr int kScanThreads = 256;
+constexpr int kScanThreads = 512;
+constexpr int kRunBlock = 16;   // tokens per run-prep CTA
 
+// Sum of the split-K partials of one column, in split order; the (at most
+// 8) loads are issued together.
 __device__ __forceinline__ float split_sum_c(const float* pr, int col, int splits, size_t split_stride) {
-  float v = pr[col];
-  for (int s = 1; s < splits; ++s) v += pr[size_t(s) * split_stride + col];
+  float part[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) part[s] = s < splits ? pr[size_t(s) * split_stride + col] : 0.f;
+  float v = part[0];
+#pragma unroll
+  for (int s = 1; s < 8; ++s)
+    if (s < splits) v += part[s];
   return v;
+}
+
+// 16-byte global -> shared copy without registers (zero-filled when !valid).
+__device__ __forceinline__ void cp16(float* dst, const float* src, bool valid) {
+  const uint32_t d = uint32_t(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 template <int DK, int DV>
 __global__ void __launch_bounds__(DK + DV)
     gdn_chunk_prep_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens,
                           const int32_t* __restrict__ items, int hk, int hv, const float* __restrict__ qk,
-                          const float* __restrict__ vv, const float* __restrict__ gb, float* __restrict__ U,
-                          float* __restrict__ W, float* __restrict__ A, float* __restrict__ LG) {
+                          const float* __restrict__ vv, const float* __restrict__ proj, int ld, int splits,
+                          size_t split_stride, int cd, const float* __restrict__ a_log,
+                          const float* __restrict__ dt_bias, float* __restrict__ U, float* __restrict__ W,
+                          float* __restrict__ A, float* __restrict__ LG) {
   pdl_trigger();
   pdl_wait();
   constexpr int P = DK + 1;  // padded row stride: lanes reading different rows hit different banks
@@ -68,38 +87,81 @@ __global__ void __launch_bounds__(DK + DV)
   const int n = min(C, d.count - chunk * C);
   const int kh = head / (hv / hk), vd = hv * DV;
   const int tid = threadIdx.x, nthr = DK + DV;
-  for (int e = tid; e < C * DK; e += nthr) {
-    const int t = e / DK, c = e % DK;
-    const float* row = qk + ((size_t(t0 + t) * hk + kh) * 2) * DK;
-    Qs[t * P + c] = t < n ? row[c] : 0.f;
-    Ks[t * P + c] = t < n ? row[DK + c] : 0.f;
+  {  // q and k rows of the chunk: all loads issued before the shared stores
+    constexpr int PER = C * DK / 4 / (DK + DV);  // float4 per thread (8)
+    float4 qv[PER], kv[PER];
+#pragma unroll
+    for (int m = 0; m < PER; ++m) {
+      const int e = tid + m * nthr, t = e / (DK / 4), c4 = e % (DK / 4);
+      const float4* row = reinterpret_cast<const float4*>(qk + ((size_t(t0 + t) * hk + kh) * 2) * DK);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      qv[m] = t < n ? row[c4] : z;
+      kv[m] = t < n ? row[DK / 4 + c4] : z;
+    }
+#pragma unroll
+    for (int m = 0; m < PER; ++m) {
+      const int e = tid + m * nthr, t = e / (DK / 4), c = 4 * (e % (DK / 4));
+      Qs[t * P + c] = qv[m].x, Qs[t * P + c + 1] = qv[m].y, Qs[t * P + c + 2] = qv[m].z, Qs[t * P + c + 3] = qv[m].w;
+      Ks[t * P + c] = kv[m].x, Ks[t * P + c + 1] = kv[m].y, Ks[t * P + c + 2] = kv[m].z, Ks[t * P + c + 3] = kv[m].w;
+    }
   }
-  if (tid < C) {
-    const float g = tid < n ? gb[(size_t(t0 + tid) * hv + head) * 2] : 1.f;
-    lg[tid] = fmaxf(logf(g), -1e4f);  // a zero decay stays finite: later ratios underflow to 0
-    beta[tid] = tid < n ? gb[(size_t(t0 + tid) * hv + head) * 2 + 1] : 0.f;
+  if (tid < C) {  // decay and beta (gdn_prep's arithmetic), kept in log form for the products
+    float lgv = 0.f, bt = 0.f;
+    if (tid < n) {
+      const float* pr = proj + size_t(t0 + tid) * ld;
+      const float av = split_sum_c(pr, cd + vd + head, splits, split_stride) + dt_bias[head];
+      const float bv = split_sum_c(pr, cd + vd + hv + head, splits, split_stride);
+      const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
+      const float g = expf(-expf(a_log[head]) * sp);
+      lgv = fmaxf(logf(g), -1e4f);  // a zero decay stays finite: later ratios underflow to 0
+      bt = sigmoidf_(bv);
+    }
+    lg[tid] = lgv;
+    beta[tid] = bt;
   }
   __syncthreads();
   if (tid == 0)
     for (int t = 1; t < C; ++t) lg[t] += lg[t - 1];
   __syncthreads();
-  // decayed products: L (strictly lower, k.k) and A (lower with diagonal, q.k)
+  // decayed products: L (strictly lower, k.k) and A (lower with diagonal, q.k),
+  // in 4x4 register tiles of (t, i); tiles above the diagonal are skipped
   const size_t sc = size_t(item) * hv + head;
   float* Ag = A + sc * C * C;
-  for (int p = tid; p < C * C; p += nthr) {
-    const int t = p / C, i = p % C;
-    float kk = 0.f, qkv = 0.f;
-    if (i <= t) {
-#pragma unroll 8
+  for (int tile = tid; tile < (C / 4) * (C / 4); tile += nthr) {
+    const int tb = tile / (C / 4), ib = tile % (C / 4);
+    float kk[4][4], qq[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) kk[a][b] = qq[a][b] = 0.f;
+    if (ib <= tb) {
+#pragma unroll 4
       for (int c = 0; c < DK; ++c) {
-        const float ki = Ks[i * P + c];
-        kk = fmaf(Ks[t * P + c], ki, kk);
-        qkv = fmaf(Qs[t * P + c], ki, qkv);
+        float kt[4], qt[4], ki[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          kt[a] = Ks[(4 * tb + a) * P + c];
+          qt[a] = Qs[(4 * tb + a) * P + c];
+          ki[a] = Ks[(4 * ib + a) * P + c];
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            kk[a][b] = fmaf(kt[a], ki[b], kk[a][b]);
+            qq[a][b] = fmaf(qt[a], ki[b], qq[a][b]);
+          }
       }
     }
-    const float ratio = i <= t ? expf(lg[t] - lg[i]) : 0.f;
-    L[t * (C + 1) + i] = i < t ? beta[t] * ratio * kk : 0.f;
-    Ag[p] = (i <= t && t < n) ? ratio * qkv : 0.f;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int t = 4 * tb + a, i = 4 * ib + b;
+        const float ratio = i <= t ? expf(lg[t] - lg[i]) : 0.f;
+        L[t * (C + 1) + i] = i < t ? beta[t] * ratio * kk[a][b] : 0.f;
+        Ag[t * C + i] = (i <= t && t < n) ? ratio * qq[a][b] : 0.f;
+      }
   }
   __syncthreads();
   // forward substitution, one column per thread: U columns (values), then W columns (keys)
@@ -111,20 +173,20 @@ __global__ void __launch_bounds__(DK + DV)
     float b;
     if (is_u) b = t < n ? beta[t] * vv[size_t(t0 + t) * vd + head * DV + col] : 0.f;
     else b = beta[t] * expf(lg[t]) * Ks[t * P + col];
-    float acc = b;
+    float part[4] = {b, 0.f, 0.f, 0.f};  // four independent chains
 #pragma unroll
-    for (int i = 0; i < t; ++i) acc = fmaf(-L[t * (C + 1) + i], x[i], acc);
-    x[t] = acc;
+    for (int i = 0; i < t; ++i) part[i & 3] = fmaf(-L[t * (C + 1) + i], x[i], part[i & 3]);
+    x[t] = (part[0] + part[1]) + (part[2] + part[3]);
   }
   float* dst = is_u ? U + sc * C * DV : W + sc * C * DK;
-  const int ld = is_u ? DV : DK;
+  const int ldx = is_u ? DV : DK;
 #pragma unroll
-  for (int t = 0; t < C; ++t) dst[t * ld + col] = x[t];
+  for (int t = 0; t < C; ++t) dst[t * ldx + col] = x[t];
   if (tid < C) LG[sc * C + tid] = lg[tid];
 }
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(kScanThreads)
+__global__ void __launch_bounds__(kScanThreads, 1)
     gdn_chunk_scan_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens,
                           const int32_t* __restrict__ longs, GdnPool pool, int li, int hk, int hv,
                           const float* __restrict__ qk, const float* __restrict__ U, const float* __restrict__ W,
@@ -132,16 +194,21 @@ __global__ void __launch_bounds__(kScanThreads)
                           uint32_t* err) {
   pdl_trigger();
   pdl_wait();
-  constexpr int P = DK + 1, RP = kScanRows + 1, BLOCKS = DV / kScanRows;
-  extern __shared__ float sm[];
-  float* Ws = sm;                    // [C][P]
-  float* Qs = Ws + C * P;            // [C][P]
-  float* Ks = Qs + C * P;            // [C][P]
-  float* As = Ks + C * P;            // [C][C+1]
-  float* S = As + C * (C + 1);       // [kScanRows][P]
-  float* Us = S + kScanRows * P;     // [C][RP]
-  float* Hs = Us + C * RP;           // [C][RP]
-  __shared__ float lg[C];
+  // Row strides keep every row 16-byte aligned (asynchronous copies and
+  // 16-byte shared loads) and put the rows a quarter-warp reads together in
+  // distinct banks: W / q / k (PW) and the state rows (PS) are 4 floats wider
+  // than a row, and the state rows a thread owns are interleaved (row aq + 4m).
+  constexpr int PS = DK + 4, PW = DK + 4, PA = C + 4, PU = kScanRows + 4, RP = kScanRows + 1,
+                BLOCKS = DV / kScanRows, C4 = DK / 4;
+  extern __shared__ __align__(16) float sm[];
+  float* Ws = sm;                    // [C][PW]
+  float* Qs = Ws + C * PW;           // [C][PW]
+  float* Ks = Qs + C * PW;           // [C][PW]
+  float* As = Ks + C * PW;           // [C][PA]
+  float* S = As + C * PA;            // [kScanRows][PS]
+  float* Us = S + kScanRows * PS;    // [C][PU]
+  float* Hs = Us + C * PU;           // [C][RP]
+  __shared__ __align__(16) float lg[C];
   const int ls = blockIdx.x / (hv * BLOCKS), rem = blockIdx.x % (hv * BLOCKS);
   const int head = rem / BLOCKS, rb = rem % BLOCKS;
   const int seq = longs[3 * ls], item0 = longs[3 * ls + 1], n_chunks = longs[3 * ls + 2];
@@ -154,79 +221,102 @@ __global__ void __launch_bounds__(kScanThreads)
   float* dst = pool.state + (size_t(d.child) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
   for (int e = tid; e < kScanRows * DK; e += kScanThreads) {
     const int r = e / DK, c = e % DK;
-    S[r * P + c] = src ? src[size_t(r0 + r) * DK + c] : 0.f;
+    S[r * PS + c] = src ? src[size_t(r0 + r) * DK + c] : 0.f;
   }
-  // phase A / B: token t = tid / 4 (64 tokens), rows quarter*8 .. +8
-  const int at = tid >> 2, aq = tid & 3;
-  // phase C: row tid / 8, columns (tid % 8) + 8m
-  const int cr = tid >> 3, cb = tid & 7;
+  auto f4 = [](const float* p) { return *reinterpret_cast<const float4*>(p); };
+  auto dot4 = [](float4 a, float4 b, float acc) {
+    return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, fmaf(a.x, b.x, acc))));
+  };
+  // phase A / B: token at = tid / 8 (64 tokens), rows aq + 8m (m < 4)
+  const int at = tid >> 3, aq = tid & 7;
+  // phase C: row cr = tid / 16, column quads cb + 16m
+  const int cr = tid >> 4, cb = tid & 15;
+  constexpr int MR = kScanRows / 8, MQ = C4 / 16;  // rows / column quads per thread
   for (int j = 0; j < n_chunks; ++j) {
     const size_t sc = size_t(item0 + j) * hv + head;
     const int t0 = cu_seqlens[seq] + j * C;
     const int n = min(C, d.count - j * C);
     __syncthreads();  // the previous chunk's readers are done
-    for (int e = tid; e < C * DK; e += kScanThreads) {
-      const int t = e / DK, c = e % DK;
+    // the chunk's W, q, k, A, U block and decay sums: 16-byte asynchronous
+    // copies, all in flight together
+    for (int e = tid; e < C * DK / 4; e += kScanThreads) {
+      const int t = e / (DK / 4), c = 4 * (e % (DK / 4));
       const float* row = qk + ((size_t(t0 + t) * hk + kh) * 2) * DK;
-      Ws[t * P + c] = W[sc * C * DK + e];
-      Qs[t * P + c] = t < n ? row[c] : 0.f;
-      Ks[t * P + c] = t < n ? row[DK + c] : 0.f;
+      cp16(Ws + t * PW + c, W + sc * C * DK + size_t(t) * DK + c, true);
+      cp16(Qs + t * PW + c, t < n ? row + c : qk, t < n);
+      cp16(Ks + t * PW + c, t < n ? row + DK + c : qk, t < n);
     }
-    for (int e = tid; e < C * C; e += kScanThreads) As[(e / C) * (C + 1) + e % C] = A[sc * C * C + e];
-    for (int e = tid; e < C * kScanRows; e += kScanThreads) {
-      const int t = e / kScanRows, r = e % kScanRows;
-      Us[t * RP + r] = U[sc * C * DV + size_t(t) * DV + r0 + r];
+    for (int e = tid; e < C * C / 4; e += kScanThreads) {
+      const int t = e / (C / 4), i = 4 * (e % (C / 4));
+      cp16(As + t * PA + i, A + sc * C * C + size_t(t) * C + i, true);
     }
-    if (tid < C) lg[tid] = LG[sc * C + tid];
+    for (int e = tid; e < C * kScanRows / 4; e += kScanThreads) {
+      const int t = e / (kScanRows / 4), r = 4 * (e % (kScanRows / 4));
+      cp16(Us + t * PU + r, U + sc * C * DV + size_t(t) * DV + r0 + r, true);
+    }
+    if (tid < C / 4) cp16(lg + 4 * tid, LG + sc * C + 4 * tid, true);
+    cp_wait_all();
     __syncthreads();
-    float hacc[8], qacc[8];
+    // phase A: h = U - W s and q s for token `at`, rows aq + 8m
+    float hacc[MR], qacc[MR];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) hacc[m] = qacc[m] = 0.f;
+    for (int m = 0; m < MR; ++m) hacc[m] = qacc[m] = 0.f;
 #pragma unroll 4
-    for (int c = 0; c < DK; ++c) {
-      const float w = Ws[at * P + c], q = Qs[at * P + c];
+    for (int c4 = 0; c4 < C4; ++c4) {
+      const float4 w = f4(Ws + at * PW + 4 * c4), q = f4(Qs + at * PW + 4 * c4);
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const float s = S[(aq * 8 + m) * P + c];
-        hacc[m] = fmaf(w, s, hacc[m]);
-        qacc[m] = fmaf(q, s, qacc[m]);
+      for (int m = 0; m < MR; ++m) {
+        const float4 sv = f4(S + (aq + 8 * m) * PS + 4 * c4);
+        hacc[m] = dot4(w, sv, hacc[m]);
+        qacc[m] = dot4(q, sv, qacc[m]);
       }
     }
 #pragma unroll
-    for (int m = 0; m < 8; ++m) Hs[at * RP + aq * 8 + m] = Us[at * RP + aq * 8 + m] - hacc[m];
+    for (int m = 0; m < MR; ++m) Hs[at * RP + aq + 8 * m] = Us[at * PU + aq + 8 * m] - hacc[m];
     __syncthreads();
+    // phase B: outputs o = gamma_t q s + sum_{i <= t} A[t][i] h_i
     const float gt = expf(lg[at]);
-    float o[8];
+    float o[MR];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) o[m] = gt * qacc[m];
+    for (int m = 0; m < MR; ++m) o[m] = gt * qacc[m];
     for (int i = 0; i <= at; ++i) {
-      const float a = As[at * (C + 1) + i];
+      const float a = As[at * PA + i];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) o[m] = fmaf(a, Hs[i * RP + aq * 8 + m], o[m]);
+      for (int m = 0; m < MR; ++m) o[m] = fmaf(a, Hs[i * RP + aq + 8 * m], o[m]);
     }
     if (at < n) {
 #pragma unroll
-      for (int m = 0; m < 8; ++m) obuf[size_t(t0 + at) * vd + head * DV + r0 + aq * 8 + m] = o[m];
+      for (int m = 0; m < MR; ++m) obuf[size_t(t0 + at) * vd + head * DV + r0 + aq + 8 * m] = o[m];
     }
-    // next rows: S = gamma_C S + sum_t (gamma_C / gamma_t) h_t k_t^T
-    const float lc = lg[C - 1];
-    float acc[DK / 8];
+    // phase C: next rows S = gamma_C S + sum_t (gamma_C / gamma_t) h_t k_t^T
+    const float lc = lg[C - 1], gc = expf(lc);
+    float4 acc[MQ];
 #pragma unroll
-    for (int m = 0; m < DK / 8; ++m) acc[m] = expf(lc) * S[cr * P + cb + 8 * m];
+    for (int m = 0; m < MQ; ++m) {
+      const float4 sv = f4(S + cr * PS + 4 * (cb + 16 * m));
+      acc[m] = make_float4(gc * sv.x, gc * sv.y, gc * sv.z, gc * sv.w);
+    }
+#pragma unroll 4
     for (int t = 0; t < C; ++t) {
       const float f = expf(lc - lg[t]) * Hs[t * RP + cr];
 #pragma unroll
-      for (int m = 0; m < DK / 8; ++m) acc[m] = fmaf(f, Ks[t * P + cb + 8 * m], acc[m]);
+      for (int m = 0; m < MQ; ++m) {
+        const float4 kv = f4(Ks + t * PW + 4 * (cb + 16 * m));
+        acc[m].x = fmaf(f, kv.x, acc[m].x);
+        acc[m].y = fmaf(f, kv.y, acc[m].y);
+        acc[m].z = fmaf(f, kv.z, acc[m].z);
+        acc[m].w = fmaf(f, kv.w, acc[m].w);
+      }
     }
     __syncthreads();  // phase A's readers of S are done before it is overwritten
 #pragma unroll
-    for (int m = 0; m < DK / 8; ++m) S[cr * P + cb + 8 * m] = acc[m];
+    for (int m = 0; m < MQ; ++m) *reinterpret_cast<float4*>(S + cr * PS + 4 * (cb + 16 * m)) = acc[m];
   }
   __syncthreads();
   bool finite = true;
   for (int e = tid; e < kScanRows * DK; e += kScanThreads) {
     const int r = e / DK, c = e % DK;
-    const float v = S[r * P + c];
+    const float v = S[r * PS + c];
     finite &= isfinite(v);
     dst[size_t(r0 + r) * DK + c] = v;
   }
@@ -266,13 +356,13 @@ __global__ void __launch_bounds__(1024, 1)
 // Token-parallel preparation of long runs: CTA = (64-token chunk, key head),
 // one thread per channel of the key head (its q and k channels and its R
 // value heads' v channels), gdn_prep's arithmetic per token: causal conv +
-// SiLU, q / k RMS scaling (per-warp partials summed in a fixed order), decay
-// and beta. A chunk starts from the K-1 inputs before it: earlier tokens of
+// SiLU and q / k RMS scaling (per-warp partials summed in a fixed order); the
+// decay and beta come from gdn_chunk_prep. A chunk starts from the K-1 inputs before it: earlier tokens of
 // the run (their projection rows) or the parent's conv history. The child's
 // history is written afterwards by gdn_conv_tail (a consumed parent's history
 // is the child's, so it must not change while any chunk still reads it).
 template <int DK, int DV, int R>
-__global__ void __launch_bounds__(2 * DK + R * DV, 2)
+__global__ void __launch_bounds__(2 * DK + R * DV, 1)
     gdn_run_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
                         const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens,
                         const int32_t* __restrict__ items, GdnPool pool, int li, int hk, int hv, int conv,
@@ -283,11 +373,13 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 2)
   pdl_wait();
   constexpr int QW = DK / 32;
   __shared__ float red[2][2 * QW];
-  const int item = blockIdx.x, kh = blockIdx.y;
+  constexpr int SUB = C / kRunBlock;
+  const int item = blockIdx.x / SUB, kh = blockIdx.y;
   const int seq = items[2 * item], chunk = items[2 * item + 1];
   const SeqDesc d = descs[seq];
-  const int s0 = cu_seqlens[seq], c0 = chunk * C;
-  const int n = min(C, d.count - c0);
+  const int s0 = cu_seqlens[seq], c0 = chunk * C + (blockIdx.x % SUB) * kRunBlock;
+  const int n = min(kRunBlock, d.count - c0);
+  if (n <= 0) return;
   const int kd = hk * DK, vd = hv * DV, cd = 2 * kd + vd;
   const int c = threadIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gc = c < DK ? kh * DK + c : (c < 2 * DK ? kd + kh * DK + (c - DK) : 2 * kd + kh * R * DV + (c - 2 * DK));
@@ -307,14 +399,20 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 2)
   for (int j = 0; j < 8; ++j)
     if (j == conv - 1) cw_last = cw[j];
   const int R_ = R;
-  const int gh = kh * R_ + (c < R_ ? c : 0);
-  const float gdt = c < R_ ? dt_bias[gh] : 0.f, galog = c < R_ ? a_log[gh] : 0.f;
+  constexpr int G = 8;  // tokens whose inputs are requested together, ahead of their barriers
+  static_assert(kRunBlock % G == 0, "run block is whole request groups");
+  float cur_g[G];
   for (int i = 0; i < n; ++i) {
     const int t = s0 + c0 + i;
-    const float* pr = proj + size_t(t) * ld;
-    const float cur = split_sum_c(pr, gc, splits, split_stride);
-    const float ga = c < R_ ? split_sum_c(pr, cd + vd + gh, splits, split_stride) : 0.f;
-    const float gbeta = c < R_ ? split_sum_c(pr, cd + vd + hv + gh, splits, split_stride) : 0.f;
+    if ((i % G) == 0) {
+#pragma unroll
+      for (int k = 0; k < G; ++k)
+        cur_g[k] = split_sum_c(proj + size_t(s0 + c0 + min(i + k, n - 1)) * ld, gc, splits, split_stride);
+    }
+    float cur = 0.f;
+#pragma unroll
+    for (int k = 0; k < G; ++k)
+      if (k == i % G) cur = cur_g[k];
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < 7; ++j)
@@ -338,12 +436,6 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 2)
       float* dstq = qk_out + ((size_t(t) * hk + kh) * 2) * DK;
       if (c < DK) dstq[c] = act * (rinv / DK);
       else dstq[DK + (c - DK)] = act * (rinv * rsqrtf(float(DK)));
-    }
-    if (c < R_) {
-      const float av = ga + gdt;
-      const float sp = fmaxf(av, 0.f) + log1pf(__expf(-fabsf(av)));
-      gb_out[(size_t(t) * hv + gh) * 2 + 0] = expf(-expf(galog) * sp);
-      gb_out[(size_t(t) * hv + gh) * 2 + 1] = sigmoidf_(gbeta);
     }
   }
 }
@@ -372,8 +464,8 @@ void launch_chunked(const GdnChunkPlan& cp, const Dims& d, const LayerDev& ly, c
                     int li, gemm_in_t* out, uint32_t* err, const float* qk_buf, float* v_buf, const float* gb_buf,
                     cudaStream_t s) {
   constexpr size_t prep_smem = (2 * C * (DK + 1) + C * (C + 1)) * sizeof(float);
-  constexpr size_t scan_smem =
-      (3 * C * (DK + 1) + C * (C + 1) + kScanRows * (DK + 1) + 2 * C * (kScanRows + 1)) * sizeof(float);
+  constexpr size_t scan_smem = (3 * C * (DK + 4) + C * (C + 4) + kScanRows * (DK + 4) + C * (kScanRows + 4) +
+                                C * (kScanRows + 1)) * sizeof(float);
   static_assert(prep_smem <= 227 * 1024 && scan_smem <= 227 * 1024, "chunked DeltaNet shared memory");
   static std::atomic<uint64_t> set{0};
   once_per_device(set, [] {
@@ -383,7 +475,8 @@ void launch_chunked(const GdnChunkPlan& cp, const Dims& d, const LayerDev& ly, c
                                    int(scan_smem)));
   });
   launch_pdl(gdn_chunk_prep_kernel<DK, DV>, dim3(cp.n_items, d.hv), DK + DV, prep_smem, s, descs, cu_seqlens,
-             cp.items, d.hk, d.hv, qk_buf, v_buf, gb_buf, cp.U, cp.W, cp.A, cp.LG);
+             cp.items, d.hk, d.hv, qk_buf, v_buf, proj, ld_proj, splits, split_stride, d.cd, ly.a_log, ly.dt_bias,
+             cp.U, cp.W, cp.A, cp.LG);
   launch_pdl(gdn_chunk_scan_kernel<DK, DV>, cp.n_long * d.hv * (DV / kScanRows), kScanThreads, scan_smem, s, descs,
              cu_seqlens, cp.longs, pool, li, d.hk, d.hv, qk_buf, cp.U, cp.W, cp.A, cp.LG, v_buf, err);
   launch_pdl(gdn_chunk_norm_kernel<DV>, cp.n_tokens, 32 * d.hv, 0, s, cp.tokens, d.hv, v_buf, proj, ld_proj, splits,
@@ -401,7 +494,8 @@ void launch_gdn_run_prep(const GdnChunkPlan& cp, const Dims& d, const LayerDev& 
   if (d.conv > 8 || d.conv < 2) throw std::invalid_argument("conv kernel width unsupported");
   const int R = d.hv / d.hk;
   auto go = [&](auto kernel, int threads) {
-    launch_pdl(kernel, dim3(cp.n_items, d.hk), threads, 0, s, proj, ld_proj, splits, split_stride, descs, cu_seqlens,
+    launch_pdl(kernel, dim3(cp.n_items * (C / kRunBlock), d.hk), threads, 0, s, proj, ld_proj, splits, split_stride,
+               descs, cu_seqlens,
                cp.items, pool, li, d.hk, d.hv, d.conv, ly.conv_w, ly.a_log, ly.dt_bias, qk_buf, v_buf, gb_buf);
   };
   if (d.dk == 128 && d.dv == 128 && R == 2) go(gdn_run_prep_kernel<128, 128, 2>, 2 * 128 + 2 * 128);

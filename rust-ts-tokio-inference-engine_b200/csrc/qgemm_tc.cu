@@ -78,6 +78,11 @@ __device__ __forceinline__ void deq_word(uint32_t w, uint32_t m, uint32_t s2, ui
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(out[3]) : "r"(c3), "r"(s2), "r"(b2));
 }
 
+// Token groups of a dense launch (1 when the tokens are not split).
+__host__ __device__ __forceinline__ int dense_token_groups(const TcArgs& a) {
+  return a.token_group > 0 ? (a.n_tokens + a.token_group - 1) / a.token_group : 1;
+}
+
 struct Work {
   int rt;       // global row tile of W
   int c0, c1;   // chunk range
@@ -93,14 +98,17 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* g
   Work w;
   const int kc = a.W.k_chunks();
   if (a.mode == kGemmStoreF32) {
+    // item = (row tile, split, token group), row tile fastest
     w.rt = i % a.W.row_tiles;
-    w.g = i / a.W.row_tiles;  // split
+    const int rest = i / a.W.row_tiles;
+    w.g = rest % a.splits;  // split
     w.rt_local = w.rt;
     const int per = (kc + a.splits - 1) / a.splits;
     w.c0 = w.g * per;
     w.c1 = min(kc, w.c0 + per);
-    w.p0 = 0;
-    w.p1 = a.n_tokens;
+    const int tg = rest / a.splits;
+    w.p0 = a.token_group > 0 ? tg * a.token_group : 0;
+    w.p1 = a.token_group > 0 ? min(a.n_tokens, w.p0 + a.token_group) : a.n_tokens;
   } else {
     w.g = act[i / a.expert_tiles];
     w.rt_local = i % a.expert_tiles;
@@ -186,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int total = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : act[kMaxGroups] * a.expert_tiles;
+  const int total = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits * dense_token_groups(a)
+                                             : act[kMaxGroups] * a.expert_tiles;
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
@@ -439,7 +448,10 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   once_per_device(configured, [] {
     QWEN_CUDA(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
   });
-  const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits : a.groups * a.expert_tiles;
+  if (a.mode == kGemmStoreF32 && a.token_group > 0 && (a.token_group % a.box_rows || a.splits != 1))
+    throw std::invalid_argument("GEMM token groups must be whole boxes, without split-K");
+  const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits * dense_token_groups(a)
+                                            : a.groups * a.expert_tiles;
   const int grid = std::max(1, std::min(items, sm_count));
   if (smem > 227 * 1024) throw std::invalid_argument("tcgen05 GEMM shared memory above 227 KB");
   launch_pdl(qgemm_tc_kernel, grid, kThreads, smem, s, bmap, a);

@@ -15,6 +15,8 @@ struct TcArgs {
   int n_tokens = 0;                    // dense: token rows
   int splits = 1;                      // dense: split-K slices (partials at Y + split*split_stride)
   size_t split_stride = 0;
+  int token_group = 0;                 // dense: tokens per work item (0 = all; many-token steps
+                                       // split the tokens instead of K)
   int b_row0 = 0;      // first activation row of the B tensor map
   int box_rows = 16;   // N tile: 16, 32, 64 or 128 (the tensor map's box height)
   int stages = 0;      // TMEM A stages in chunks (set by the launcher)

@@ -219,11 +219,17 @@ struct Session {
     a.n_tokens = T;
     a.box_rows = box_for(std::min(T, 128));
     const int kc = W.k_chunks();
-    // split-K: enough items for ~2 waves, slices of whole 4-chunk units when possible
-    const int want = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc}));
     int splits = 1;
-    for (int sp = want; sp >= 1; --sp)
-      if (kc % sp == 0 && (kc / sp) % 4 == 0) { splits = sp; break; }
+    if (T > 128) {
+      // many tokens: one 128-token block per work item, no split-K (the
+      // weights of a row tile are re-read from L2 by each block)
+      a.token_group = 128;
+    } else {
+      // split-K: enough items for ~2 waves, slices of whole 4-chunk units when possible
+      const int want = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc}));
+      for (int sp = want; sp >= 1; --sp)
+        if (kc % sp == 0 && (kc / sp) % 4 == 0) { splits = sp; break; }
+    }
     a.splits = splits;
     a.split_stride = split_stride;
     a.Y = Y;
