@@ -168,11 +168,13 @@ __global__ void __launch_bounds__(DK + DV)
   float x[C];
   const bool is_u = tid < DV;
   const int col = is_u ? tid : tid - DV;
+  // right-hand sides: this thread's column of beta V (values, loaded up front)
+  // or of beta gamma K (keys)
+#pragma unroll
+  for (int t = 0; t < C; ++t) x[t] = (is_u && t < n) ? vv[size_t(t0 + t) * vd + head * DV + col] : 0.f;
 #pragma unroll
   for (int t = 0; t < C; ++t) {
-    float b;
-    if (is_u) b = t < n ? beta[t] * vv[size_t(t0 + t) * vd + head * DV + col] : 0.f;
-    else b = beta[t] * expf(lg[t]) * Ks[t * P + col];
+    const float b = is_u ? beta[t] * x[t] : beta[t] * expf(lg[t]) * Ks[t * P + col];
     float part[4] = {b, 0.f, 0.f, 0.f};  // four independent chains
 #pragma unroll
     for (int i = 0; i < t; ++i) part[i & 3] = fmaf(-L[t * (C + 1) + i], x[i], part[i & 3]);
@@ -399,7 +401,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 1)
   for (int j = 0; j < 8; ++j)
     if (j == conv - 1) cw_last = cw[j];
   const int R_ = R;
-  constexpr int G = 8;  // tokens whose inputs are requested together, ahead of their barriers
+  constexpr int G = kRunBlock;  // tokens whose inputs are requested together, ahead of their barriers
   static_assert(kRunBlock % G == 0, "run block is whole request groups");
   float cur_g[G];
   for (int i = 0; i < n; ++i) {
