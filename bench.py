@@ -659,7 +659,8 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps,
-        "p50_step_ms": statistics.median(step_ms), "higher_is_better": True,
+        "p50_step_ms": statistics.median(step_ms), "step_ms": [round(x, 3) for x in step_ms],
+        "higher_is_better": True,
         "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f16",
         "dtype_note": "projection operands IEEE half (4-bit weights dequantised with one rounding to 11 significant "
                       "bits, activations likewise), fp32 accumulation, fp32 recurrent state, bf16 KV cache",

@@ -1,4 +1,5 @@
-// Paged GQA attention for decode and chunked prefill (flash-decoding).
+// Paged GQA attention: the split decode kernel (flash-decoding) and the
+// chunked-prefill kernel below.
 //
 // CTA = (work item, kv head g), kAttnWarps warps. A work item is one (query token t,
 // KV split) pair from a host-built list holding only the splits that token
@@ -14,10 +15,12 @@
 // output gate. Keys at positions >= pos(t)+1 are masked (causal, bottom-right).
 #include <cuda.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cfloat>
 
 #include "kernels.h"
+#include "qgemm_tc.h"
 
 namespace qwen {
 
@@ -38,6 +41,9 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -296,7 +302,232 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   }
 }
 
+// Chunked-prefill attention: CTA = (block of consecutive query tokens of one
+// sequence, kv head g), kPfWarps warps. Warp w owns 16 query rows: tokens
+// w*16/G .. of the block, each with the G query heads of kv head g (row r =
+// token r / G, head r % G). Every K/V page of the block's prefix is loaded ONCE
+// per CTA into a shared ring (one TMA per 64 head dims, K and V, 128B swizzle)
+// and read by all warps, so a page crosses L2 once per (block, kv head)
+// instead of once per query token. Per page a warp computes S = Q K^T (16 rows
+// x 16 keys), the causal mask (key position <= the row token's position), the
+// online softmax and O += P V with mma.sync (bf16 operands, fp32 accumulators),
+// exactly like the decode kernel. Every warp releases a page it has read
+// (empty barrier, one arrival per warp); lane 0 of warp 0 refills the slot.
+// Pages are taken in increasing order and key 0 is visible to every token, so
+// a row's running maximum is finite from the first page on. The epilogue
+// divides by the row sum, applies the output gate sigmoid(gate) and writes the
+// fp16 o_proj input; these tokens skip attention_merge_kernel.
+constexpr int kPfWarps = kAttnPrefillWarps;
+constexpr int kPfStages = 4;
+
+template <int D>
+__global__ void __launch_bounds__(kPfWarps * 32, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap kvmap, const float* __restrict__ q,
+                        const int32_t* __restrict__ token_pos, const SeqDesc* __restrict__ descs,
+                        const int32_t* __restrict__ block_table, int stride, const int4* __restrict__ blocks,
+                        int Hq, int Hkv, int G, const float* __restrict__ gate, gemm_in_t* __restrict__ out,
+                        uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int KS = D / 16;
+  constexpr int NT = D / 8;
+  constexpr int TILE = 16 * D * 2;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;  // [kPfStages][K tile, V tile]; first holds the warps' Q tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + size_t(max(kPfStages * 2, kPfWarps)) * TILE);
+  uint64_t* empty = full + kPfStages;
+
+  const int4 blk = blocks[blockIdx.x];  // first packed token, tokens, sequence, pages
+  const int t0 = blk.x, n_tok = blk.y, n_pages = blk.w, g = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tpw = 16 / G;  // tokens per warp
+  const int32_t* row = block_table + size_t(descs[blk.z].child) * stride;
+
+  // Q tiles (rows r: token w*tpw + r/G, head g*G + r%G), scaled by log2(e)/sqrt(D)
+  const float qscale = 1.4426950408889634f * rsqrtf(float(D));
+  for (int e = threadIdx.x; e < kPfWarps * 16 * (D / 8); e += blockDim.x) {
+    const int w = e / (16 * (D / 8)), rem = e % (16 * (D / 8));
+    const int r = rem / (D / 8), chunk = rem % (D / 8);
+    const int tl = w * tpw + r / G;
+    uint32_t v[4] = {0, 0, 0, 0};
+    if (tl < n_tok) {
+      const float* src = q + (size_t(t0 + tl) * Hq + g * G + r % G) * D + chunk * 8;
+      const float4 x0 = *reinterpret_cast<const float4*>(src), x1 = *reinterpret_cast<const float4*>(src + 4);
+      v[0] = pack_bf16(x0.x * qscale, x0.y * qscale);
+      v[1] = pack_bf16(x0.z * qscale, x0.w * qscale);
+      v[2] = pack_bf16(x1.x * qscale, x1.y * qscale);
+      v[3] = pack_bf16(x1.z * qscale, x1.w * qscale);
+    }
+    *reinterpret_cast<uint4*>(ring + size_t(w) * TILE + sw_off(r, chunk)) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+  if (threadIdx.x < kPfStages) {
+    mbar_init(&full[threadIdx.x], 1);
+    mbar_init(&empty[threadIdx.x], kPfWarps);
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  __syncthreads();
+  uint32_t qa[KS][4];
+  {
+    const int r = lane & 15, cadd = lane >> 4;
+    const uint32_t qt = smem_u32(ring + size_t(warp) * TILE);
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) ldsm_x4(qt + sw_off(r, ks * 2 + cadd), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  }
+  __syncthreads();  // the Q tiles are in registers: the ring is free
+  auto issue = [&](int page_local, int stage) {
+    const int page = row[page_local];
+    const int yk = ((page * 2 + 0) * Hkv + g) * kPageTokens;
+    const int yv = ((page * 2 + 1) * Hkv + g) * kPageTokens;
+    uint8_t* kt = ring + size_t(stage) * 2 * TILE;
+    mbar_expect_tx(&full[stage], 2 * TILE);
+#pragma unroll
+    for (int b = 0; b < D / 64; ++b) {
+      tma_load_2d(kt + b * 16 * 128, &kvmap, b * 64, yk, &full[stage]);
+      tma_load_2d(kt + TILE + b * 16 * 128, &kvmap, b * 64, yv, &full[stage]);
+    }
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kPfStages && i < n_pages; ++i) issue(i, i);
+
+  // positions of this lane's two rows (-1: past the block's last token)
+  const int r0 = lane >> 2, r1 = r0 + 8;
+  const int tl0 = warp * tpw + r0 / G, tl1 = warp * tpw + r1 / G;
+  const int pos0 = tl0 < n_tok ? token_pos[t0 + tl0] : -1;
+  const int pos1 = tl1 < n_tok ? token_pos[t0 + tl1] : -1;
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
+  bool ok = true;
+  int stalled = 0;
+  for (int i = 0; i < n_pages; ++i) {
+    const int stage = i % kPfStages;
+    if (!mbar_wait_bounded(&full[stage], (i / kPfStages) & 1, err)) { ok = false; stalled = i; break; }
+    const uint32_t kt = smem_u32(ring + size_t(stage) * 2 * TILE), vt = kt + TILE;
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int krow = (lane & 7) + ((lane >> 4) << 3), cadd = (lane >> 3) & 1;
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kt + sw_off(krow, ks * 2 + cadd), b0, b1, b2, b3);
+        mma_bf16(s0, qa[ks], b0, b1);
+        mma_bf16(s1, qa[ks], b2, b3);
+      }
+    }
+    const int key0 = i * kPageTokens + (lane & 3) * 2;
+    if (key0 + 0 > pos0) s0[0] = -FLT_MAX;
+    if (key0 + 1 > pos0) s0[1] = -FLT_MAX;
+    if (key0 + 0 > pos1) s0[2] = -FLT_MAX;
+    if (key0 + 1 > pos1) s0[3] = -FLT_MAX;
+    if (key0 + 8 > pos0) s1[0] = -FLT_MAX;
+    if (key0 + 9 > pos0) s1[1] = -FLT_MAX;
+    if (key0 + 8 > pos1) s1[2] = -FLT_MAX;
+    if (key0 + 9 > pos1) s1[3] = -FLT_MAX;
+    float mx0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1]));
+    float mx1 = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    const float e00 = exp2f(s0[0] - mn0), e01 = exp2f(s0[1] - mn0), e02 = exp2f(s0[2] - mn1), e03 = exp2f(s0[3] - mn1);
+    const float e10 = exp2f(s1[0] - mn0), e11 = exp2f(s1[1] - mn0), e12 = exp2f(s1[2] - mn1), e13 = exp2f(s1[3] - mn1);
+    float rs0 = e00 + e01 + e10 + e11, rs1 = e02 + e03 + e12 + e13;
+    rs0 += __shfl_xor_sync(0xffffffffu, rs0, 1);
+    rs0 += __shfl_xor_sync(0xffffffffu, rs0, 2);
+    rs1 += __shfl_xor_sync(0xffffffffu, rs1, 1);
+    rs1 += __shfl_xor_sync(0xffffffffu, rs1, 2);
+    l0 = l0 * c0 + rs0;
+    l1 = l1 * c1 + rs1;
+    const uint32_t pa[4] = {pack_bf16(e00, e01), pack_bf16(e02, e03), pack_bf16(e10, e11), pack_bf16(e12, e13)};
+    {
+      const int vrow = (lane & 7) + (((lane >> 3) & 1) << 3), cadd = lane >> 4;
+#pragma unroll
+      for (int nt = 0; nt < NT; nt += 2) {
+        o[nt][0] *= c0; o[nt][1] *= c0; o[nt][2] *= c1; o[nt][3] *= c1;
+        o[nt + 1][0] *= c0; o[nt + 1][1] *= c0; o[nt + 1][2] *= c1; o[nt + 1][3] *= c1;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vt + sw_off(vrow, nt + cadd), b0, b1, b2, b3);
+        mma_bf16(o[nt], pa, b0, b1);
+        mma_bf16(o[nt + 1], pa, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (warp == 0 && i + kPfStages < n_pages) {
+      // refill this slot once every warp has left page i
+      if (!mbar_wait_bounded(&empty[stage], (i / kPfStages) & 1, err)) { ok = false; stalled = i + 1; break; }
+      if (lane == 0) issue(i + kPfStages, stage);
+      __syncwarp();
+    }
+  }
+  if (!ok) {
+    // timed out: let the page loads in flight land before the CTA leaves
+    __syncwarp();
+    if (lane == 0)
+      for (int j = stalled; j < min(n_pages, stalled + kPfStages); ++j)
+        mbar_wait_bounded(&full[j % kPfStages], (j / kPfStages) & 1, err);
+  }
+  // epilogue: O / l * sigmoid(gate) -> fp16 rows of the o_proj input
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const int h0 = g * G + r0 % G, h1 = g * G + r1 % G;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int col = nt * 8 + (lane & 3) * 2;
+    if (pos0 >= 0) {
+      const size_t off = (size_t(t0 + tl0) * Hq + h0) * D + col;
+      const float2 gt = *reinterpret_cast<const float2*>(gate + off);
+      *reinterpret_cast<__half2*>(out + off) =
+          to_gemm_in2(o[nt][0] * inv0 * sigmoidf_(gt.x), o[nt][1] * inv0 * sigmoidf_(gt.y));
+    }
+    if (pos1 >= 0) {
+      const size_t off = (size_t(t0 + tl1) * Hq + h1) * D + col;
+      const float2 gt = *reinterpret_cast<const float2*>(gate + off);
+      *reinterpret_cast<__half2*>(out + off) =
+          to_gemm_in2(o[nt][2] * inv1 * sigmoidf_(gt.x), o[nt][3] * inv1 * sigmoidf_(gt.y));
+    }
+  }
+}
+
 }  // namespace
+
+size_t attn_prefill_smem(int D) {
+  const size_t tile = 16 * size_t(D) * 2;
+  return 1024 + size_t(std::max(kPfStages * 2, kPfWarps)) * tile + 2 * kPfStages * 8;
+}
+
+void launch_attn_prefill(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_pos,
+                         const SeqDesc* descs, const int32_t* block_table, int bt_stride, const int4* blocks,
+                         int n_blocks, const float* gate, gemm_in_t* out, uint32_t* err, cudaStream_t s) {
+  const int G = d.Hq / d.Hkv;
+  if (G < 1 || G > 16 || 16 % G) throw std::invalid_argument("prefill attention needs 16 % (query heads per KV head) == 0");
+  if (n_blocks <= 0) return;
+  dim3 grid(n_blocks, d.Hkv);
+  const size_t smem = attn_prefill_smem(d.D);
+#define QWEN_ATTN_PF(DD)                                                                                      \
+  if (d.D == DD) {                                                                                          \
+    static std::atomic<uint64_t> cfg_##DD{0};                                                               \
+    once_per_device(cfg_##DD, [&] {                                                                         \
+      QWEN_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                     int(smem)));                                                           \
+    });                                                                                                     \
+    launch_pdl(attn_prefill_kernel<DD>, grid, kPfWarps * 32, smem, s, kvmap, q, token_pos, descs, block_table, \
+               bt_stride, blocks, d.Hq, d.Hkv, G, gate, out, err);                                            \
+    QWEN_CUDA(cudaGetLastError());                                                                          \
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);                                              \
+    return;                                                                                                 \
+  }
+  QWEN_ATTN_PF(256)
+  QWEN_ATTN_PF(128)
+  QWEN_ATTN_PF(64)
+#undef QWEN_ATTN_PF
+  throw std::invalid_argument("head_dim must be 64, 128 or 256");
+}
 
 size_t attn_decode_smem(int D) {
   const size_t tile = 16 * size_t(D) * 2;

@@ -313,15 +313,16 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
 // Merge split partials, apply the output gate sigmoid(gate), write fp16 (the o_proj input).
 // The split weights exp(m_s - M) / sum_s l_s exp(m_s - M) are computed once
 // per (token, head) into shared memory (dynamic: max_splits floats).
+// tokens: the step's tokens that ran the split decode kernel (null: all of them).
 __global__ void attention_merge_kernel(const float* __restrict__ ws, const float* __restrict__ gate,
-                                       const int32_t* __restrict__ token_pos, int Hq, int D, int spl,
-                                       int max_splits, gemm_in_t* out) {
+                                       const int32_t* __restrict__ token_pos, const int32_t* __restrict__ tokens,
+                                       int Hq, int D, int spl, int max_splits, gemm_in_t* out) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float wsplit[];
   __shared__ float red[32];
   __shared__ float s_max, s_den;
-  const int t = blockIdx.x, h = blockIdx.y;
+  const int t = tokens ? tokens[blockIdx.x] : blockIdx.x, h = blockIdx.y;
   const int n = (token_pos[t] + 1 + spl - 1) / spl;
   const float* base = ws + (size_t(t) * Hq + h) * max_splits * (D + 2);
   float m = -FLT_MAX;
@@ -925,12 +926,12 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
   throw std::invalid_argument("head_dim must be 64, 128 or 256");
 }
 
-void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int split_pages, int max_splits, gemm_in_t* out, cudaStream_t s) {
+void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos,
+                            const int32_t* tokens, int T, int split_pages, int max_splits, gemm_in_t* out,
+                            cudaStream_t s) {
   if (T <= 0) return;
   launch_pdl(attention_merge_kernel, dim3(T, d.Hq), 128, size_t(max_splits) * sizeof(float), s, ws, gate, token_pos,
-             d.Hq, d.D, split_pages * kPageTokens,
-                                                       max_splits, out);
+             tokens, d.Hq, d.D, split_pages * kPageTokens, max_splits, out);
   count_launch();
 }
 

@@ -44,8 +44,19 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
                         const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
                         const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
                         cudaStream_t s);
-void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos, int T,
-                            int split_pages, int max_splits, gemm_in_t* out, cudaStream_t s);
+// Merges the split partials of `T` tokens (the listed token indices, or
+// 0..T-1 when `tokens` is null) and applies the output gate.
+void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos,
+                            const int32_t* tokens, int T, int split_pages, int max_splits, gemm_in_t* out,
+                            cudaStream_t s);
+// Chunked-prefill attention (attention.cu): blocks[i] = (first packed token,
+// tokens, sequence, pages) of kAttnPrefillWarps * 16 / G consecutive tokens of
+// one sequence; writes the gated fp16 o_proj input of those tokens.
+constexpr int kAttnPrefillWarps = 8;
+constexpr int kAttnPrefillMin = 16;  // tokens a sequence feeds before its attention takes the prefill kernel
+void launch_attn_prefill(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_pos,
+                         const SeqDesc* descs, const int32_t* block_table, int bt_stride, const int4* blocks,
+                         int n_blocks, const float* gate, gemm_in_t* out, uint32_t* err, cudaStream_t s);
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s);
 size_t qgemm_tc_smem(int box_rows, int stages, int unit);
 int qgemm_tc_stages(int box_rows);

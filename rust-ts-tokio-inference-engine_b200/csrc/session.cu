@@ -86,6 +86,11 @@ struct DevBuf {
     QWEN_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
     n = count;
   }
+  // per-step buffers whose size varies from step to step: grow with headroom,
+  // so the (device-synchronising) reallocation stays rare
+  void ensure_grow(size_t count) {
+    if (count > n) ensure(count + count / 2);
+  }
 };
 
 template <class T>
@@ -101,6 +106,9 @@ struct PinBuf {
     p = nullptr;
     QWEN_CUDA(cudaMallocHost(&p, std::max<size_t>(count, 1) * sizeof(T)));
     n = count;
+  }
+  void ensure_grow(size_t count) {
+    if (count > n) ensure(count + count / 2);
   }
 };
 
@@ -155,6 +163,8 @@ struct Session {
   DevBuf<float> x, proj, partial, q, gate, attn_ws, weights, moe_y, logits, hidden_stage;
   DevBuf<float> gdn_qk, gdn_v, gdn_gb;  // DeltaNet prepared q/k, v, (decay, beta) per token
   DevBuf<int2> attn_items;              // attention work list: (token, KV split) pairs
+  DevBuf<int4> pf_dev;                  // chunked-prefill attention blocks
+  DevBuf<int32_t> merge_dev;            // tokens of the split decode attention (when some run the prefill kernel)
   DevBuf<uint64_t> argmax_part;         // per-row slice maxima of the split argmax
   DevBuf<uint32_t> argmax_done;         // per-row slice counters (kept at zero between launches)
   // speculative verify: per-token candidate state slots, EOS list, accept results
@@ -176,7 +186,7 @@ struct Session {
   size_t mpage_bytes = 0;
   size_t draft_residents() const { return drafts ? drafts->residents() : 0; }
   uint64_t draft_bytes() const { return drafts ? drafts->bytes() : 0; }
-  int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1;
+  int attn_split_pages = 16, attn_n_items = 0, attn_splits = 1, pf_n_blocks = 0, n_merge = 0;
   DevBuf<gemm_in_t> hb, hb2, act, xperm, hb_out;  // projection inputs (fp16)
   int sm_count = 148;
   int cur_layer = 0;
@@ -554,23 +564,50 @@ struct Session {
     // Attention work list. A split spans enough pages to amortise its CTA's
     // query load and warp merge (16..64 pages) while leaving at least four
     // CTAs per SM; each token gets one item per split its keys reach.
+    // Sequences that feed at least kAttnPrefillMin tokens run the chunked-prefill
+    // kernel (blocks of consecutive tokens sharing each K/V page load, longest
+    // prefixes first); the decode kernel and the split merge take the rest.
     std::vector<int2> items;
+    std::vector<int4> pf_blocks;
+    std::vector<int32_t> merge_tokens;
+    attn_n_items = pf_n_blocks = 0;
     if (d.n_attn > 0) {
+      const int G = d.Hq / d.Hkv;
+      const bool pf_ok = G >= 1 && G <= 16 && 16 % G == 0;
+      const int QB = pf_ok ? kAttnPrefillWarps * (16 / G) : 0;
+      auto prefill = [&](const SeqIn& s) { return pf_ok && s.count >= uint32_t(kAttnPrefillMin); };
       int64_t page_heads = 0;
       for (const auto& s : seqs)
-        for (uint32_t j = 0; j < s.count; ++j) page_heads += (int64_t(s.position) + j + kPageTokens) / kPageTokens;
+        if (!prefill(s))
+          for (uint32_t j = 0; j < s.count; ++j) page_heads += (int64_t(s.position) + j + kPageTokens) / kPageTokens;
       page_heads *= d.Hkv;
       int sp = 16;
       while (sp < 64 && page_heads / (2 * sp) >= int64_t(sm_count) * 4) sp *= 2;
       attn_split_pages = sp;
       attn_splits = std::max(1, (max_len + sp * kPageTokens - 1) / (sp * kPageTokens));
       int t = 0;
-      for (const auto& s : seqs)
+      for (int i = 0; i < n; ++i) {
+        const SeqIn& s = seqs[i];
+        if (prefill(s)) {
+          for (int j0 = 0; j0 < int(s.count); j0 += QB) {
+            const int nb = std::min(QB, int(s.count) - j0);
+            const int last = int(s.position) + j0 + nb - 1;
+            pf_blocks.push_back(make_int4(t + j0, nb, i, last / kPageTokens + 1));
+          }
+          t += int(s.count);
+          continue;
+        }
         for (uint32_t j = 0; j < s.count; ++j, ++t) {
           const int pages = int((int64_t(s.position) + j + kPageTokens) / kPageTokens);
           for (int k = 0; k * sp < pages; ++k) items.push_back(make_int2(t, k));
+          merge_tokens.push_back(t);
         }
+      }
+      std::stable_sort(pf_blocks.begin(), pf_blocks.end(), [](const int4& x, const int4& y) { return x.w > y.w; });
       attn_n_items = int(items.size());
+      pf_n_blocks = int(pf_blocks.size());
+      n_merge = int(merge_tokens.size());
+      if (pf_blocks.empty()) merge_tokens.clear();  // every token merges: no list needed
     }
     if (R > max_rows) throw std::invalid_argument("ragged step exceeds the output-row budget");
     // DeltaNet runs of at least kGdnChunkMin tokens (not verify steps) take the chunked kernels
@@ -628,7 +665,8 @@ struct Session {
       throw std::runtime_error("combined resident budget exhausted");
 
     // page planning (host), descriptors
-    staging.ensure(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64 + items.size() * 8);
+    staging.ensure_grow(sizeof(SeqDesc) * n + 4 * (size_t(T) + n + T / kPageTokens + 16) + 64 + items.size() * 8 +
+                        16 + pf_blocks.size() * 16 + merge_tokens.size() * 4);
     SeqDesc* hd = reinterpret_cast<SeqDesc*>(staging.p);
     std::vector<int32_t> npages;
     std::vector<std::vector<int32_t>> child_pages(n);
@@ -744,6 +782,10 @@ struct Session {
     for (int i = 0; i < n; ++i) std::memcpy(ht + tok_off[i], seqs[i].tokens, seqs[i].count * 4);
     int2* hi = reinterpret_cast<int2*>((reinterpret_cast<uintptr_t>(ht + T) + 7) & ~uintptr_t(7));
     if (!items.empty()) std::memcpy(hi, items.data(), items.size() * 8);
+    int4* hpf = reinterpret_cast<int4*>((reinterpret_cast<uintptr_t>(hi + items.size()) + 15) & ~uintptr_t(15));
+    if (!pf_blocks.empty()) std::memcpy(hpf, pf_blocks.data(), pf_blocks.size() * 16);
+    int32_t* hmt = reinterpret_cast<int32_t*>(hpf + pf_blocks.size());
+    if (!merge_tokens.empty()) std::memcpy(hmt, merge_tokens.data(), merge_tokens.size() * 4);
     try {
       QWEN_CUDA(cudaMemcpyAsync(descs.p, hd, sizeof(SeqDesc) * n, cudaMemcpyHostToDevice, stream));
       if (!npages.empty())
@@ -757,23 +799,31 @@ struct Session {
       }
       QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, stream));
       if (!items.empty()) {
-        attn_items.ensure(items.size());
+        attn_items.ensure_grow(items.size());
         QWEN_CUDA(cudaMemcpyAsync(attn_items.p, hi, items.size() * 8, cudaMemcpyHostToDevice, stream));
+      }
+      if (!pf_blocks.empty()) {
+        pf_dev.ensure_grow(pf_blocks.size());
+        QWEN_CUDA(cudaMemcpyAsync(pf_dev.p, hpf, pf_blocks.size() * 16, cudaMemcpyHostToDevice, stream));
+      }
+      if (!merge_tokens.empty()) {
+        merge_dev.ensure_grow(merge_tokens.size());
+        QWEN_CUDA(cudaMemcpyAsync(merge_dev.p, hmt, merge_tokens.size() * 4, cudaMemcpyHostToDevice, stream));
       }
       if (!gl_longs.empty()) {
         const size_t nl = gl_longs.size(), ni = gl_items.size(), nt = gl_tokens.size();
-        gplan_stage.ensure(nl + ni + nt);
-        gplan_dev.ensure(nl + ni + nt);
+        gplan_stage.ensure_grow(nl + ni + nt);
+        gplan_dev.ensure_grow(nl + ni + nt);
         std::memcpy(gplan_stage.p, gl_longs.data(), nl * 4);
         std::memcpy(gplan_stage.p + nl, gl_items.data(), ni * 4);
         std::memcpy(gplan_stage.p + nl + ni, gl_tokens.data(), nt * 4);
         QWEN_CUDA(cudaMemcpyAsync(gplan_dev.p, gplan_stage.p, (nl + ni + nt) * 4, cudaMemcpyHostToDevice, stream));
         uploads += (nl + ni + nt) * 4;
         const size_t units = ni / 2 * size_t(d.hv) * kGdnChunk;  // (chunk, head) pairs x chunk tokens
-        gplan_u.ensure(units * d.dv);
-        gplan_w.ensure(units * d.dk);
-        gplan_a.ensure(units * kGdnChunk);
-        gplan_lg.ensure(units);
+        gplan_u.ensure_grow(units * d.dv);
+        gplan_w.ensure_grow(units * d.dk);
+        gplan_a.ensure_grow(units * kGdnChunk);
+        gplan_lg.ensure_grow(units);
         gplan.n_long = int(nl / 3);
         gplan.n_items = int(ni / 2);
         gplan.n_tokens = int(nt);
@@ -787,13 +837,14 @@ struct Session {
       }
       if (!ch_host.empty()) {
         QWEN_CUDA(cudaStreamSynchronize(stream));  // the pinned stage may still feed the previous step's copy
-        choice_stage.ensure(ch_host.size());
-        choice_dev.ensure(ch_host.size());
+        choice_stage.ensure_grow(ch_host.size());
+        choice_dev.ensure_grow(ch_host.size());
         std::memcpy(choice_stage.p, ch_host.data(), ch_host.size() * 4);
         QWEN_CUDA(cudaMemcpyAsync(choice_dev.p, choice_stage.p, ch_host.size() * 4, cudaMemcpyHostToDevice, stream));
         uploads += ch_host.size() * 4;
       }
       uploads += sizeof(SeqDesc) * n + npages.size() * 4 + size_t(T) * 4 + items.size() * 8 +
+                 pf_blocks.size() * 16 + merge_tokens.size() * 4 +
                  (vin ? cand_host.size() * 4 + vin->n_eos * 4 : 0);
       const uint64_t t_graph = now_ns();
       ev_used = 0;
@@ -941,7 +992,10 @@ struct Session {
         launch_attn_decode(kv_maps[ly.type_index], d, q.p, token_seq.p, token_pos.p, descs.p, block_table.p,
                            bt_stride, attn_items.p, attn_n_items, attn_split_pages, attn_ws.p, attn_splits, err.p,
                            s);
-        launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, attn_split_pages, attn_splits, hb2.p, s);
+        launch_attn_prefill(kv_maps[ly.type_index], d, q.p, token_pos.p, descs.p, block_table.p, bt_stride,
+                            pf_dev.p, pf_n_blocks, gate.p, hb2.p, err.p, s);
+        launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, pf_n_blocks ? merge_dev.p : nullptr,
+                               pf_n_blocks ? n_merge : T, attn_split_pages, attn_splits, hb2.p, s);
         stage(8);  // AttentionOutput
       }
       const size_t out_stride = size_t(T) * d.H;
@@ -1223,7 +1277,7 @@ struct Session {
         for (int k = 0; k * 16 < (pos + j + kPageTokens) / kPageTokens; ++k) items.push_back(make_int2(j, k));
       const int splits = std::max(1, (pos + cnt + 16 * kPageTokens - 1) / (16 * kPageTokens));
       attn_ws.ensure(size_t(cnt) * d.Hq * splits * (d.D + 2));
-      attn_items.ensure(items.size());
+      attn_items.ensure_grow(items.size());
       cudaStream_t s = stream;
       QWEN_CUDA(cudaMemcpyAsync(descs.p, &sd, sizeof(sd), cudaMemcpyHostToDevice, s));
       if (n_new) QWEN_CUDA(cudaMemcpyAsync(new_pages.p, fresh.data(), size_t(n_new) * 4, cudaMemcpyHostToDevice, s));
@@ -1274,7 +1328,7 @@ struct Session {
     launch_attn_prep(d, ly, partial.p, aw, ps, astride, token_pos.p, slot_mapping.p, T, mkv, 0, q.p, gate.p, s);
     launch_attn_decode(mkv_map, d, q.p, token_seq.p, token_pos.p, descs.p, mbt.p, bt_stride, attn_items.p, n_items,
                        16, attn_ws.p, splits, err.p, s);
-    launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, T, 16, splits, hb2.p, s);
+    launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, nullptr, T, 16, splits, hb2.p, s);
     const int os = dense(ly.out_proj, hb2.p, max_tokens, T, partial.p, d.H, hstride, kMaxSplits, s);
     launch_residual_norm(x.p, partial.p, os, hstride, T, d.H, ly.post_norm, d.eps, hb.p, nullptr, 0, nullptr, s);
     const int A = T * (d.top + 1);

@@ -62,6 +62,32 @@ def test_topk_and_sort_bit_exact(wide, O):
     sess.drain()
 
 
+@pytest.mark.parametrize("T", [200, 300])
+def test_prefill_routing_sort_bit_exact(wide, O, T):
+    """Prefill-sized steps (the chunked-prefill attention and DeltaNet kernels
+    upstream of the router): top-k ids given the captured router logits and
+    the stable expert sort equal the oracle's rules, layer by layer."""
+    pkg, cfg, store, sess = wide
+    sess.drain()
+    E, K = cfg.experts, cfg.top
+    toks = np.random.default_rng(T).integers(0, cfg.vocab, size=T).astype(np.uint32)
+    sess.set_capture(True)
+    outs, _, _ = sess.step_ragged([None], [0], [T], toks)
+    logits = sess.debug_capture(0, np.float32).reshape(cfg.layers, T, E + 1)
+    offsets = sess.debug_capture(1).reshape(cfg.layers, E + 2)
+    perm = sess.debug_capture(2).reshape(cfg.layers, T * (K + 1))
+    ids = sess.debug_routing(T)
+    sess.set_capture(False)
+    for layer in range(cfg.layers):
+        assert np.array_equal(O.topk(logits[layer, :, :E], K), ids[layer]), layer
+        flat = np.concatenate([ids[layer], np.full((T, 1), E, np.int32)], axis=1).ravel()
+        counts, offs, p, inv = O.expert_sort(flat, E + 1)
+        assert np.array_equal(offs, offsets[layer, : E + 2]), layer
+        assert np.array_equal(p, perm[layer]), layer
+    sess.release(outs[0])
+    sess.drain()
+
+
 def _unpack(blob):
     n, T, R, nn = map(int, blob[:4])
     o = 4

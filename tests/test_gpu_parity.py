@@ -178,7 +178,12 @@ def test_cfg0_branching_and_release(tiny):
     # reference replay: full sequences from scratch
     (ra,), _, rla = sess.step_ragged([None], [0], [22], np.append(prefix, 7), flags=pkg.RAGGED_LOGITS)
     (rb,), _, rlb = sess.step_ragged([None], [0], [22], np.append(prefix, 9), flags=pkg.RAGGED_LOGITS)
-    assert rel_l2(la[0], rla[0]) < 1e-4 and rel_l2(lb[0], rlb[0]) < 1e-4
+    # The replays' 22 tokens run the chunked-prefill attention kernel, the
+    # branches' last token the split decode kernel: both round the softmax
+    # weights to bf16, against different running maxima, so the last layer's
+    # attention output (and the logits) differ at the 1e-4 level. The states
+    # (KV rows, DeltaNet states) do not depend on that output.
+    assert rel_l2(la[0], rla[0]) < 2e-3 and rel_l2(lb[0], rlb[0]) < 2e-3
     assert rel_l2(sess.snapshot(a), sess.snapshot(ra)) < 1e-4
     assert rel_l2(sess.snapshot(b), sess.snapshot(rb)) < 1e-4
     sess.release(p)
@@ -255,7 +260,9 @@ def test_cfg1_width_mixed_prefill_decode(wide):
       the operand rounding of each projection accumulates into it; with fp16
       operands the oracle's emulation of that rounding puts the worst row at
       2.7e-3 (bf16 operands: 3.7e-2);
-    - the chunks equal the same tokens decoded one step at a time (1e-3);
+    - the chunks equal the same tokens decoded one step at a time (1e-3) up to
+      the first router near-tie the two attention kernels resolve differently,
+      and every one-token row matches the oracle fed its own routing (1e-2);
     - every sequence's logits equal, bit for bit, those of the sequence stepped
       alone (a token's arithmetic does not depend on the batch it is in)."""
     pkg, cfg, store, sess, model = wide
@@ -278,14 +285,35 @@ def test_cfg1_width_mixed_prefill_decode(wide):
         assert max(errs) <= 1e-2, (s, [round(e, 5) for e in errs])
         assert rel_l2(sess.snapshot(outs[s]), st) < 1e-2, s
     for s in (0, 1):  # the chunks against one-token steps of the same tokens
-        cur = parents[s]
+        # The chunk's attention runs the prefill kernel, a one-token step the
+        # split decode kernel (bf16 softmax weights against different maxima),
+        # so a router near-tie can pick another expert; from then on the two
+        # paths hold different (each valid) states. Rows before the first
+        # divergence of the expert sets must agree within 1e-3; every
+        # one-token row must match the oracle fed its own routing (1e-2).
+        cur, step_logits, step_route, diverged = parents[s], [], [], None
         for j, t in enumerate(toks[s]):
+            sess.set_capture(True)
             (nxt,), _, lj = sess.step_ragged([cur], [positions[s] + j], [1], [t], flags=pkg.RAGGED_LOGITS)
+            rj = sess.debug_routing(1)
+            sess.set_capture(False)
             if cur is not parents[s]:
                 sess.release(cur)
             cur = nxt
-            assert rel_l2(lj[0], logits[cu[s] + j]) < 1e-3, (s, j, rel_l2(lj[0], logits[cu[s] + j]))
-        assert rel_l2(sess.snapshot(cur), sess.snapshot(outs[s])) < 1e-3, s
+            step_logits.append(lj[0])
+            step_route.append(rj)
+            same = all(set(rj[l, 0]) == set(route[l, cu[s] + j]) for l in range(cfg.layers))
+            if diverged is None and not same:
+                diverged = j
+            if diverged is None:
+                assert rel_l2(lj[0], logits[cu[s] + j]) < 1e-3, (s, j, rel_l2(lj[0], logits[cu[s] + j]))
+        lg, st, _, _ = model.forward(toks[s], positions[s], old_state=snaps[s],
+                                     forced_routing=np.concatenate(step_route, axis=1))
+        errs = [rel_l2(step_logits[j], lg[j]) for j in range(counts[s])]
+        assert max(errs) <= 1e-2, (s, [round(e, 5) for e in errs])
+        if diverged is None:
+            assert rel_l2(sess.snapshot(cur), sess.snapshot(outs[s])) < 1e-3, s
+        assert rel_l2(sess.snapshot(cur), st) < 1e-2, s
         sess.release(cur)
     for s in range(len(parents)):
         (o1,), s1, l1 = sess.step_ragged([parents[s]], [positions[s]], [counts[s]], toks[s], flags=flags)
