@@ -24,7 +24,8 @@
 //  gdn_chunk_scan: CTA = (sequence, value head, block of kScanRows rows).
 //    The rows of S are independent given the chunk's U, W, q, k and decays,
 //    so each CTA carries its rows through the sequence's chunks: h, the
-//    outputs o and the next rows, all in fp32 on the CUDA cores.
+//    outputs o and the next rows as tensor-core products (3xTF32, fp32
+//    accumulation, about fp32 accuracy), the state kept in fp32.
 // gdn_chunk_norm then applies the gated RMSNorm over dv (rows from different
 // CTAs) and writes the fp16 out_proj input.
 #include <atomic>
@@ -187,6 +188,48 @@ __global__ void __launch_bounds__(DK + DV)
   if (tid < C) LG[sc * C + tid] = lg[tid];
 }
 
+// 3xTF32 products on the tensor cores: x = big + small with big = tf32(x)
+// and small = tf32(x - big); a.b ~ a_s.b_b + a_b.b_s + a_b.b_b (the small.small
+// term is below fp32 rounding), accumulated in fp32 by mma.sync m16n8k8.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& big, uint32_t& small) {
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(big) : "f"(x));
+  const float r = x - __uint_as_float(big);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(small) : "f"(r));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += A B for one m16n8k8 step from fp32 fragments (A: a[4], B: b0, b1).
+__device__ __forceinline__ void mma3_tf32(float (&d)[4], const float (&a)[4], float b0, float b1) {
+  uint32_t ab[4], as[4], bb0, bs0, bb1, bs1;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) split_tf32(a[k], ab[k], as[k]);
+  split_tf32(b0, bb0, bs0);
+  split_tf32(b1, bb1, bs1);
+  mma_tf32(d, as, bb0, bb1);
+  mma_tf32(d, ab, bs0, bs1);
+  mma_tf32(d, ab, bb0, bb1);
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_groups() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// One CTA carries kScanRows rows of one value head's state through the
+// sequence's chunks. Per chunk, on the tensor cores (3xTF32, fp32
+// accumulation; fragments of m16n8k8: lane (g, t) = (lane / 4, lane % 4)):
+//   A: H = U - W S^T and QS = Q S^T (64 tokens x 32 rows, K = dk): warp w owns
+//      the 16-token x 8-row tile (w / 4, w % 4) of both;
+//   B: O = gamma_t QS + A H (the decayed masked q.k products times H, K = 64),
+//      same tiles, written to obuf;
+//   C: S = gamma_C S + (f H)^T K with f_t = gamma_C / gamma_t (32 rows x dk,
+//      K = 64), dk / 64 tiles per warp, read and written in place.
+// The next chunk's W, q, U and decays are requested once phase A is done,
+// its A block once phase B is done and its k rows once phase C is done, so
+// the copies overlap the remaining phases. Shared-memory row strides put the
+// 32 fragment elements a warp reads at once in distinct banks.
 template <int DK, int DV>
 __global__ void __launch_bounds__(kScanThreads, 1)
     gdn_chunk_scan_kernel(const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens,
@@ -196,125 +239,142 @@ __global__ void __launch_bounds__(kScanThreads, 1)
                           uint32_t* err) {
   pdl_trigger();
   pdl_wait();
-  // Row strides keep every row 16-byte aligned (asynchronous copies and
-  // 16-byte shared loads) and put the rows a quarter-warp reads together in
-  // distinct banks: W / q / k (PW) and the state rows (PS) are 4 floats wider
-  // than a row, and the state rows a thread owns are interleaved (row aq + 4m).
-  constexpr int PS = DK + 4, PW = DK + 4, PA = C + 4, PU = kScanRows + 4, RP = kScanRows + 1,
-                BLOCKS = DV / kScanRows, C4 = DK / 4;
+  static_assert(kScanThreads == 512 && kScanRows == 32 && C == 64 && DK % 64 == 0, "scan tiling");
+  constexpr int PQ = DK + 4;   // W, q rows (A operands: bank = 4g + t)
+  constexpr int PK = DK + 8;   // k rows (B operand over tokens: bank = 8t + g)
+  constexpr int PS = DK + 4;   // state rows (B operand of phase A: bank = 4g + t)
+  constexpr int PA = C + 4;    // A block rows
+  constexpr int PH = kScanRows + 8;  // H / U rows (bank = 8t + g)
+  constexpr int BLOCKS = DV / kScanRows;
+  constexpr int NTC = DK / 8, TPW = 2 * NTC / 16;  // phase C: n tiles, tiles per warp
   extern __shared__ __align__(16) float sm[];
-  float* Ws = sm;                    // [C][PW]
-  float* Qs = Ws + C * PW;           // [C][PW]
-  float* Ks = Qs + C * PW;           // [C][PW]
-  float* As = Ks + C * PW;           // [C][PA]
-  float* S = As + C * PA;            // [kScanRows][PS]
-  float* Us = S + kScanRows * PS;    // [C][PU]
-  float* Hs = Us + C * PU;           // [C][RP]
-  __shared__ __align__(16) float lg[C];
+  float* Ws = sm;                  // [C][PQ]
+  float* Qs = Ws + C * PQ;         // [C][PQ]
+  float* Ks = Qs + C * PQ;         // [C][PK]
+  float* As = Ks + C * PK;         // [C][PA]
+  float* S = As + C * PA;          // [kScanRows][PS]
+  float* Us = S + kScanRows * PS;  // [C][PH]
+  float* Hs = Us + C * PH;         // [C][PH]
+  __shared__ __align__(16) float lgb[2][C];
+  __shared__ float gs[C], fs[C];
   const int ls = blockIdx.x / (hv * BLOCKS), rem = blockIdx.x % (hv * BLOCKS);
   const int head = rem / BLOCKS, rb = rem % BLOCKS;
   const int seq = longs[3 * ls], item0 = longs[3 * ls + 1], n_chunks = longs[3 * ls + 2];
   const SeqDesc d = descs[seq];
   const int kh = head / (hv / hk), vd = hv * DV, r0 = rb * kScanRows;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tq = lane & 3;
   const size_t sl = size_t(hv) * DV * DK;
   const float* src = d.parent >= 0 ? pool.state + (size_t(d.parent) * pool.n_gdn + li) * sl + size_t(head) * DV * DK
                                    : nullptr;
   float* dst = pool.state + (size_t(d.child) * pool.n_gdn + li) * sl + size_t(head) * DV * DK;
-  for (int e = tid; e < kScanRows * DK; e += kScanThreads) {
-    const int r = e / DK, c = e % DK;
-    S[r * PS + c] = src ? src[size_t(r0 + r) * DK + c] : 0.f;
-  }
-  auto f4 = [](const float* p) { return *reinterpret_cast<const float4*>(p); };
-  auto dot4 = [](float4 a, float4 b, float acc) {
-    return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, fmaf(a.x, b.x, acc))));
-  };
-  // phase A / B: token at = tid / 8 (64 tokens), rows aq + 8m (m < 4)
-  const int at = tid >> 3, aq = tid & 7;
-  // phase C: row cr = tid / 16, column quads cb + 16m
-  const int cr = tid >> 4, cb = tid & 15;
-  constexpr int MR = kScanRows / 8, MQ = C4 / 16;  // rows / column quads per thread
-  for (int j = 0; j < n_chunks; ++j) {
+  const int cu0 = cu_seqlens[seq];
+
+  // chunk j's inputs: group 1 = W, q, U, decays; group 2 = A; group 3 = k rows
+  auto load_wqu = [&](int j) {
     const size_t sc = size_t(item0 + j) * hv + head;
-    const int t0 = cu_seqlens[seq] + j * C;
-    const int n = min(C, d.count - j * C);
-    __syncthreads();  // the previous chunk's readers are done
-    // the chunk's W, q, k, A, U block and decay sums: 16-byte asynchronous
-    // copies, all in flight together
+    const int t0 = cu0 + j * C, n = min(C, d.count - j * C);
     for (int e = tid; e < C * DK / 4; e += kScanThreads) {
       const int t = e / (DK / 4), c = 4 * (e % (DK / 4));
       const float* row = qk + ((size_t(t0 + t) * hk + kh) * 2) * DK;
-      cp16(Ws + t * PW + c, W + sc * C * DK + size_t(t) * DK + c, true);
-      cp16(Qs + t * PW + c, t < n ? row + c : qk, t < n);
-      cp16(Ks + t * PW + c, t < n ? row + DK + c : qk, t < n);
+      cp16(Ws + t * PQ + c, W + sc * C * DK + size_t(t) * DK + c, true);
+      cp16(Qs + t * PQ + c, t < n ? row + c : qk, t < n);
     }
+    for (int e = tid; e < C * kScanRows / 4; e += kScanThreads) {
+      const int t = e / (kScanRows / 4), r = 4 * (e % (kScanRows / 4));
+      cp16(Us + t * PH + r, U + sc * C * DV + size_t(t) * DV + r0 + r, true);
+    }
+    if (tid < C / 4) cp16(lgb[j & 1] + 4 * tid, LG + sc * C + 4 * tid, true);
+    cp_commit();
+  };
+  auto load_a = [&](int j) {
+    const size_t sc = size_t(item0 + j) * hv + head;
     for (int e = tid; e < C * C / 4; e += kScanThreads) {
       const int t = e / (C / 4), i = 4 * (e % (C / 4));
       cp16(As + t * PA + i, A + sc * C * C + size_t(t) * C + i, true);
     }
-    for (int e = tid; e < C * kScanRows / 4; e += kScanThreads) {
-      const int t = e / (kScanRows / 4), r = 4 * (e % (kScanRows / 4));
-      cp16(Us + t * PU + r, U + sc * C * DV + size_t(t) * DV + r0 + r, true);
+    cp_commit();
+  };
+  auto load_k = [&](int j) {
+    const int t0 = cu0 + j * C, n = min(C, d.count - j * C);
+    for (int e = tid; e < C * DK / 4; e += kScanThreads) {
+      const int t = e / (DK / 4), c = 4 * (e % (DK / 4));
+      const float* row = qk + ((size_t(t0 + t) * hk + kh) * 2) * DK;
+      cp16(Ks + t * PK + c, t < n ? row + DK + c : qk, t < n);
     }
-    if (tid < C / 4) cp16(lg + 4 * tid, LG + sc * C + 4 * tid, true);
-    cp_wait_all();
-    __syncthreads();
-    // phase A: h = U - W s and q s for token `at`, rows aq + 8m
-    float hacc[MR], qacc[MR];
-#pragma unroll
-    for (int m = 0; m < MR; ++m) hacc[m] = qacc[m] = 0.f;
-#pragma unroll 4
-    for (int c4 = 0; c4 < C4; ++c4) {
-      const float4 w = f4(Ws + at * PW + 4 * c4), q = f4(Qs + at * PW + 4 * c4);
-#pragma unroll
-      for (int m = 0; m < MR; ++m) {
-        const float4 sv = f4(S + (aq + 8 * m) * PS + 4 * c4);
-        hacc[m] = dot4(w, sv, hacc[m]);
-        qacc[m] = dot4(q, sv, qacc[m]);
-      }
-    }
-#pragma unroll
-    for (int m = 0; m < MR; ++m) Hs[at * RP + aq + 8 * m] = Us[at * PU + aq + 8 * m] - hacc[m];
-    __syncthreads();
-    // phase B: outputs o = gamma_t q s + sum_{i <= t} A[t][i] h_i
-    const float gt = expf(lg[at]);
-    float o[MR];
-#pragma unroll
-    for (int m = 0; m < MR; ++m) o[m] = gt * qacc[m];
-    for (int i = 0; i <= at; ++i) {
-      const float a = As[at * PA + i];
-#pragma unroll
-      for (int m = 0; m < MR; ++m) o[m] = fmaf(a, Hs[i * RP + aq + 8 * m], o[m]);
-    }
-    if (at < n) {
-#pragma unroll
-      for (int m = 0; m < MR; ++m) obuf[size_t(t0 + at) * vd + head * DV + r0 + aq + 8 * m] = o[m];
-    }
-    // phase C: next rows S = gamma_C S + sum_t (gamma_C / gamma_t) h_t k_t^T
-    const float lc = lg[C - 1], gc = expf(lc);
-    float4 acc[MQ];
-#pragma unroll
-    for (int m = 0; m < MQ; ++m) {
-      const float4 sv = f4(S + cr * PS + 4 * (cb + 16 * m));
-      acc[m] = make_float4(gc * sv.x, gc * sv.y, gc * sv.z, gc * sv.w);
-    }
-#pragma unroll 4
-    for (int t = 0; t < C; ++t) {
-      const float f = expf(lc - lg[t]) * Hs[t * RP + cr];
-#pragma unroll
-      for (int m = 0; m < MQ; ++m) {
-        const float4 kv = f4(Ks + t * PW + 4 * (cb + 16 * m));
-        acc[m].x = fmaf(f, kv.x, acc[m].x);
-        acc[m].y = fmaf(f, kv.y, acc[m].y);
-        acc[m].z = fmaf(f, kv.z, acc[m].z);
-        acc[m].w = fmaf(f, kv.w, acc[m].w);
-      }
-    }
-    __syncthreads();  // phase A's readers of S are done before it is overwritten
-#pragma unroll
-    for (int m = 0; m < MQ; ++m) *reinterpret_cast<float4*>(S + cr * PS + 4 * (cb + 16 * m)) = acc[m];
+    cp_commit();
+  };
+  load_wqu(0);
+  load_a(0);
+  load_k(0);
+  for (int e = tid; e < kScanRows * DK; e += kScanThreads) {
+    const int r = e / DK, c = e % DK;
+    S[r * PS + c] = src ? src[size_t(r0 + r) * DK + c] : 0.f;
   }
-  __syncthreads();
+  const int mt = warp >> 2, nt = warp & 3;          // phase A / B tile
+  const int ta = 16 * mt + g, tb = ta + 8;          // this lane's two token rows
+  const int rr = 8 * nt + 2 * tq;                   // and its two state rows (rr, rr + 1)
+  for (int j = 0; j < n_chunks; ++j) {
+    const int t0 = cu0 + j * C, n = min(C, d.count - j * C);
+    const float* lg = lgb[j & 1];
+    cp_wait_groups();
+    __syncthreads();
+    // phase A
+    float hw[4] = {0.f, 0.f, 0.f, 0.f}, qs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int k0 = 0; k0 < DK; k0 += 8) {
+      const float aw[4] = {Ws[ta * PQ + k0 + tq], Ws[tb * PQ + k0 + tq], Ws[ta * PQ + k0 + tq + 4],
+                           Ws[tb * PQ + k0 + tq + 4]};
+      const float aq[4] = {Qs[ta * PQ + k0 + tq], Qs[tb * PQ + k0 + tq], Qs[ta * PQ + k0 + tq + 4],
+                           Qs[tb * PQ + k0 + tq + 4]};
+      const float b0 = S[(8 * nt + g) * PS + k0 + tq], b1 = S[(8 * nt + g) * PS + k0 + tq + 4];
+      mma3_tf32(hw, aw, b0, b1);
+      mma3_tf32(qs, aq, b0, b1);
+    }
+    Hs[ta * PH + rr] = Us[ta * PH + rr] - hw[0];
+    Hs[ta * PH + rr + 1] = Us[ta * PH + rr + 1] - hw[1];
+    Hs[tb * PH + rr] = Us[tb * PH + rr] - hw[2];
+    Hs[tb * PH + rr + 1] = Us[tb * PH + rr + 1] - hw[3];
+    if (tid < C) {
+      gs[tid] = expf(lg[tid]);
+      fs[tid] = expf(lg[C - 1] - lg[tid]);
+    }
+    __syncthreads();  // H, decays ready; W, q, U free
+    if (j + 1 < n_chunks) load_wqu(j + 1);
+    // phase B: o = gamma_t qs + A h (A is zero above the diagonal)
+    float o[4] = {gs[ta] * qs[0], gs[ta] * qs[1], gs[tb] * qs[2], gs[tb] * qs[3]};
+    for (int i0 = 0; i0 <= 16 * mt + 8; i0 += 8) {
+      const float aa[4] = {As[ta * PA + i0 + tq], As[tb * PA + i0 + tq], As[ta * PA + i0 + tq + 4],
+                           As[tb * PA + i0 + tq + 4]};
+      mma3_tf32(o, aa, Hs[(i0 + tq) * PH + 8 * nt + g], Hs[(i0 + tq + 4) * PH + 8 * nt + g]);
+    }
+    if (ta < n)
+      *reinterpret_cast<float2*>(obuf + size_t(t0 + ta) * vd + head * DV + r0 + rr) = make_float2(o[0], o[1]);
+    if (tb < n)
+      *reinterpret_cast<float2*>(obuf + size_t(t0 + tb) * vd + head * DV + r0 + rr) = make_float2(o[2], o[3]);
+    __syncthreads();  // A free
+    if (j + 1 < n_chunks) load_a(j + 1);
+    // phase C: S = gamma_C S + (f h)^T k, in place (each warp owns its tiles)
+    const float gc = gs[C - 1];
+#pragma unroll
+    for (int u = 0; u < TPW; ++u) {
+      const int tile = warp * TPW + u, mc = tile / NTC, nc = tile % NTC;
+      const int ra = 16 * mc + g, rb2 = ra + 8, cc = 8 * nc + 2 * tq;
+      const float2 s0 = *reinterpret_cast<const float2*>(S + ra * PS + cc);
+      const float2 s1 = *reinterpret_cast<const float2*>(S + rb2 * PS + cc);
+      float acc[4] = {gc * s0.x, gc * s0.y, gc * s1.x, gc * s1.y};
+#pragma unroll 2
+      for (int k0 = 0; k0 < C; k0 += 8) {
+        const float f0 = fs[k0 + tq], f1 = fs[k0 + tq + 4];
+        const float ah[4] = {f0 * Hs[(k0 + tq) * PH + ra], f0 * Hs[(k0 + tq) * PH + rb2],
+                             f1 * Hs[(k0 + tq + 4) * PH + ra], f1 * Hs[(k0 + tq + 4) * PH + rb2]};
+        mma3_tf32(acc, ah, Ks[(k0 + tq) * PK + 8 * nc + g], Ks[(k0 + tq + 4) * PK + 8 * nc + g]);
+      }
+      *reinterpret_cast<float2*>(S + ra * PS + cc) = make_float2(acc[0], acc[1]);
+      *reinterpret_cast<float2*>(S + rb2 * PS + cc) = make_float2(acc[2], acc[3]);
+    }
+    __syncthreads();  // k rows and H free; S complete
+    if (j + 1 < n_chunks) load_k(j + 1);
+  }
   bool finite = true;
   for (int e = tid; e < kScanRows * DK; e += kScanThreads) {
     const int r = e / DK, c = e % DK;
@@ -466,8 +526,8 @@ void launch_chunked(const GdnChunkPlan& cp, const Dims& d, const LayerDev& ly, c
                     int li, gemm_in_t* out, uint32_t* err, const float* qk_buf, float* v_buf, const float* gb_buf,
                     cudaStream_t s) {
   constexpr size_t prep_smem = (2 * C * (DK + 1) + C * (C + 1)) * sizeof(float);
-  constexpr size_t scan_smem = (3 * C * (DK + 4) + C * (C + 4) + kScanRows * (DK + 4) + C * (kScanRows + 4) +
-                                C * (kScanRows + 1)) * sizeof(float);
+  constexpr size_t scan_smem = (2 * C * (DK + 4) + C * (DK + 8) + C * (C + 4) + kScanRows * (DK + 4) +
+                                2 * C * (kScanRows + 8)) * sizeof(float);
   static_assert(prep_smem <= 227 * 1024 && scan_smem <= 227 * 1024, "chunked DeltaNet shared memory");
   static std::atomic<uint64_t> set{0};
   once_per_device(set, [] {

@@ -62,7 +62,7 @@ def test_topk_and_sort_bit_exact(wide, O):
     sess.drain()
 
 
-@pytest.mark.parametrize("T", [200, 300])
+@pytest.mark.parametrize("T", [200, 256, 300])
 def test_prefill_routing_sort_bit_exact(wide, O, T):
     """Prefill-sized steps (the chunked-prefill attention and DeltaNet kernels
     upstream of the router): top-k ids given the captured router logits and
