@@ -385,9 +385,10 @@ int rs_qwen_debug_gemm(void* session, int which, int layer, const uint16_t* x, s
  * synchronises that stream and returns once the result is in y_device. It
  * runs on the session's device and leaves the calling thread's current device
  * as it found it. The first call on each device resolves the scratch address
- * (a one-time set-up); make that call before any stream capture begins. Every call on a device shares the one array: calls that
- * overlap in time (several host threads, or several sessions on one device)
- * race and corrupt each other's results, so serialise them. Returns 0/-1. */
+ * (a one-time set-up); make that call before any stream capture begins.
+ * Every call on a device shares the one array: calls that overlap in time
+ * (several host threads, or several sessions on one device) race and corrupt
+ * each other's results, so serialise them. Returns 0/-1. */
 int rs_qwen_project_noalloc(void* session, int which, int layer, const void* x_device, size_t T,
                             float* y_device, size_t y_count, void* stream, char* error, size_t capacity);
 
