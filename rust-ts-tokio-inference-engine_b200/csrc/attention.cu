@@ -112,6 +112,7 @@ template <int D>
 __global__ void __launch_bounds__(kAttnWarps * 32)
     attn_decode_kernel(const __grid_constant__ CUtensorMap kvmap, const float* __restrict__ q,
                        const int32_t* __restrict__ token_seq, const int32_t* __restrict__ token_pos,
+                       const int32_t* __restrict__ dec_tokens,
                        const SeqDesc* __restrict__ descs, const int32_t* __restrict__ block_table, int stride,
                        const int2* __restrict__ items, int split_pages, int Hq, int Hkv, int G, int max_splits,
                        float* __restrict__ ws, uint32_t* err) {
@@ -128,8 +129,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   float* obuf = reinterpret_cast<float*>(kv);               // [16][D] merge buffer, on the drained ring
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + kAttnWarps * 16 * 2);  // [warps][stages]
 
+  // item.x indexes the step's split-decoded tokens (the workspace row);
+  // dec_tokens maps it to the packed token (null: the same index)
   const int2 item = items[blockIdx.x];
-  const int t = item.x, split = item.y, g = blockIdx.y;
+  const int md = item.x, t = dec_tokens ? dec_tokens[md] : md, split = item.y, g = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = token_pos[t] + 1;
   const int n_pages = (len + kPageTokens - 1) / kPageTokens;
@@ -293,7 +296,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
       const float mw = red[(w * 16 + hr) * 2];
       if (mw > -FLT_MAX) Lh += red[(w * 16 + hr) * 2 + 1] * exp2f(mw - Mh);
     }
-    float* out = ws + ((size_t(t) * Hq + g * G + hr) * max_splits + split) * (D + 2);
+    float* out = ws + ((size_t(md) * Hq + g * G + hr) * max_splits + split) * (D + 2);
     if (threadIdx.x == 0) {
       out[0] = Mh * 0.6931471805599453f;
       out[1] = Lh;
@@ -537,7 +540,7 @@ size_t attn_decode_smem(int D) {
 CUtensorMap make_kv_map(const KvPool& kv, int layer);
 
 void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_seq,
-                        const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
+                        const int32_t* token_pos, const int32_t* dec_tokens, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
                         const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
                         cudaStream_t s) {
   const int G = d.Hq / d.Hkv;
@@ -553,7 +556,7 @@ void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q,
       QWEN_CUDA(cudaFuncSetAttribute(attn_decode_kernel<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
                                      int(smem)));                                                           \
     });                                                                                                     \
-    launch_pdl(attn_decode_kernel<DD>, grid, kAttnWarps * 32, smem, s, kvmap, q, token_seq, token_pos, descs,      \
+    launch_pdl(attn_decode_kernel<DD>, grid, kAttnWarps * 32, smem, s, kvmap, q, token_seq, token_pos, dec_tokens, descs, \
                                                                block_table, bt_stride, items, split_pages,  \
                                                                d.Hq, d.Hkv, G, max_splits, ws, err);        \
     QWEN_CUDA(cudaGetLastError());                                                                          \

@@ -324,7 +324,7 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
   __shared__ float s_max, s_den;
   const int t = tokens ? tokens[blockIdx.x] : blockIdx.x, h = blockIdx.y;
   const int n = (token_pos[t] + 1 + spl - 1) / spl;
-  const float* base = ws + (size_t(t) * Hq + h) * max_splits * (D + 2);
+  const float* base = ws + (size_t(blockIdx.x) * Hq + h) * max_splits * (D + 2);
   float m = -FLT_MAX;
   for (int s = threadIdx.x; s < n; s += blockDim.x) m = fmaxf(m, base[s * (D + 2)]);
   m = warp_max(m);

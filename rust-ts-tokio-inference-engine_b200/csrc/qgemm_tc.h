@@ -40,12 +40,15 @@ int qgemm_tc_unit(const TcArgs& a);
 // Tensor map over one attention layer's KV page pool: rows
 // ((page*2 + k_or_v)*Hkv + head)*16 + token, D columns, 16x64 128B-swizzled box.
 CUtensorMap make_kv_map(const KvPool& kv, int layer);
+// items[i] = (index into dec_tokens, KV split); dec_tokens maps that index to
+// the packed token (null: identity); the split partials are stored per index.
 void launch_attn_decode(const CUtensorMap& kvmap, const Dims& d, const float* q, const int32_t* token_seq,
-                        const int32_t* token_pos, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
+                        const int32_t* token_pos, const int32_t* dec_tokens, const SeqDesc* descs, const int32_t* block_table, int bt_stride,
                         const int2* items, int n_items, int split_pages, float* ws, int max_splits, uint32_t* err,
                         cudaStream_t s);
-// Merges the split partials of `T` tokens (the listed token indices, or
-// 0..T-1 when `tokens` is null) and applies the output gate.
+// Merges the split partials of `T` split-decoded tokens (partials stored per
+// index; `tokens` maps an index to the packed token, null: identity) and
+// applies the output gate.
 void launch_attention_merge(const Dims& d, const float* ws, const float* gate, const int32_t* token_pos,
                             const int32_t* tokens, int T, int split_pages, int max_splits, gemm_in_t* out,
                             cudaStream_t s);

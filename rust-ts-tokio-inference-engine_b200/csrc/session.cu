@@ -577,14 +577,17 @@ struct Session {
       const int QB = pf_ok ? kAttnPrefillWarps * (16 / G) : 0;
       auto prefill = [&](const SeqIn& s) { return pf_ok && s.count >= uint32_t(kAttnPrefillMin); };
       int64_t page_heads = 0;
+      int dec_len = 1;  // longest context of a split-decoded token
       for (const auto& s : seqs)
-        if (!prefill(s))
+        if (!prefill(s)) {
           for (uint32_t j = 0; j < s.count; ++j) page_heads += (int64_t(s.position) + j + kPageTokens) / kPageTokens;
+          dec_len = std::max<int>(dec_len, int(s.position + s.count));
+        }
       page_heads *= d.Hkv;
       int sp = 16;
       while (sp < 64 && page_heads / (2 * sp) >= int64_t(sm_count) * 4) sp *= 2;
       attn_split_pages = sp;
-      attn_splits = std::max(1, (max_len + sp * kPageTokens - 1) / (sp * kPageTokens));
+      attn_splits = std::max(1, (dec_len + sp * kPageTokens - 1) / (sp * kPageTokens));
       int t = 0;
       for (int i = 0; i < n; ++i) {
         const SeqIn& s = seqs[i];
@@ -599,7 +602,8 @@ struct Session {
         }
         for (uint32_t j = 0; j < s.count; ++j, ++t) {
           const int pages = int((int64_t(s.position) + j + kPageTokens) / kPageTokens);
-          for (int k = 0; k * sp < pages; ++k) items.push_back(make_int2(t, k));
+          const int md = int(merge_tokens.size());  // workspace row (= t when nothing runs the prefill kernel)
+          for (int k = 0; k * sp < pages; ++k) items.push_back(make_int2(md, k));
           merge_tokens.push_back(t);
         }
       }
@@ -964,7 +968,7 @@ struct Session {
     if (d.n_attn > 0) launch_cow(kv, descs.p, n, new_pages.p, s);
     launch_embed_norm(m.embed, tokens.p, T, m.layers[0].in_norm, d.eps, x.p, hb.p, s);
     const int slots_per_tok = d.top + 1, A = T * slots_per_tok;
-    if (d.n_attn > 0) attn_ws.ensure(size_t(T) * d.Hq * attn_splits * (d.D + 2));
+    if (d.n_attn > 0) attn_ws.ensure_grow(size_t(pf_n_blocks ? n_merge : T) * d.Hq * attn_splits * (d.D + 2));
     if (capture_routing) {
       capture.ensure(size_t(d.L) * A);
       cap_logits.ensure(size_t(d.L) * T * (d.E + 1));
@@ -989,7 +993,8 @@ struct Session {
         stage(7);  // AttentionReduction (q/k norm, RoPE, KV append, paged attention)
         launch_attn_prep(d, ly, partial.p, proj_w, ps, proj_stride, token_pos.p, slot_mapping.p, T, kv,
                          ly.type_index, q.p, gate.p, s);
-        launch_attn_decode(kv_maps[ly.type_index], d, q.p, token_seq.p, token_pos.p, descs.p, block_table.p,
+        launch_attn_decode(kv_maps[ly.type_index], d, q.p, token_seq.p, token_pos.p,
+                           pf_n_blocks ? merge_dev.p : nullptr, descs.p, block_table.p,
                            bt_stride, attn_items.p, attn_n_items, attn_split_pages, attn_ws.p, attn_splits, err.p,
                            s);
         launch_attn_prefill(kv_maps[ly.type_index], d, q.p, token_pos.p, descs.p, block_table.p, bt_stride,
@@ -1326,7 +1331,7 @@ struct Session {
     const size_t astride = size_t(T) * aw;
     const int ps = dense(ly.in_proj, hb.p, max_tokens, T, partial.p, aw, astride, kMaxSplits, s);
     launch_attn_prep(d, ly, partial.p, aw, ps, astride, token_pos.p, slot_mapping.p, T, mkv, 0, q.p, gate.p, s);
-    launch_attn_decode(mkv_map, d, q.p, token_seq.p, token_pos.p, descs.p, mbt.p, bt_stride, attn_items.p, n_items,
+    launch_attn_decode(mkv_map, d, q.p, token_seq.p, token_pos.p, nullptr, descs.p, mbt.p, bt_stride, attn_items.p, n_items,
                        16, attn_ws.p, splits, err.p, s);
     launch_attention_merge(d, attn_ws.p, gate.p, token_pos.p, nullptr, T, 16, splits, hb2.p, s);
     const int os = dense(ly.out_proj, hb2.p, max_tokens, T, partial.p, d.H, hstride, kMaxSplits, s);
