@@ -526,6 +526,83 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __rest
   }
 }
 
+// The same stable sort from one bit mask of tokens per expert (single CTA,
+// 1024 threads; used when the masks fit in shared memory): a token picks an
+// expert at most once, so an assignment's rank inside its expert, i.e. the
+// number of assignments of that expert with a smaller flat index, is the
+// number of earlier tokens that picked the expert: the popcount of the
+// expert's mask below the token. Per expert the counts of every 8 mask words
+// are prefix-summed, so a rank costs at most 8 popcounts. Same bytes as
+// expert_sort_kernel (a stable sort has one result).
+constexpr int kMaskWordsPerBlock = 8;
+__global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* __restrict__ ids, int T, int slots,
+                                                                int n_exp, int32_t* counts, int32_t* offsets,
+                                                                int32_t* perm, int32_t* inv, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ uint32_t smm[];
+  const int nw = (T + 31) >> 5, nb = (nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock, A = T * slots;
+  uint32_t* mask = smm;                                                   // [n_exp][nw]
+  int32_t* pre = reinterpret_cast<int32_t*>(mask + size_t(n_exp) * nw);   // [n_exp][nb] ranks before block b
+  int32_t* off = pre + size_t(n_exp) * nb;                                // [n_exp]
+  __shared__ int32_t warp_tot[32];
+  for (int i = threadIdx.x; i < n_exp * nw; i += blockDim.x) mask[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < A; i += blockDim.x) {
+    const int e = ids[i], t = i / slots;
+    if (e >= 0 && e < n_exp) atomicOr(&mask[e * nw + (t >> 5)], 1u << (t & 31));
+    else atomicOr(err, kErrBounds);
+  }
+  __syncthreads();
+  // per expert: block prefixes and the count; then an exclusive scan over experts
+  int cnt = 0;
+  for (int e = threadIdx.x; e < n_exp; e += blockDim.x) {
+    int run = 0;
+    for (int b = 0; b < nb; ++b) {
+      pre[e * nb + b] = run;
+      const int w1 = min(nw, (b + 1) * kMaskWordsPerBlock);
+      for (int w = b * kMaskWordsPerBlock; w < w1; ++w) run += __popc(mask[e * nw + w]);
+    }
+    off[e] = run;  // the count, until the scan below
+  }
+  __syncthreads();
+  // exclusive scan of off[] (n_exp <= 1025): thread i owns experts [i * per, (i + 1) * per)
+  const int per = (n_exp + blockDim.x - 1) / blockDim.x;
+  const int e0 = threadIdx.x * per, e1 = min(n_exp, e0 + per);
+  for (int e = e0; e < e1; ++e) cnt += off[e];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int base = incl - cnt;
+  for (int w = 0; w < warp; ++w) base += warp_tot[w];
+  for (int e = e0; e < e1; ++e) {
+    const int c = off[e];
+    off[e] = base;
+    offsets[e] = base;
+    counts[e] = c;
+    base += c;
+  }
+  if (threadIdx.x == blockDim.x - 1) offsets[n_exp] = base;
+  __syncthreads();
+  for (int i = threadIdx.x; i < A; i += blockDim.x) {
+    const int e = ids[i], t = i / slots;
+    if (e < 0 || e >= n_exp) continue;
+    const uint32_t* m = mask + size_t(e) * nw;
+    const int wt = t >> 5, b = wt / kMaskWordsPerBlock;
+    int rank = pre[e * nb + b] + __popc(m[wt] & ((1u << (t & 31)) - 1u));
+    for (int w = b * kMaskWordsPerBlock; w < wt; ++w) rank += __popc(m[w]);
+    const int pos = off[e] + rank;
+    perm[pos] = i;
+    inv[i] = pos;
+  }
+}
+
 // x[t] += sum_j w[t][j] * y[inv[t*slots+j]] (fixed slot order, deterministic);
 // then optional hb[t] = fp16(rms(x[t]) * norm_w).
 __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
@@ -944,8 +1021,22 @@ void launch_route(const float* logits, int ld, int splits, size_t split_stride, 
   count_launch();
 }
 
-void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
-                        int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s) {
+void launch_expert_sort(const int32_t* ids, int n_assign, int slots, int n_experts, int32_t* counts,
+                        int32_t* offsets, int32_t* perm, int32_t* inv, uint32_t* err, cudaStream_t s) {
+  if (n_assign <= 0) return;
+  const int T = n_assign / slots, nw = (T + 31) / 32, nb = (nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock;
+  const size_t mask_smem = (size_t(n_experts) * (nw + nb) + n_experts) * 4;
+  if (n_assign % slots == 0 && n_experts <= 1025 && mask_smem <= 200 * 1024) {
+    static std::atomic<uint64_t> mask_configured{0};
+    once_per_device(mask_configured, [] {
+      QWEN_CUDA(cudaFuncSetAttribute(expert_sort_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024));
+    });
+    launch_pdl(expert_sort_mask_kernel, 1, 1024, mask_smem, s, ids, T, slots, n_experts, counts, offsets, perm, inv,
+               err);
+    count_launch();
+    return;
+  }
   const size_t smem = size_t(3 * n_experts) * 4 + size_t(32) * n_experts * 2;
   if (smem > 200 * 1024) throw std::invalid_argument("expert sort exceeds shared memory");
   static std::atomic<uint64_t> configured{0};

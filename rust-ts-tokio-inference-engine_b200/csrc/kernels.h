@@ -123,8 +123,11 @@ void launch_attn_prep(const Dims& d, const LayerDev& ly, const float* proj, int 
                       int kv_layer, float* q, float* gate, cudaStream_t s);
 void launch_route(const float* logits, int ld, int splits, size_t split_stride, int T, int E, int top,
                   int32_t* ids, float* weights, float* logits_out, cudaStream_t s);
-void launch_expert_sort(const int32_t* ids, int n_assign, int n_experts, int32_t* counts,
-                        int32_t* offsets, int32_t* perm, int32_t* inv, cudaStream_t s);
+// Stable sort of the assignments (n_assign = tokens * slots, each token's
+// slots distinct experts) by expert: token bit masks when they fit in shared
+// memory, else per-round counting.
+void launch_expert_sort(const int32_t* ids, int n_assign, int slots, int n_experts, int32_t* counts,
+                        int32_t* offsets, int32_t* perm, int32_t* inv, uint32_t* err, cudaStream_t s);
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
                         float eps, gemm_in_t* hb, const int32_t* out_token, int rows,

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <atomic>
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <numeric>
@@ -1543,7 +1544,7 @@ struct Session {
     const int rs = dense(ly.router, hb.p, max_tokens, T, partial.p, rw, rstride, kMaxSplits, s);
     launch_route(partial.p, rw, rs, rstride, T, d.E, d.top, ids.p, weights.p,
                  capture_routing ? cap_logits.p + size_t(cur_layer) * T * (d.E + 1) : nullptr, s);
-    launch_expert_sort(ids.p, A, d.E + 1, counts.p, offsets.p, perm.p, inv.p, s);
+    launch_expert_sort(ids.p, A, d.top + 1, d.E + 1, counts.p, offsets.p, perm.p, inv.p, err.p, s);
     stage(11);  // MoeUpGate
     if (ep.on && !in_mtp && !simple_gemm) {
       moe_ep(ly, T, A, s);
@@ -1578,8 +1579,12 @@ struct Session {
       return;
     }
     launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
+    // Token block of the grouped GEMMs: the mean rows per expert plus two
+    // standard deviations of a binomial count, so nearly every expert fits one
+    // block (a larger block re-reads more activation rows per weight tile and
+    // runs wider MMAs on padding; an expert over the block takes a second one)
     const int per_expert = (A + d.E) / (d.E + 1);
-    const int box = box_for(std::max(1, 2 * per_expert));
+    const int box = box_for(std::max(1, per_expert + int(2.0 * std::sqrt(double(per_expert)) + 0.5)));
     TcArgs gu;
     gu.W = ly.expert_gu;
     gu.mode = kGemmGateUp;
