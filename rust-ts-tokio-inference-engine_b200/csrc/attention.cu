@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
                        const int2* __restrict__ items, int split_pages, int Hq, int Hkv, int G, int max_splits,
                        float* __restrict__ ws, uint32_t* err) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(q, token_seq, token_pos, dec_tokens, descs, block_table, items, ws);
   constexpr int KS = D / 16;     // k-steps of Q K^T
   constexpr int NT = D / 8;      // n-tiles of O
   constexpr int TILE = 16 * D * 2;  // bytes of one 16-row tile
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1)
                         int Hq, int Hkv, int G, const float* __restrict__ gate, gemm_in_t* __restrict__ out,
                         uint32_t* err) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(q, token_pos, descs, block_table, blocks, gate, out);
   constexpr int KS = D / 16;
   constexpr int NT = D / 8;
   constexpr int TILE = 16 * D * 2;

@@ -200,8 +200,26 @@ enum ErrorBits : uint32_t {
 // that earlier kernels of the stream write (pdl_wait returns once they have
 // completed and their writes are visible; without a programmatic predecessor
 // it returns at once).
+//
+// pdl_wait(p, q, ...) takes the kernel's __restrict__ pointer parameters.
+// The wait's memory clobber does not order accesses through a __restrict__
+// pointer (restrict promises the compiler that nothing else touches that
+// data), so the compiler may schedule such loads before the wait, where they
+// can read what the still-running predecessor has not written yet. Each
+// pointer is therefore passed through an empty asm after the wait: every
+// access through it then depends on an instruction that follows the wait.
+template <typename P>
+__device__ __forceinline__ void pdl_reseat(P& p) {
+  uint64_t v = reinterpret_cast<uint64_t>(p);
+  asm volatile("" : "+l"(v));
+  p = reinterpret_cast<P>(v);
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+template <typename... P>
+__device__ __forceinline__ void pdl_wait(P&... ptrs) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  (pdl_reseat(ptrs), ...);
+}
 
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

@@ -90,7 +90,7 @@ __global__ void ep_pack_kernel(const gemm_in_t* __restrict__ src, int ld, const 
                                int per_rank, int hdr_ints, int cap, int H, uint32_t* const* flag_dst, uint32_t epoch,
                                uint32_t* done) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(src, perm, counts, offsets, dst);
   const int p = blockIdx.y;
   uint8_t* st = dst[p];
   const int e0 = p * per_rank;
@@ -139,7 +139,7 @@ __global__ void ep_plan_kernel(const uint8_t* const* __restrict__ srcs, int worl
                                int32_t* __restrict__ seg, int32_t* __restrict__ n_rows, uint32_t* err, int cap,
                                const uint32_t* wait_flags, uint32_t epoch) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(srcs, counts, goff, seg, n_rows);
   ep_wait_flags(wait_flags, world, epoch, err);
   extern __shared__ int32_t sm[];
   const int n = world * per_rank;
@@ -193,7 +193,7 @@ __global__ void ep_gather_kernel(const uint8_t* const* __restrict__ srcs, int wo
                                  gemm_in_t* __restrict__ xloc, int32_t* __restrict__ origin, int cap, int H,
                                  int rank) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(srcs, goff, seg, offsets, xsrc, perm, xloc, origin);
   extern __shared__ int32_t sseg[];  // [per_rank * world][2]
   const int nseg = per_rank * world;
   for (int i = threadIdx.x; i < 2 * nseg; i += blockDim.x) sseg[i] = seg[i];
@@ -233,7 +233,7 @@ __global__ void ep_return_pack_kernel(const float* __restrict__ yloc, const int3
                                       float* __restrict__ y_sorted, int cap, int H, int world,
                                       uint32_t* const* flag_dst, uint32_t epoch, uint32_t* done) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(yloc, origin, n_rows, rdst, y_sorted);
   const int n = *n_rows;
   const int h4 = H / 4;
   for (int row = blockIdx.x; row < n; row += gridDim.x) {
@@ -250,7 +250,7 @@ __global__ void ep_return_unpack_kernel(const float* const* __restrict__ rsrcs, 
                                         float* __restrict__ y_sorted, int world, int per_rank, int H,
                                         const uint32_t* wait_flags, uint32_t epoch, uint32_t* err) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(rsrcs, offsets, y_sorted);
   ep_wait_flags(wait_flags, world, epoch, err);
   const int n_routed = offsets[world * per_rank];
   const int h4 = H / 4;

@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 2)
                     const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
                     float* __restrict__ gb_out, const int32_t* __restrict__ cand_slots, int skip_count) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(proj, descs, cu_seqlens, conv_w, a_log, dt_bias, qk_out, v_out, gb_out, cand_slots);
   {
     const SeqDesc dd = descs[blockIdx.x];
     if (dd.cand < 0 && dd.count >= skip_count) return;  // a long run: gdn_run_prep owns it
@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(256, 3)
                       gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots,
                       int skip_count) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cu_seqlens, qk, vv, gb, proj, gnorm, out, cand_slots);
   constexpr int CPL = DK / 32;  // columns per lane (4 or 2)
   constexpr int RPW = DV / 8;   // rows per warp
   {
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(288, 3)
                       size_t split_stride, int cd, const float* __restrict__ gnorm, float eps,
                       gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cu_seqlens, qk, vv, gb, proj, gnorm, out, cand_slots);
   constexpr int CPL = DK / 32;   // state columns per lane
   constexpr int CR = 32;         // rows per chunk: 4 per consumer warp
   constexpr int CPI = DV / CR;   // chunks per item
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm)
                       const float* __restrict__ dt_bias, const float* __restrict__ gnorm, float eps,
                       gemm_in_t* __restrict__ out, uint32_t* err, const int32_t* __restrict__ cand_slots) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(proj, descs, cu_seqlens, conv_w, a_log, dt_bias, gnorm, out, cand_slots);
   constexpr int CPL = DK / 32;      // state columns per lane
   constexpr int NCW = kDecConsumerWarps, IW = NCW, SW0 = NCW + 1;  // consumer / issuer / first stager warp
   constexpr int CR = 32;            // rows per chunk

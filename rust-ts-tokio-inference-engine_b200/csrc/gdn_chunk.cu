@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(DK + DV)
                           const float* __restrict__ dt_bias, float* __restrict__ U, float* __restrict__ W,
                           float* __restrict__ A, float* __restrict__ LG) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cu_seqlens, items, qk, vv, proj, a_log, dt_bias, U, W, A, LG);
   constexpr int P = DK + 1;  // padded row stride: lanes reading different rows hit different banks
   extern __shared__ float sm[];
   float* Ks = sm;               // [C][P]
@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
                           const float* __restrict__ A, const float* __restrict__ LG, float* __restrict__ obuf,
                           uint32_t* err) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cu_seqlens, longs, qk, U, W, A, LG, obuf);
   static_assert(kScanThreads == 512 && kScanRows == 32 && C == 64 && DK % 64 == 0, "scan tiling");
   constexpr int PQ = DK + 4;   // W, q rows (A operands: bank = 4g + t)
   constexpr int PK = DK + 8;   // k rows (B operand over tokens: bank = 8t + g)
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(1024, 1)
                           const float* __restrict__ proj, int ld, int splits, size_t split_stride, int cd,
                           const float* __restrict__ gnorm, float eps, gemm_in_t* __restrict__ out) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(tokens, obuf, proj, gnorm, out);
   constexpr int PER = DV / 32;
   const int t = tokens[blockIdx.x];
   const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 1)
                         const float* __restrict__ dt_bias, float* __restrict__ qk_out, float* __restrict__ v_out,
                         float* __restrict__ gb_out) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(proj, descs, cu_seqlens, items, conv_w, a_log, dt_bias, qk_out, v_out, gb_out);
   constexpr int QW = DK / 32;
   __shared__ float red[2][2 * QW];
   constexpr int SUB = C / kRunBlock;
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(256)
                          const SeqDesc* __restrict__ descs, const int32_t* __restrict__ cu_seqlens,
                          const int32_t* __restrict__ longs, GdnPool pool, int li, int conv, int cd) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(proj, descs, cu_seqlens, longs);
   const int seq = longs[3 * blockIdx.y];
   const SeqDesc d = descs[seq];
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;

@@ -43,7 +43,7 @@ __global__ void pack_kernel(const SeqDesc* __restrict__ descs, int n_seq,
                             const int32_t* __restrict__ new_pages, int32_t* block_table,
                             int stride, Packed p) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, new_pages);
   __shared__ int red[32];
   const int s = blockIdx.x;
   int local = 0;
@@ -80,7 +80,7 @@ __global__ void pack_kernel(const SeqDesc* __restrict__ descs, int n_seq,
 __global__ void cow_kernel(KvPool kv, const SeqDesc* __restrict__ descs,
                            const int32_t* __restrict__ new_pages) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, new_pages);
   const SeqDesc d = descs[blockIdx.x];
   if (d.cow_src < 0 || d.n_new <= 0) return;
   const int layer = blockIdx.y;
@@ -100,7 +100,7 @@ __global__ void embed_norm_kernel(QMat embed, const uint32_t* __restrict__ token
                                   const float* __restrict__ norm_w, float eps, float* x,
                                   gemm_in_t* hb) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(tokens, norm_w);
   __shared__ float red[32];
   const int t = blockIdx.x, H = embed.k;
   const uint32_t tok = tokens[t];
@@ -135,7 +135,7 @@ __global__ void residual_norm_kernel(float* __restrict__ x, const float* __restr
                                      float eps, gemm_in_t* __restrict__ hb,
                                      const int32_t* __restrict__ out_token, float* __restrict__ hidden) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(x, partial, norm_w, hb, out_token, hidden);
   // Thread i owns column pairs i, i + blockDim, ... (H <= 2 * kPer * blockDim);
   // every load of the row is issued before the first add.
   constexpr int kPer = 4, kSplits = 8;
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(1024) attn_prep_kernel(const float* __restrict
                                                          const int64_t* __restrict__ slots, KvPool kv, int layer,
                                                          float* q, float* gate) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(proj, qn, kn, token_pos, slots);
   constexpr int E = D / 32;
   __shared__ float sm[32][D];
   __shared__ double rot[2][D / 2];
@@ -318,7 +318,7 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
                                        const int32_t* __restrict__ token_pos, const int32_t* __restrict__ tokens,
                                        int Hq, int D, int spl, int max_splits, gemm_in_t* out) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(ws, gate, token_pos, tokens);
   extern __shared__ float wsplit[];
   __shared__ float red[32];
   __shared__ float s_max, s_den;
@@ -363,18 +363,31 @@ __global__ void attention_merge_kernel(const float* __restrict__ ws, const float
 }
 
 // ------------------------------------------------------------------- routing --
-// One warp per token. Top-k over the router logits by (logit desc, expert id
-// asc) on the fp32 total order; weights renormalised over the selection
+// Top-k over the router logits by (logit desc, expert id asc) on the fp32
+// total order; weights renormalised over the selection
 // (native/qwen_model.inc:77-79: softmax then divide by the selected sum);
 // slot `top` is the shared expert (id E) with weight sigmoid(shared gate).
-__global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits, int ld, int splits,
-                                                    size_t split_stride, int E, int top, int32_t* ids,
-                                                    float* weights, float* logits_out) {
+// Both kernels below run the same rounds with the same arithmetic: the split-K
+// partials summed in split order, one maximum of the packed (total-order key,
+// ~id) per round, w_r = exp(l_r - l_0), then w_r / sum. The thread (lane) r
+// keeps round r's id and weight in registers and writes them at the end.
+
+// Decode of the total-order key back to the float.
+__device__ __forceinline__ float from_total_key(uint32_t tk) {
+  return __uint_as_float((tk & 0x80000000u) ? (tk ^ 0x80000000u) : ~tk);
+}
+
+// One CTA of 256 threads per token (thread i holds experts i, i + 256, ...;
+// E <= 1024): used when the router GEMM split K, so each token's split
+// partials (up to 8 x E values) are read by 256 threads at once.
+__global__ void __launch_bounds__(256) route_block_kernel(const float* __restrict__ logits, int ld, int splits,
+                                                          size_t split_stride, int E, int top, int32_t* ids,
+                                                          float* weights, float* logits_out) {
   pdl_trigger();
-  pdl_wait();
-  // One CTA per token; thread i holds experts i, i+256, ... (E <= 1024).
+  pdl_wait(logits);
   constexpr int kPer = 4, kSplits = 8;
   __shared__ uint64_t wbest[2][8];
+  __shared__ float s_shared_logit;
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* lr = logits + size_t(t) * ld;
   // the shared expert's gate logit (column E): lane sp of warp 0 requests
@@ -386,7 +399,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     const int e = threadIdx.x + k * 256;
     float part[kSplits];
 #pragma unroll
-    for (int sp = 0; sp < kSplits; ++sp)  // split-K partials: independent loads, summed in split order
+    for (int sp = 0; sp < kSplits; ++sp)  // independent loads, then the adds in split order
       part[sp] = (e < E && sp < splits) ? lr[sp * split_stride + e] : 0.f;
     float acc = part[0];
 #pragma unroll
@@ -394,8 +407,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
       if (sp < splits) acc += part[sp];
     v[k] = acc;
   }
-  __shared__ float s_shared_logit;
-  if (warp == 0) {  // summed in split order
+  if (warp == 0) {
     float sl = __shfl_sync(0xffffffffu, sh_part, 0);
 #pragma unroll
     for (int sp = 1; sp < kSplits; ++sp) {
@@ -411,11 +423,9 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
       if (threadIdx.x + k * 256 < E) lo[threadIdx.x + k * 256] = v[k];
   }
   uint32_t taken = 0;
-  float top_val = 0.f, denom = 0.f;
-  int32_t* out_ids = ids + size_t(t) * (top + 1);
-  float* out_w = weights + size_t(t) * (top + 1);
+  float top_val = 0.f, denom = 0.f, my_w = 0.f;
+  int my_e = 0;
   for (int r = 0; r < top; ++r) {
-    // key = (logit on the fp32 total order, then lowest expert id): one max per round
     uint64_t best = 0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
@@ -437,17 +447,80 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     for (int w = 1; w < 8; ++w) best = wbest[r & 1][w] > best ? wbest[r & 1][w] : best;
     const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
     if ((e & 255) == threadIdx.x) taken |= 1u << (e >> 8);
-    const uint32_t tk = uint32_t(best >> 32);
-    const float sel_val = __uint_as_float((tk & 0x80000000u) ? (tk ^ 0x80000000u) : ~tk);
+    const float sel_val = from_total_key(uint32_t(best >> 32));
     if (r == 0) top_val = sel_val;
     const float w = expf(sel_val - top_val);
     denom += w;
-    if (threadIdx.x == 0) { out_ids[r] = e; out_w[r] = w; }
+    if (threadIdx.x == r) { my_e = e; my_w = w; }
   }
-  if (threadIdx.x == 0) {
+  int32_t* out_ids = ids + size_t(t) * (top + 1);
+  float* out_w = weights + size_t(t) * (top + 1);
+  if (threadIdx.x < top) {
+    out_ids[threadIdx.x] = my_e;
+    out_w[threadIdx.x] = my_w / denom;
+  } else if (threadIdx.x == top) {
     const float shared_logit = s_shared_logit;
     if (logits_out) logits_out[size_t(t) * (E + 1) + E] = shared_logit;
-    for (int r = 0; r < top; ++r) out_w[r] = out_w[r] / denom;
+    out_ids[top] = E;
+    out_w[top] = 1.f / (1.f + expf(-shared_logit));
+  }
+}
+
+// One warp per token, 8 tokens per CTA, for unsplit router logits: lane l
+// holds experts l, l + 32, ... (PL of them); each round is a lane-local
+// maximum and five shuffles, with no block-wide barrier.
+template <int PL>
+__global__ void __launch_bounds__(256) route_warp_kernel(const float* __restrict__ logits, int ld, int E, int top,
+                                                         int T, int32_t* ids, float* weights, float* logits_out) {
+  pdl_trigger();
+  pdl_wait(logits);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const float* lr = logits + size_t(t) * ld;
+  const float shared_logit = lr[E];
+  float v[PL];
+#pragma unroll
+  for (int m = 0; m < PL; ++m) v[m] = lane + 32 * m < E ? lr[lane + 32 * m] : 0.f;
+  if (logits_out) {  // diagnostic capture of the router logits
+    float* lo = logits_out + size_t(t) * (E + 1);
+#pragma unroll
+    for (int m = 0; m < PL; ++m)
+      if (lane + 32 * m < E) lo[lane + 32 * m] = v[m];
+    if (lane == 0) lo[E] = shared_logit;
+  }
+  uint32_t taken = 0;
+  float top_val = 0.f, denom = 0.f, my_w = 0.f;
+  int my_e = 0;
+  for (int r = 0; r < top; ++r) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int m = 0; m < PL; ++m) {
+      const int e = lane + 32 * m;
+      if (e < E && !(taken >> m & 1u)) {
+        const uint64_t key = (uint64_t(total_key(v[m])) << 32) | uint32_t(0xFFFFFFFFu - e);
+        best = key > best ? key : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    const int e = int(0xFFFFFFFFu - uint32_t(best & 0xFFFFFFFFu));
+    if ((e & 31) == lane) taken |= 1u << (e >> 5);
+    const float sel_val = from_total_key(uint32_t(best >> 32));
+    if (r == 0) top_val = sel_val;
+    const float w = expf(sel_val - top_val);
+    denom += w;
+    if (lane == r) { my_e = e; my_w = w; }
+  }
+  int32_t* out_ids = ids + size_t(t) * (top + 1);
+  float* out_w = weights + size_t(t) * (top + 1);
+  if (lane < top) {
+    out_ids[lane] = my_e;
+    out_w[lane] = my_w / denom;
+  } else if (lane == top) {
     out_ids[top] = E;
     out_w[top] = 1.f / (1.f + expf(-shared_logit));
   }
@@ -463,7 +536,7 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __rest
                                                            int n_experts, int32_t* counts, int32_t* offsets,
                                                            int32_t* perm, int32_t* inv) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(ids);
   extern __shared__ int32_t smi[];
   int32_t* cnt = smi;                 // [n_experts]
   int32_t* cursor = cnt + n_experts;  // [n_experts]
@@ -539,7 +612,7 @@ __global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* _
                                                                 int n_exp, int32_t* counts, int32_t* offsets,
                                                                 int32_t* perm, int32_t* inv, uint32_t* err) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(ids);
   extern __shared__ uint32_t smm[];
   const int nw = (T + 31) >> 5, nb = (nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock, A = T * slots;
   uint32_t* mask = smm;                                                   // [n_exp][nw]
@@ -610,7 +683,7 @@ __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x
                                    int slots, const float* __restrict__ norm_w, float eps,
                                    gemm_in_t* __restrict__ hb) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(x, y, inv, weights, norm_w, hb);
   // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
   // Thread i owns column pairs i, i + blockDim, ...; the residual row and up
   // to kBatch slot rows are requested together before the ordered adds.
@@ -675,7 +748,7 @@ __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x
 __global__ void gather_rows_kernel(const gemm_in_t* __restrict__ src, int ld, const int32_t* __restrict__ perm,
                                    int div, int H, gemm_in_t* dst) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(src, perm);
   const int p = blockIdx.x;
   const int row = perm[p] / div;
   const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(row) * ld);
@@ -702,7 +775,7 @@ __global__ void __launch_bounds__(256) choice_select_kernel(const float* __restr
                                                            const uint32_t* __restrict__ offsets,
                                                            const uint32_t* __restrict__ ids, uint32_t* tokens) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(logits, rows, offsets, ids);
   __shared__ uint64_t red[8];
   const int k = blockIdx.x, r = rows[k];
   const float* lr = logits + size_t(r) * V;
@@ -729,7 +802,7 @@ __global__ void __launch_bounds__(256) choice_select_kernel(const float* __restr
 __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int V, uint32_t* tokens,
                                                      uint32_t* err, uint64_t* part, uint32_t* done) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(logits);
   __shared__ uint64_t red[16];
   __shared__ bool last;
   const int r = blockIdx.x, sp = blockIdx.y;
@@ -793,7 +866,7 @@ __global__ void mtp_input_kernel(QMat embed, const uint32_t* __restrict__ tokens
                                  const float* __restrict__ w_e, const float* __restrict__ w_h, float eps,
                                  gemm_in_t* __restrict__ cat) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(tokens, hidden, w_e, w_h, cat);
   __shared__ float red[32];
   extern __shared__ float erow[];  // [H]
   const int t = blockIdx.x, H = embed.k;
@@ -839,7 +912,7 @@ __global__ void accept_kernel(const SeqDesc* __restrict__ descs, int n, const in
                               const uint32_t* __restrict__ eos, int n_eos, int ctx, int32_t* acc_out,
                               uint32_t* emitted, int emit_stride, uint32_t* n_emitted) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cu_seqlens, tokens, sampled, eos);
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= n) return;
   const SeqDesc d = descs[s];
@@ -880,7 +953,7 @@ __global__ void verify_compact_kernel(const SeqDesc* __restrict__ descs, const i
                                       const float* __restrict__ hidden_stage, const int32_t* __restrict__ cu_seqlens,
                                       float* hidden_pool, int chunk, int H) {
   pdl_trigger();
-  pdl_wait();
+  pdl_wait(descs, cand_slots, acc, hidden_stage, cu_seqlens);
   const int s = blockIdx.x;
   const SeqDesc d = descs[s];
   const int a = acc[s];
@@ -1016,8 +1089,20 @@ void launch_route(const float* logits, int ld, int splits, size_t split_stride, 
                   int32_t* ids, float* weights, float* logits_out, cudaStream_t s) {
   if (E > 1024) throw std::invalid_argument("more than 1024 experts");
   if (splits > 8) throw std::invalid_argument("router split-K above 8");
+  if (top < 1 || top > E || top > 255) throw std::invalid_argument("router top-k outside 1..min(experts, 255)");
   if (T <= 0) return;
-  launch_pdl(route_kernel, T, 256, 0, s, logits, ld, splits, split_stride, E, top, ids, weights, logits_out);
+  if (splits > 1 || top > 31) {
+    launch_pdl(route_block_kernel, T, 256, 0, s, logits, ld, splits, split_stride, E, top, ids, weights, logits_out);
+  } else {
+    const int grid = (T + 7) / 8;
+    auto go = [&](auto kernel) { launch_pdl(kernel, grid, 256, 0, s, logits, ld, E, top, T, ids, weights, logits_out); };
+    if (E <= 32) go(route_warp_kernel<1>);
+    else if (E <= 64) go(route_warp_kernel<2>);
+    else if (E <= 128) go(route_warp_kernel<4>);
+    else if (E <= 256) go(route_warp_kernel<8>);
+    else if (E <= 512) go(route_warp_kernel<16>);
+    else go(route_warp_kernel<32>);
+  }
   count_launch();
 }
 

@@ -53,6 +53,7 @@ constexpr int kWarps = kEpiWarp0 + 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxStages = 12;       // shared-memory ring = TMEM A stages (32 columns each)
 constexpr int kMaxGroups = 1040;     // shared-memory cache of group offsets
+constexpr int kItemCache = 128;      // grouped: this CTA's first items, decoded once at kernel start
 constexpr int kTmemCols = 512;
 // One packed word (8 columns) into four f16x2 A-operand registers
 // (columns 0-1, 2-3, 4-5, 6-7): the bytes of (w & 0x0F0F0F0F) and of
@@ -92,9 +93,33 @@ struct Work {
   bool valid;
 };
 
-// Grouped items run over the non-empty groups only (`act`, `n_act` built in
-// shared memory at kernel start), so CTAs get equal shares of real work.
-__device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* goff, const int32_t* act) {
+// Grouped items run over the non-empty groups only (`act`, built in shared
+// memory at kernel start) and hold one token block each: item = (group, row
+// tile, token block), token block fastest. `bpre[j]` counts the token blocks
+// of the first j non-empty groups, so group j owns items
+// [bpre[j] * expert_tiles, bpre[j + 1] * expert_tiles). A group far larger
+// than the rest (the shared expert of a prefill step) is thereby spread over
+// many CTAs instead of lengthening the few that draw its row tiles.
+__device__ __forceinline__ int4 grouped_item(const TcArgs& a, int i, const int32_t* goff, const int32_t* act,
+                                             const int32_t* bpre) {
+  // the last non-empty group j with bpre[j] * expert_tiles <= i
+  const int key = i / a.expert_tiles;
+  int lo = 0, hi = act[kMaxGroups] - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (bpre[mid] <= key) lo = mid;
+    else hi = mid - 1;
+  }
+  const int nb = bpre[lo + 1] - bpre[lo];
+  const int local = i - bpre[lo] * a.expert_tiles;
+  const int g = act[lo], rt_local = local / nb;
+  const int p0 = goff[g] + (local - rt_local * nb) * a.box_rows;
+  return make_int4(g, rt_local, p0, min(goff[g + 1], p0 + a.box_rows));
+}
+
+// Item i, the k-th of this CTA (i = blockIdx.x + k * gridDim.x).
+__device__ __forceinline__ Work item_at(const TcArgs& a, int i, int k, const int32_t* goff, const int32_t* act,
+                                        const int32_t* bpre, const int4* icache) {
   Work w;
   const int kc = a.W.k_chunks();
   if (a.mode == kGemmStoreF32) {
@@ -110,13 +135,14 @@ __device__ __forceinline__ Work item_at(const TcArgs& a, int i, const int32_t* g
     w.p0 = a.token_group > 0 ? tg * a.token_group : 0;
     w.p1 = a.token_group > 0 ? min(a.n_tokens, w.p0 + a.token_group) : a.n_tokens;
   } else {
-    w.g = act[i / a.expert_tiles];
-    w.rt_local = i % a.expert_tiles;
+    const int4 it = k < kItemCache ? icache[k] : grouped_item(a, i, goff, act, bpre);
+    w.g = it.x;
+    w.rt_local = it.y;
     w.rt = w.g * a.expert_tiles + w.rt_local;
     w.c0 = 0;
     w.c1 = kc;
-    w.p0 = goff[w.g];
-    w.p1 = goff[w.g + 1];
+    w.p0 = it.z;
+    w.p1 = it.w;
   }
   w.valid = w.p1 > w.p0 && w.c1 > w.c0;
   return w;
@@ -154,6 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2) + 1;
   int32_t* goff = reinterpret_cast<int32_t*>(acc_empty + 3);  // [groups + 1]
   int32_t* act = goff + (kMaxGroups + 1);                      // [non-empty groups], then their count
+  int32_t* bpre = act + (kMaxGroups + 1);                      // token blocks before each non-empty group
+  int4* icache = reinterpret_cast<int4*>((reinterpret_cast<uintptr_t>(bpre + kMaxGroups + 1) + 15) & ~uintptr_t(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
@@ -180,30 +208,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (a.mode != kGemmStoreF32 && warp == 2) {
     // stable compaction of the non-empty groups (ballot + popc per 32 groups)
-    int n = 0;
+    // and the prefix of their token block counts (warp scan)
+    int n = 0, blocks = 0;
     for (int g0 = 0; g0 < a.groups; g0 += 32) {
       const int g = g0 + lane;
-      const bool live = g < a.groups && goff[g + 1] > goff[g];
+      const int cnt = g < a.groups ? goff[g + 1] - goff[g] : 0;
+      const bool live = cnt > 0;
       const uint32_t m = __ballot_sync(0xffffffffu, live);
-      if (live) act[n + __popc(m & ((1u << lane) - 1u))] = g;
+      int x = live ? (cnt + a.box_rows - 1) / a.box_rows : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (live) {
+        const int j = n + __popc(m & ((1u << lane) - 1u));
+        act[j] = g;
+        bpre[j + 1] = blocks + x;
+      }
       n += __popc(m);
+      blocks += __shfl_sync(0xffffffffu, x, 31);
     }
-    if (lane == 0) act[kMaxGroups] = n;
+    if (lane == 0) {
+      act[kMaxGroups] = n;
+      bpre[0] = 0;
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int total = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits * dense_token_groups(a)
-                                             : act[kMaxGroups] * a.expert_tiles;
+                                             : bpre[act[kMaxGroups]] * a.expert_tiles;
+  if (a.mode != kGemmStoreF32) {
+    // decode this CTA's first items once (a binary search each), so the
+    // roles' per-item lookups are one shared-memory load
+    for (int k = threadIdx.x; k < kItemCache; k += blockDim.x) {
+      const int i = blockIdx.x + k * gridDim.x;
+      if (i < total) icache[k] = grouped_item(a, i, goff, act, bpre);
+    }
+    __syncthreads();
+  }
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
     int ws = 0;
     uint32_t wph = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff, act);
+    for (int i = blockIdx.x, k_item = 0; i < total && ok && !*abort_flag; i += gridDim.x, ++k_item) {
+      const Work w = item_at(a, i, k_item, goff, act, bpre, icache);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
         for (int c = w.c0; c < w.c1; c += U) {
@@ -222,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int bs = 0;
     uint32_t bph = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff, act);
+    for (int i = blockIdx.x, k_item = 0; i < total && ok && !*abort_flag; i += gridDim.x, ++k_item) {
+      const Work w = item_at(a, i, k_item, goff, act, bpre, icache);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
         for (int c = w.c0; c < w.c1; c += U) {
@@ -243,8 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t ph = 0, bph = 0, acc_it = 0;
     const uint32_t idesc = idesc_f16(box);
     bool ok = true;
-    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff, act);
+    for (int i = blockIdx.x, k_item = 0; i < total && ok && !*abort_flag; i += gridDim.x, ++k_item) {
+      const Work w = item_at(a, i, k_item, goff, act, bpre, icache);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
         const int d = acc_it & 1;
@@ -292,8 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int st = wg * U, ws = wg, rel = wg, mine = 0, skip = wg;
     uint32_t ph = 0, wph = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff, act);
+    for (int i = blockIdx.x, k_item = 0; i < total && ok && !*abort_flag; i += gridDim.x, ++k_item) {
+      const Work w = item_at(a, i, k_item, goff, act, bpre, icache);
       if (!w.valid) continue;
       const int nb = (w.c1 - w.c0) / U;  // units per token block (K ranges are multiples of U)
       for (int tb = w.p0; tb < w.p1 && ok; tb += box) {
@@ -343,8 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = uint32_t(quad * 32) << 16;
     uint32_t acc_it = 0;
     bool ok = true;
-    for (int i = blockIdx.x; i < total && ok && !*abort_flag; i += gridDim.x) {
-      const Work w = item_at(a, i, goff, act);
+    for (int i = blockIdx.x, k_item = 0; i < total && ok && !*abort_flag; i += gridDim.x, ++k_item) {
+      const Work w = item_at(a, i, k_item, goff, act, bpre, icache);
       if (!w.valid) continue;
       for (int tb = w.p0; tb < w.p1 && ok; tb += box, ++acc_it) {
         const int d = acc_it & 1;
@@ -407,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 size_t qgemm_tc_smem(int box_rows, int stages, int unit) {
   const int b_stages = qgemm_tc_bstages(box_rows);
   return 1024 + size_t(b_stages) * size_t(box_rows) * 128 + size_t(kWSlots) * unit * kTileBytes + 64 * 9 * 4 +
-         (2 * size_t(kWSlots) + 2 * size_t(b_stages) + 3 * size_t(stages) + 4) * 8 + 16 + (kMaxGroups + 1) * 4 +
-         (kMaxGroups + 1) * 4;
+         (2 * size_t(kWSlots) + 2 * size_t(b_stages) + 3 * size_t(stages) + 4) * 8 + 16 +
+         3 * (kMaxGroups + 1) * 4 + 16 + kItemCache * 16;  // group offsets, non-empty groups, token block
+                                                            // prefix, item cache
 }
 
 // Activation ring depth (chunks): 96 KB of box-row tiles, at least the TMEM
@@ -450,8 +504,8 @@ void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream
   });
   if (a.mode == kGemmStoreF32 && a.token_group > 0 && (a.token_group % a.box_rows || a.splits != 1))
     throw std::invalid_argument("GEMM token groups must be whole boxes, without split-K");
-  const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits * dense_token_groups(a)
-                                            : a.groups * a.expert_tiles;
+  // grouped: the item count (token blocks x row tiles) is known on the device only
+  const int items = a.mode == kGemmStoreF32 ? a.W.row_tiles * a.splits * dense_token_groups(a) : sm_count;
   const int grid = std::max(1, std::min(items, sm_count));
   if (smem > 227 * 1024) throw std::invalid_argument("tcgen05 GEMM shared memory above 227 KB");
   launch_pdl(qgemm_tc_kernel, grid, kThreads, smem, s, bmap, a);
