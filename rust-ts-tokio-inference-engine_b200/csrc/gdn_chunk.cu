@@ -434,14 +434,19 @@ __global__ void __launch_bounds__(1024, 1)
   }
 }
 
-// Token-parallel preparation of long runs: CTA = (64-token chunk, key head),
-// one thread per channel of the key head (its q and k channels and its R
-// value heads' v channels), gdn_prep's arithmetic per token: causal conv +
-// SiLU and q / k RMS scaling (per-warp partials summed in a fixed order); the
-// decay and beta come from gdn_chunk_prep. A chunk starts from the K-1 inputs before it: earlier tokens of
-// the run (their projection rows) or the parent's conv history. The child's
-// history is written afterwards by gdn_conv_tail (a consumed parent's history
-// is the child's, so it must not change while any chunk still reads it).
+// Token-parallel preparation of long runs: CTA = (16 tokens of a 64-token
+// chunk, key head), one thread per channel of the key head (its q and k
+// channels and its R value heads' v channels), gdn_prep's arithmetic per
+// token: causal conv + SiLU and q / k RMS scaling; the decay and beta come
+// from gdn_chunk_prep. Each thread runs its channel's conv over the block's
+// tokens with the taps in registers and leaves the q / k activations in
+// shared memory; after one barrier, warp w scales token w's q and k rows
+// (the sums of squares formed per 32 channels by the same butterfly, then
+// added in channel-group order, as gdn_prep does). A chunk starts from the
+// K-1 inputs before it: earlier tokens of the run (their projection rows) or
+// the parent's conv history. The child's history is written afterwards by
+// gdn_conv_tail (a consumed parent's history is the child's, so it must not
+// change while any chunk still reads it).
 template <int DK, int DV, int R>
 __global__ void __launch_bounds__(2 * DK + R * DV, 1)
     gdn_run_prep_kernel(const float* __restrict__ proj, int ld, int splits, size_t split_stride,
@@ -453,8 +458,9 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 1)
   pdl_trigger();
   pdl_wait(proj, descs, cu_seqlens, items, conv_w, a_log, dt_bias, qk_out, v_out, gb_out);
   constexpr int QW = DK / 32;
-  __shared__ float red[2][2 * QW];
   constexpr int SUB = C / kRunBlock;
+  constexpr int kThreads = 2 * DK + R * DV;
+  __shared__ float acts[kRunBlock][2 * DK];  // q and k activations of the block's tokens
   const int item = blockIdx.x / SUB, kh = blockIdx.y;
   const int seq = items[2 * item], chunk = items[2 * item + 1];
   const SeqDesc d = descs[seq];
@@ -479,44 +485,51 @@ __global__ void __launch_bounds__(2 * DK + R * DV, 1)
 #pragma unroll
   for (int j = 0; j < 8; ++j)
     if (j == conv - 1) cw_last = cw[j];
-  const int R_ = R;
-  constexpr int G = kRunBlock;  // tokens whose inputs are requested together, ahead of their barriers
-  static_assert(kRunBlock % G == 0, "run block is whole request groups");
-  float cur_g[G];
-  for (int i = 0; i < n; ++i) {
-    const int t = s0 + c0 + i;
-    if ((i % G) == 0) {
+  // the block's inputs: each split's 16 partials requested together, added
+  // in split order (split_sum_c's order)
+  float cur_g[kRunBlock];
+  const float* base = proj + size_t(s0 + c0) * ld + gc;
 #pragma unroll
-      for (int k = 0; k < G; ++k)
-        cur_g[k] = split_sum_c(proj + size_t(s0 + c0 + min(i + k, n - 1)) * ld, gc, splits, split_stride);
+  for (int k = 0; k < kRunBlock; ++k) cur_g[k] = base[size_t(min(k, n - 1)) * ld];
+  for (int sp = 1; sp < splits; ++sp) {
+    float part[kRunBlock];
+#pragma unroll
+    for (int k = 0; k < kRunBlock; ++k) part[k] = base[sp * split_stride + size_t(min(k, n - 1)) * ld];
+#pragma unroll
+    for (int k = 0; k < kRunBlock; ++k) cur_g[k] += part[k];
+  }
+#pragma unroll
+  for (int i = 0; i < kRunBlock; ++i) {
+    if (i < n) {
+      const float cur = cur_g[i];
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < 7; ++j)
+        if (j < conv - 1) acc += taps[j] * cw[j];
+      acc += cur * cw_last;
+#pragma unroll
+      for (int j = 0; j < 7; ++j)
+        if (j < conv - 1) taps[j] = j + 1 < conv - 1 ? taps[j + 1] : cur;
+      const float act = siluf_(acc);
+      if (c >= 2 * DK) v_out[size_t(s0 + c0 + i) * vd + kh * R * DV + (c - 2 * DK)] = act;
+      else acts[i][c] = act;
     }
-    float cur = 0.f;
+  }
+  __syncthreads();
+  for (int i = warp; i < n; i += kThreads / 32) {
+    float* dstq = qk_out + ((size_t(s0 + c0 + i) * hk + kh) * 2) * DK;
 #pragma unroll
-    for (int k = 0; k < G; ++k)
-      if (k == i % G) cur = cur_g[k];
-    float acc = 0.f;
+    for (int h = 0; h < 2; ++h) {  // q, then k
+      float a[QW], tot = 0.f;
 #pragma unroll
-    for (int j = 0; j < 7; ++j)
-      if (j < conv - 1) acc += taps[j] * cw[j];
-    acc += cur * cw_last;
-#pragma unroll
-    for (int j = 0; j < 7; ++j)
-      if (j < conv - 1) taps[j] = j + 1 < conv - 1 ? taps[j + 1] : cur;
-    const float act = siluf_(acc);
-    if (c >= 2 * DK) {
-      v_out[size_t(t) * vd + kh * R_ * DV + (c - 2 * DK)] = act;
-    } else {
-      float ss = warp_sum(act * act);
-      if (lane == 0) red[i & 1][warp] = ss;
-      asm volatile("bar.sync 1, %0;" ::"r"(2 * DK) : "memory");
-      const int g0 = c < DK ? 0 : QW;
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < QW; ++w) tot += red[i & 1][g0 + w];
+      for (int j = 0; j < QW; ++j) {
+        a[j] = acts[i][h * DK + 32 * j + lane];
+        tot += warp_sum(a[j] * a[j]);
+      }
       const float rinv = rsqrtf(tot / DK + 1e-6f);
-      float* dstq = qk_out + ((size_t(t) * hk + kh) * 2) * DK;
-      if (c < DK) dstq[c] = act * (rinv / DK);
-      else dstq[DK + (c - DK)] = act * (rinv * rsqrtf(float(DK)));
+      const float scale = h == 0 ? rinv / DK : rinv * rsqrtf(float(DK));
+#pragma unroll
+      for (int j = 0; j < QW; ++j) dstq[h * DK + 32 * j + lane] = a[j] * scale;
     }
   }
 }
