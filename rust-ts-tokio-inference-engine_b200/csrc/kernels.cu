@@ -677,70 +677,62 @@ __global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* _
 }
 
 // x[t] += sum_j w[t][j] * y[inv[t*slots+j]] (fixed slot order, deterministic);
-// then optional hb[t] = fp16(rms(x[t]) * norm_w).
+// then optional hb[t] = fp16(rms(x[t]) * norm_w). One CTA per token, thread i
+// owns columns 4i..4i+3 (H <= 4096, H % 4 == 0): 512 threads for H = 2048,
+// so two tokens share an SM and one token's dependent loads (its slot rows,
+// then those rows' values) overlap the other's. The slot rows are requested
+// in batches of 8 float4 before their ordered adds.
 __global__ void __launch_bounds__(1024) moe_combine_kernel(float* __restrict__ x, const float* __restrict__ y,
                                    const int32_t* __restrict__ inv, const float* __restrict__ weights, int H,
                                    int slots, const float* __restrict__ norm_w, float eps,
                                    gemm_in_t* __restrict__ hb) {
   pdl_trigger();
   pdl_wait(x, y, inv, weights, norm_w, hb);
-  // x[t] += sum_j w_j * y[inv(t, j)] in slot order, then RMSNorm into hb.
-  // Thread i owns column pairs i, i + blockDim, ...; the residual row and up
-  // to kBatch slot rows are requested together before the ordered adds.
-  constexpr int kPer = 4, kBatch = 16;
+  constexpr int kBatch = 8;
   __shared__ float red[32];
   __shared__ float sw[64];
   __shared__ int32_t srow[64];
-  const int t = blockIdx.x;
-  if (threadIdx.x < slots) {
-    sw[threadIdx.x] = weights[size_t(t) * slots + threadIdx.x];
-    srow[threadIdx.x] = inv[size_t(t) * slots + threadIdx.x];
+  const int t = blockIdx.x, c = threadIdx.x;
+  if (c < slots) {
+    sw[c] = weights[size_t(t) * slots + c];
+    srow[c] = inv[size_t(t) * slots + c];
   }
-  const int H2 = H >> 1;
-  float2* xr = reinterpret_cast<float2*>(x + size_t(t) * H);
-  float2 xo[kPer];
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    xo[k] = c < H2 ? xr[c] : make_float2(0.f, 0.f);
-  }
+  const bool live = c < (H >> 2);
+  float4* xr = reinterpret_cast<float4*>(x + size_t(t) * H);
+  const float4 xo = live ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
   __syncthreads();
-  float2 v[kPer];
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
   float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    v[k] = make_float2(0.f, 0.f);
-    if (c >= H2) continue;
-    for (int j0 = 0; j0 < slots; j0 += kBatch) {  // fixed slot order: deterministic sum
-      float2 yv[kBatch];
+  if (live) {
+    for (int j0 = 0; j0 < slots; j0 += kBatch) {
+      float4 yv[kBatch];
 #pragma unroll
       for (int b = 0; b < kBatch; ++b)
-        if (j0 + b < slots) yv[b] = reinterpret_cast<const float2*>(y + size_t(srow[j0 + b]) * H)[c];
+        if (j0 + b < slots) yv[b] = reinterpret_cast<const float4*>(y + size_t(srow[j0 + b]) * H)[c];
 #pragma unroll
       for (int b = 0; b < kBatch; ++b)
         if (j0 + b < slots) {
-          v[k].x += sw[j0 + b] * yv[b].x;
-          v[k].y += sw[j0 + b] * yv[b].y;
+          const float w = sw[j0 + b];
+          v.x += w * yv[b].x;
+          v.y += w * yv[b].y;
+          v.z += w * yv[b].z;
+          v.w += w * yv[b].w;
         }
     }
-    v[k].x += xo[k].x;
-    v[k].y += xo[k].y;
-    xr[c] = v[k];
-    ss += v[k].x * v[k].x + v[k].y * v[k].y;
+    v.x += xo.x;
+    v.y += xo.y;
+    v.z += xo.z;
+    v.w += xo.w;
+    xr[c] = v;
+    ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
   const float tot = block_sum(ss, red);
-  if (!norm_w) return;
+  if (!norm_w || !live) return;
   const float inv_r = rsqrtf(tot / H + eps);
-#pragma unroll
-  for (int k = 0; k < kPer; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    if (c < H2) {
-      const float2 w = reinterpret_cast<const float2*>(norm_w)[c];
-      reinterpret_cast<__half2*>(hb + size_t(t) * H)[c] =
-          to_gemm_in2(v[k].x * inv_r * w.x, v[k].y * inv_r * w.y);
-    }
-  }
+  const float4 w = reinterpret_cast<const float4*>(norm_w)[c];
+  __half2* o = reinterpret_cast<__half2*>(hb + size_t(t) * H) + 2 * c;
+  o[0] = to_gemm_in2(v.x * inv_r * w.x, v.y * inv_r * w.y);
+  o[1] = to_gemm_in2(v.z * inv_r * w.z, v.w * inv_r * w.w);
 }
 
 // X_perm[p] = X[perm[p] / slots]: expert-sorted copy of the MoE input rows
@@ -1138,9 +1130,9 @@ void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, con
                         const int32_t* out_token, int rows, float* hidden_f32, cudaStream_t s) {
   (void)out_token; (void)rows; (void)hidden_f32;
   if (T <= 0) return;
-  if (slots > 64 || H > 8 * 1024 || H % 2) throw std::invalid_argument("combine geometry");
-  launch_pdl(moe_combine_kernel, T, std::max(64, row_threads(H)), 0, s, x, y_sorted, inv, weights, H, slots, norm_w, eps,
-                                                                hb);
+  if (slots > 64 || H > 4096 || H % 4) throw std::invalid_argument("combine geometry");
+  launch_pdl(moe_combine_kernel, T, std::max(64, (H / 4 + 31) / 32 * 32), 0, s, x, y_sorted, inv, weights, H, slots,
+             norm_w, eps, hb);
   count_launch();
 }
 

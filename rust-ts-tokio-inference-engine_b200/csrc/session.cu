@@ -71,26 +71,51 @@ template <class T>
 struct DevBuf {
   T* p = nullptr;
   size_t n = 0;
+  cudaStream_t pool_stream = nullptr;  // set while p comes from the stream-ordered pool
+  bool pooled = false;
   DevBuf() = default;
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
-  ~DevBuf() {
-    if (p) cudaFree(p);
+  ~DevBuf() {  // the owner has synchronised its stream
+    if (p) {
+      if (pooled) cudaFreeAsync(p, nullptr);
+      else cudaFree(p);
+    }
+  }
+  void release() {
+    if (!p) return;
+    if (pooled) {
+      QWEN_CUDA(cudaFreeAsync(p, pool_stream));
+      QWEN_CUDA(cudaStreamSynchronize(pool_stream));
+    } else {
+      QWEN_CUDA(cudaFree(p));
+    }
+    p = nullptr;
+    n = 0;
+    pooled = false;
   }
   void ensure(size_t count) {
     if (count <= n) return;
-    if (p) {
-      QWEN_CUDA(cudaFree(p));
-      p = nullptr;
-      n = 0;
-    }
+    release();
     QWEN_CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
     n = count;
   }
-  // per-step buffers whose size varies from step to step: grow with headroom,
-  // so the (device-synchronising) reallocation stays rare
-  void ensure_grow(size_t count) {
-    if (count > n) ensure(count + count / 2);
+  // Per-step buffers whose size varies from step to step: grow with headroom
+  // by stream-ordered free and allocation on the stream that uses them, so a
+  // step that needs more does not synchronise the device.
+  void ensure_grow(size_t count, cudaStream_t s) {
+    if (count <= n) return;
+    const size_t want = count + count / 2;
+    if (p) {
+      if (pooled) QWEN_CUDA(cudaFreeAsync(p, s));
+      else QWEN_CUDA(cudaFree(p));
+    }
+    p = nullptr;
+    n = 0;
+    QWEN_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&p), want * sizeof(T), s));
+    n = want;
+    pooled = true;
+    pool_stream = s;
   }
 };
 
@@ -100,6 +125,7 @@ struct PinBuf {
   size_t n = 0;
   ~PinBuf() {
     if (p) cudaFreeHost(p);
+    for (T* r : retired) cudaFreeHost(r);
   }
   void ensure(size_t count) {
     if (count <= n) return;
@@ -108,9 +134,17 @@ struct PinBuf {
     QWEN_CUDA(cudaMallocHost(&p, std::max<size_t>(count, 1) * sizeof(T)));
     n = count;
   }
+  // Growth keeps the old buffer (an async copy of the previous step may
+  // still read it) until the owner goes away, instead of freeing it, which
+  // would synchronise the device.
   void ensure_grow(size_t count) {
-    if (count > n) ensure(count + count / 2);
+    if (count <= n) return;
+    if (p) retired.push_back(p);
+    p = nullptr;
+    n = 0;
+    ensure(count + count / 2);
   }
+  std::vector<T*> retired;
 };
 
 struct Version {
@@ -327,6 +361,8 @@ struct Session {
   bool in_mtp = false;  // the MTP head's MoE computes every expert locally
 
   ~Session() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);  // pooled step buffers are freed after this
     if (ep.comm) ncclCommDestroy(ep.comm);
     for (void* w : ep.peer_windows)
       if (w) cudaIpcCloseMemHandle(w);
@@ -804,31 +840,31 @@ struct Session {
       }
       QWEN_CUDA(cudaMemsetAsync(err.p, 0, 4, stream));
       if (!items.empty()) {
-        attn_items.ensure_grow(items.size());
+        attn_items.ensure_grow(items.size(), stream);
         QWEN_CUDA(cudaMemcpyAsync(attn_items.p, hi, items.size() * 8, cudaMemcpyHostToDevice, stream));
       }
       if (!pf_blocks.empty()) {
-        pf_dev.ensure_grow(pf_blocks.size());
+        pf_dev.ensure_grow(pf_blocks.size(), stream);
         QWEN_CUDA(cudaMemcpyAsync(pf_dev.p, hpf, pf_blocks.size() * 16, cudaMemcpyHostToDevice, stream));
       }
       if (!merge_tokens.empty()) {
-        merge_dev.ensure_grow(merge_tokens.size());
+        merge_dev.ensure_grow(merge_tokens.size(), stream);
         QWEN_CUDA(cudaMemcpyAsync(merge_dev.p, hmt, merge_tokens.size() * 4, cudaMemcpyHostToDevice, stream));
       }
       if (!gl_longs.empty()) {
         const size_t nl = gl_longs.size(), ni = gl_items.size(), nt = gl_tokens.size();
         gplan_stage.ensure_grow(nl + ni + nt);
-        gplan_dev.ensure_grow(nl + ni + nt);
+        gplan_dev.ensure_grow(nl + ni + nt, stream);
         std::memcpy(gplan_stage.p, gl_longs.data(), nl * 4);
         std::memcpy(gplan_stage.p + nl, gl_items.data(), ni * 4);
         std::memcpy(gplan_stage.p + nl + ni, gl_tokens.data(), nt * 4);
         QWEN_CUDA(cudaMemcpyAsync(gplan_dev.p, gplan_stage.p, (nl + ni + nt) * 4, cudaMemcpyHostToDevice, stream));
         uploads += (nl + ni + nt) * 4;
         const size_t units = ni / 2 * size_t(d.hv) * kGdnChunk;  // (chunk, head) pairs x chunk tokens
-        gplan_u.ensure_grow(units * d.dv);
-        gplan_w.ensure_grow(units * d.dk);
-        gplan_a.ensure_grow(units * kGdnChunk);
-        gplan_lg.ensure_grow(units);
+        gplan_u.ensure_grow(units * d.dv, stream);
+        gplan_w.ensure_grow(units * d.dk, stream);
+        gplan_a.ensure_grow(units * kGdnChunk, stream);
+        gplan_lg.ensure_grow(units, stream);
         gplan.n_long = int(nl / 3);
         gplan.n_items = int(ni / 2);
         gplan.n_tokens = int(nt);
@@ -843,7 +879,7 @@ struct Session {
       if (!ch_host.empty()) {
         QWEN_CUDA(cudaStreamSynchronize(stream));  // the pinned stage may still feed the previous step's copy
         choice_stage.ensure_grow(ch_host.size());
-        choice_dev.ensure_grow(ch_host.size());
+        choice_dev.ensure_grow(ch_host.size(), stream);
         std::memcpy(choice_stage.p, ch_host.data(), ch_host.size() * 4);
         QWEN_CUDA(cudaMemcpyAsync(choice_dev.p, choice_stage.p, ch_host.size() * 4, cudaMemcpyHostToDevice, stream));
         uploads += ch_host.size() * 4;
@@ -969,7 +1005,7 @@ struct Session {
     if (d.n_attn > 0) launch_cow(kv, descs.p, n, new_pages.p, s);
     launch_embed_norm(m.embed, tokens.p, T, m.layers[0].in_norm, d.eps, x.p, hb.p, s);
     const int slots_per_tok = d.top + 1, A = T * slots_per_tok;
-    if (d.n_attn > 0) attn_ws.ensure_grow(size_t(pf_n_blocks ? n_merge : T) * d.Hq * attn_splits * (d.D + 2));
+    if (d.n_attn > 0) attn_ws.ensure_grow(size_t(pf_n_blocks ? n_merge : T) * d.Hq * attn_splits * (d.D + 2), s);
     if (capture_routing) {
       capture.ensure(size_t(d.L) * A);
       cap_logits.ensure(size_t(d.L) * T * (d.E + 1));
@@ -1283,7 +1319,7 @@ struct Session {
         for (int k = 0; k * 16 < (pos + j + kPageTokens) / kPageTokens; ++k) items.push_back(make_int2(j, k));
       const int splits = std::max(1, (pos + cnt + 16 * kPageTokens - 1) / (16 * kPageTokens));
       attn_ws.ensure(size_t(cnt) * d.Hq * splits * (d.D + 2));
-      attn_items.ensure_grow(items.size());
+      attn_items.ensure_grow(items.size(), stream);
       cudaStream_t s = stream;
       QWEN_CUDA(cudaMemcpyAsync(descs.p, &sd, sizeof(sd), cudaMemcpyHostToDevice, s));
       if (n_new) QWEN_CUDA(cudaMemcpyAsync(new_pages.p, fresh.data(), size_t(n_new) * 4, cudaMemcpyHostToDevice, s));
