@@ -125,7 +125,7 @@ int project_noalloc(const QMat& W, int max_splits, const gemm_in_t* x, int T, fl
   const int tb = std::min(T, 128);
   a.box_rows = tb <= 16 ? 16 : tb <= 32 ? 32 : tb <= 64 ? 64 : 128;
   const int kc = W.k_chunks();
-  const int want = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc}));
+  const int want = qgemm_tc_split_target(W.row_tiles, kc, sm_count, max_splits);
   int splits = 1;
   for (int sp = want; sp >= 1; --sp)
     if (kc % sp == 0 && (kc / sp) % 4 == 0 && size_t(sp) * n <= kPartialFloats) {

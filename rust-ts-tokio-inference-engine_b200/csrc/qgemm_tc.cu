@@ -34,6 +34,7 @@
 // raises kErrTimeout and drains out.
 #include <cuda.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "kernels.h"
@@ -484,6 +485,18 @@ int qgemm_tc_unit(const TcArgs& a) {
   for (int u : {4, 2})
     if (per % u == 0 && even_split && stages % u == 0 && (stages / u) % kDequantGroups == 0) return u;
   return 1;
+}
+
+// One wave at most: row tiles x splits <= SM count (rounded down, so a matrix
+// with more row tiles than half the SMs runs unsplit). Every extra split adds
+// a T x rows fp32 partial that the epilogue writes and the consumer re-reads,
+// and a CTA with several short items pays an epilogue per item. On B200 at 64
+// decode tokens (configs[1] shapes) the DeltaNet in_proj (97 row tiles) ran the
+// 48-layer step in 14.66 ms unsplit, 14.80 with 2 splits and 14.91 with 4
+// (two waves); out_proj and the router (16 and 5 row tiles) keep 8 splits,
+// and capping them at 2 cost 0.13 ms per step.
+int qgemm_tc_split_target(int row_tiles, int kc, int sm_count, int max_splits) {
+  return std::max(1, std::min({std::max(1, sm_count / std::max(1, row_tiles)), max_splits, kc}));
 }
 
 void launch_qgemm_tc(const CUtensorMap& bmap, TcArgs a, int sm_count, cudaStream_t s) {

@@ -37,6 +37,10 @@ CUtensorMap make_act_map(const void* base, int rows, int k, int box_rows);
 CUtensorMap make_act_map3d(const void* base, int rows, int k, int box_rows, int unit);
 // Chunks per MMA unit the launcher will use for these arguments (4, 2 or 1).
 int qgemm_tc_unit(const TcArgs& a);
+// Largest split-K count worth trying for a dense launch of at most 128 tokens
+// over `row_tiles` row tiles and `kc` 64-column chunks (callers then take the
+// largest count <= this that divides kc into whole 4-chunk units).
+int qgemm_tc_split_target(int row_tiles, int kc, int sm_count, int max_splits);
 // Tensor map over one attention layer's KV page pool: rows
 // ((page*2 + k_or_v)*Hkv + head)*16 + token, D columns, 16x64 128B-swizzled box.
 CUtensorMap make_kv_map(const KvPool& kv, int layer);

@@ -270,8 +270,8 @@ struct Session {
       // weights of a row tile are re-read from L2 by each block)
       a.token_group = 128;
     } else {
-      // split-K: enough items for ~2 waves, slices of whole 4-chunk units when possible
-      const int want = std::max(1, std::min({(2 * sm_count + W.row_tiles - 1) / W.row_tiles, max_splits, kc}));
+      // split-K: at most one wave of items, slices of whole 4-chunk units when possible
+      const int want = qgemm_tc_split_target(W.row_tiles, kc, sm_count, max_splits);
       for (int sp = want; sp >= 1; --sp)
         if (kc % sp == 0 && (kc / sp) % 4 == 0) { splits = sp; break; }
     }
