@@ -608,22 +608,34 @@ __global__ void __launch_bounds__(1024) expert_sort_kernel(const int32_t* __rest
 // are prefix-summed, so a rank costs at most 8 popcounts. Same bytes as
 // expert_sort_kernel (a stable sort has one result).
 constexpr int kMaskWordsPerBlock = 8;
-__global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* __restrict__ ids, int T, int slots,
-                                                                int n_exp, int32_t* counts, int32_t* offsets,
-                                                                int32_t* perm, int32_t* inv, uint32_t* err) {
-  pdl_trigger();
-  pdl_wait(ids);
-  extern __shared__ uint32_t smm[];
-  const int nw = (T + 31) >> 5, nb = (nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock, A = T * slots;
-  uint32_t* mask = smm;                                                   // [n_exp][nw]
-  int32_t* pre = reinterpret_cast<int32_t*>(mask + size_t(n_exp) * nw);   // [n_exp][nb] ranks before block b
-  int32_t* off = pre + size_t(n_exp) * nb;                                // [n_exp]
-  __shared__ int32_t warp_tot[32];
-  for (int i = threadIdx.x; i < n_exp * nw; i += blockDim.x) mask[i] = 0;
+
+// Shared-memory state of the mask sort: per expert its token mask, the rank
+// before each block of 8 mask words, and (after mask_sort_build) its offset.
+struct MaskSort {
+  uint32_t* mask;  // [n_exp][nw]
+  int32_t* pre;    // [n_exp][nb]
+  int32_t* off;    // [n_exp]
+  int nw, nb;
+};
+
+// Builds the masks, block prefixes and expert offsets in shared memory (every
+// CTA that runs it gets the same result); with `outputs`, writes counts and
+// offsets. Ids outside [0, n_exp) raise kErrBounds and are left out.
+__device__ __forceinline__ MaskSort mask_sort_build(const int32_t* ids, int T, int slots, int n_exp, uint32_t* smm,
+                                                    int32_t* warp_tot, bool outputs, int32_t* counts,
+                                                    int32_t* offsets, uint32_t* err) {
+  MaskSort m;
+  m.nw = (T + 31) >> 5;
+  m.nb = (m.nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock;
+  const int nw = m.nw, nb = m.nb, A = T * slots;
+  m.mask = smm;
+  m.pre = reinterpret_cast<int32_t*>(m.mask + size_t(n_exp) * nw);
+  m.off = m.pre + size_t(n_exp) * nb;
+  for (int i = threadIdx.x; i < n_exp * nw; i += blockDim.x) m.mask[i] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < A; i += blockDim.x) {
     const int e = ids[i], t = i / slots;
-    if (e >= 0 && e < n_exp) atomicOr(&mask[e * nw + (t >> 5)], 1u << (t & 31));
+    if (e >= 0 && e < n_exp) atomicOr(&m.mask[e * nw + (t >> 5)], 1u << (t & 31));
     else atomicOr(err, kErrBounds);
   }
   __syncthreads();
@@ -632,17 +644,17 @@ __global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* _
   for (int e = threadIdx.x; e < n_exp; e += blockDim.x) {
     int run = 0;
     for (int b = 0; b < nb; ++b) {
-      pre[e * nb + b] = run;
+      m.pre[e * nb + b] = run;
       const int w1 = min(nw, (b + 1) * kMaskWordsPerBlock);
-      for (int w = b * kMaskWordsPerBlock; w < w1; ++w) run += __popc(mask[e * nw + w]);
+      for (int w = b * kMaskWordsPerBlock; w < w1; ++w) run += __popc(m.mask[e * nw + w]);
     }
-    off[e] = run;  // the count, until the scan below
+    m.off[e] = run;  // the count, until the scan below
   }
   __syncthreads();
   // exclusive scan of off[] (n_exp <= 1025): thread i owns experts [i * per, (i + 1) * per)
   const int per = (n_exp + blockDim.x - 1) / blockDim.x;
   const int e0 = threadIdx.x * per, e1 = min(n_exp, e0 + per);
-  for (int e = e0; e < e1; ++e) cnt += off[e];
+  for (int e = e0; e < e1; ++e) cnt += m.off[e];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = cnt;
 #pragma unroll
@@ -655,24 +667,96 @@ __global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* _
   int base = incl - cnt;
   for (int w = 0; w < warp; ++w) base += warp_tot[w];
   for (int e = e0; e < e1; ++e) {
-    const int c = off[e];
-    off[e] = base;
-    offsets[e] = base;
-    counts[e] = c;
+    const int c = m.off[e];
+    m.off[e] = base;
+    if (outputs) {
+      offsets[e] = base;
+      counts[e] = c;
+    }
     base += c;
   }
-  if (threadIdx.x == blockDim.x - 1) offsets[n_exp] = base;
+  if (outputs && threadIdx.x == blockDim.x - 1) offsets[n_exp] = base;
   __syncthreads();
-  for (int i = threadIdx.x; i < A; i += blockDim.x) {
+  return m;
+}
+
+// Sorted position of assignment (token t, expert e): the expert's offset plus
+// the number of earlier tokens that picked it.
+__device__ __forceinline__ int mask_sort_pos(const MaskSort& m, int e, int t) {
+  const uint32_t* w = m.mask + size_t(e) * m.nw;
+  const int wt = t >> 5, b = wt / kMaskWordsPerBlock;
+  int rank = m.pre[e * m.nb + b] + __popc(w[wt] & ((1u << (t & 31)) - 1u));
+  for (int k = b * kMaskWordsPerBlock; k < wt; ++k) rank += __popc(w[k]);
+  return m.off[e] + rank;
+}
+
+__global__ void __launch_bounds__(1024) expert_sort_mask_kernel(const int32_t* __restrict__ ids, int T, int slots,
+                                                                int n_exp, int32_t* counts, int32_t* offsets,
+                                                                int32_t* perm, int32_t* inv, uint32_t* err) {
+  pdl_trigger();
+  pdl_wait(ids);
+  extern __shared__ uint32_t smm[];
+  __shared__ int32_t warp_tot[32];
+  const MaskSort m = mask_sort_build(ids, T, slots, n_exp, smm, warp_tot, true, counts, offsets, err);
+  for (int i = threadIdx.x; i < T * slots; i += blockDim.x) {
     const int e = ids[i], t = i / slots;
     if (e < 0 || e >= n_exp) continue;
-    const uint32_t* m = mask + size_t(e) * nw;
-    const int wt = t >> 5, b = wt / kMaskWordsPerBlock;
-    int rank = pre[e * nb + b] + __popc(m[wt] & ((1u << (t & 31)) - 1u));
-    for (int w = b * kMaskWordsPerBlock; w < wt; ++w) rank += __popc(m[w]);
-    const int pos = off[e] + rank;
+    const int pos = mask_sort_pos(m, e, t);
     perm[pos] = i;
     inv[i] = pos;
+  }
+}
+
+// The mask sort fused with the gather of the MoE input rows: every CTA builds
+// the (small) sort in its own shared memory; CTA 0 writes counts / offsets /
+// perm / inv, and each CTA copies the rows of its slice of the assignments,
+// dst[pos(i)] = src[i / slots] (16-byte copies, one warp per row). The same
+// bytes as expert_sort_mask_kernel followed by gather_rows_kernel, one launch
+// and one kernel-boundary wait fewer per MoE layer.
+constexpr int kGatherVec = 8;  // 16-byte vectors in flight per lane
+__global__ void __launch_bounds__(1024) expert_sort_gather_kernel(const int32_t* __restrict__ ids, int T, int slots,
+                                                                  int n_exp, int32_t* counts, int32_t* offsets,
+                                                                  int32_t* perm, int32_t* inv, uint32_t* err,
+                                                                  const gemm_in_t* __restrict__ src, int ld, int H,
+                                                                  gemm_in_t* __restrict__ dst) {
+  pdl_trigger();
+  pdl_wait(ids, src, dst);
+  extern __shared__ uint32_t smm[];
+  __shared__ int32_t warp_tot[32];
+  const bool first = blockIdx.x == 0;
+  const MaskSort m = mask_sort_build(ids, T, slots, n_exp, smm, warp_tot, first, counts, offsets, err);
+  const int A = T * slots;
+  if (first)
+    for (int i = threadIdx.x; i < A; i += blockDim.x) {
+      const int e = ids[i], t = i / slots;
+      if (e < 0 || e >= n_exp) continue;
+      const int pos = mask_sort_pos(m, e, t);
+      perm[pos] = i;
+      inv[i] = pos;
+    }
+  const int i0 = int(int64_t(A) * blockIdx.x / gridDim.x), i1 = int(int64_t(A) * (blockIdx.x + 1) / gridDim.x);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int i = i0 + warp; i < i1; i += nwarps) {
+    const int e = ids[i], t = i / slots;
+    if (e < 0 || e >= n_exp) continue;
+    const int pos = mask_sort_pos(m, e, t);
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(t) * ld);
+    uint4* d4 = reinterpret_cast<uint4*>(dst + size_t(pos) * H);
+    // all of a lane's loads of a 4 KB stretch are issued before its stores,
+    // so a row costs one L2 round trip per 4 KB instead of one per 512 B
+    for (int c0 = 0; c0 < H / 8; c0 += 32 * kGatherVec) {
+      uint4 v[kGatherVec];
+#pragma unroll
+      for (int j = 0; j < kGatherVec; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < H / 8) v[j] = s4[c];
+      }
+#pragma unroll
+      for (int j = 0; j < kGatherVec; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < H / 8) d4[c] = v[j];
+      }
+    }
   }
 }
 
@@ -1123,6 +1207,30 @@ void launch_expert_sort(const int32_t* ids, int n_assign, int slots, int n_exper
   });
   launch_pdl(expert_sort_kernel, 1, 1024, smem, s, ids, n_assign, n_experts, counts, offsets, perm, inv);
   count_launch();
+}
+
+void launch_expert_sort_gather(const int32_t* ids, int n_assign, int slots, int n_experts, int32_t* counts,
+                               int32_t* offsets, int32_t* perm, int32_t* inv, uint32_t* err, const gemm_in_t* src,
+                               int ld, int H, gemm_in_t* dst, int sm_count, cudaStream_t s) {
+  if (n_assign <= 0) return;
+  if (H % 8 || ld % 8) throw std::invalid_argument("sort + gather: rows must be whole 16-byte vectors");
+  const int T = n_assign / slots, nw = (T + 31) / 32, nb = (nw + kMaskWordsPerBlock - 1) / kMaskWordsPerBlock;
+  const size_t mask_smem = (size_t(n_experts) * (nw + nb) + n_experts) * 4;
+  if (n_assign % slots == 0 && n_experts <= 1025 && mask_smem <= 200 * 1024) {
+    static std::atomic<uint64_t> configured{0};
+    once_per_device(configured, [] {
+      QWEN_CUDA(cudaFuncSetAttribute(expert_sort_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     200 * 1024));
+    });
+    // about 8 rows per CTA (a warp per row, 32 warps), at most one CTA per SM
+    const int grid = std::max(1, std::min(sm_count, (n_assign + 7) / 8));
+    launch_pdl(expert_sort_gather_kernel, grid, 1024, mask_smem, s, ids, T, slots, n_experts, counts, offsets, perm,
+               inv, err, src, ld, H, dst);
+    count_launch();
+    return;
+  }
+  launch_expert_sort(ids, n_assign, slots, n_experts, counts, offsets, perm, inv, err, s);
+  launch_gather_rows(src, ld, perm, slots, n_assign, H, dst, s);
 }
 
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv, const float* weights,

@@ -128,6 +128,11 @@ void launch_route(const float* logits, int ld, int splits, size_t split_stride, 
 // memory, else per-round counting.
 void launch_expert_sort(const int32_t* ids, int n_assign, int slots, int n_experts, int32_t* counts,
                         int32_t* offsets, int32_t* perm, int32_t* inv, uint32_t* err, cudaStream_t s);
+// The same sort fused with the gather of the MoE input rows:
+// dst[sorted position] = src[token] (H fp16 columns, row stride ld).
+void launch_expert_sort_gather(const int32_t* ids, int n_assign, int slots, int n_experts, int32_t* counts,
+                               int32_t* offsets, int32_t* perm, int32_t* inv, uint32_t* err, const gemm_in_t* src,
+                               int ld, int H, gemm_in_t* dst, int sm_count, cudaStream_t s);
 void launch_moe_combine(float* x, const float* y_sorted, const int32_t* inv,
                         const float* weights, int T, int H, int slots, const float* norm_w,
                         float eps, gemm_in_t* hb, const int32_t* out_token, int rows,

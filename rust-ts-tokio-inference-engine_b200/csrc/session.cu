@@ -1580,9 +1580,14 @@ struct Session {
     const int rs = dense(ly.router, hb.p, max_tokens, T, partial.p, rw, rstride, kMaxSplits, s);
     launch_route(partial.p, rw, rs, rstride, T, d.E, d.top, ids.p, weights.p,
                  capture_routing ? cap_logits.p + size_t(cur_layer) * T * (d.E + 1) : nullptr, s);
-    launch_expert_sort(ids.p, A, d.top + 1, d.E + 1, counts.p, offsets.p, perm.p, inv.p, err.p, s);
+    const bool ep_layer = ep.on && !in_mtp && !simple_gemm;
+    if (ep_layer || simple_gemm)  // these read the input rows through the permutation themselves
+      launch_expert_sort(ids.p, A, d.top + 1, d.E + 1, counts.p, offsets.p, perm.p, inv.p, err.p, s);
+    else  // the grouped tcgen05 GEMM reads its input rows in expert order
+      launch_expert_sort_gather(ids.p, A, d.top + 1, d.E + 1, counts.p, offsets.p, perm.p, inv.p, err.p, hb.p, d.H,
+                                d.H, xperm.p, sm_count, s);
     stage(11);  // MoeUpGate
-    if (ep.on && !in_mtp && !simple_gemm) {
+    if (ep_layer) {
       moe_ep(ly, T, A, s);
       return;
     }
@@ -1614,7 +1619,6 @@ struct Session {
       launch_qgemm(dn, s);
       return;
     }
-    launch_gather_rows(hb.p, d.H, perm.p, d.top + 1, A, d.H, xperm.p, s);
     // Token block of the grouped GEMMs: the mean rows per expert plus two
     // standard deviations of a binomial count, so nearly every expert fits one
     // block (a larger block re-reads more activation rows per weight tile and
