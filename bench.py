@@ -257,7 +257,13 @@ def barrier(world):
 
 
 # Launches per 48-layer step of each stage's dominant kernel.
-LAUNCHES_PER_STEP = {"MoeUpGate": 48, "MoeDown": 48, "RecurrentUpdate": 36, "AttentionReduction": 12}
+def launches_per_step(stage, cfg):
+    """Launches of a stage's main kernel per step: one per layer of its kind."""
+    n_attn = cfg.layers // cfg.interval
+    return {"MoeUpGate": cfg.layers, "MoeDown": cfg.layers, "RecurrentUpdate": cfg.layers - n_attn,
+            "AttentionReduction": n_attn}.get(stage, 1)
+
+
 # ncu DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum), read from the committed
 # profile summary of that stage's kernel on the same per-layer shapes.
 PROFILE_FILES = {"MoeUpGate": "qgemm_tc_moe_gateup_cfg1.md", "MoeDown": "qgemm_tc_moe_down_cfg1.md"}
@@ -670,7 +676,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": profiled_traffic(dom) if args.workload == "cfg1" else None,
                      "peak_source": peak_kind, "bytes_per_step": bytes_per[dom], "ms_per_step": dom_ms,
-                     "algorithmic_bytes_per_launch": bytes_per[dom] / LAUNCHES_PER_STEP.get(dom, 1)},
+                     "algorithmic_bytes_per_launch": bytes_per[dom] / launches_per_step(dom, cfg)},
         "stage_ms": {k: round(v, 4) for k, v in zip(STAGES, stage_ms) if v > 0},
         "stage_gbs": {k: round(bytes_per[k] / (stage_ms[STAGES.index(k)] / 1e3) / 1e9, 1)
                       for k in bytes_per if stage_ms[STAGES.index(k)] > 0},
