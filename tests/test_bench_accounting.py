@@ -85,3 +85,19 @@ def test_expert_parallel_blocks_partition_the_weights(pkg):
         parts += (ue - 1) * cfg.layers
     # every distinct routed expert is counted by exactly one rank
     assert np.isclose(parts, whole)
+
+
+def test_per_launch_bytes_follow_the_layer_count(pkg):
+    """The roofline's bytes per launch divide a stage's step bytes by the
+    launches of its kernel in that step: one per layer of the stage's kind, so
+    a 4-layer slice reports the same per-launch bytes as the 48-layer model."""
+    import bench
+    ctx = bench.contexts(64, 0)
+    per = {}
+    for layers in (48, 4):
+        cfg = pkg.config1(layers=layers)
+        out, _ = bench.stage_bytes(cfg, ctx, None)
+        per[layers] = {k: out[k] / bench.launches_per_step(k, cfg)
+                       for k in ("MoeUpGate", "MoeDown", "RecurrentUpdate", "AttentionReduction")}
+    for k in per[48]:
+        assert np.isclose(per[48][k], per[4][k]), k
